@@ -1,0 +1,407 @@
+"""Benchmark of the POV-shuffle hot path on B200.
+
+Metric: effective shuffle GB/s = 2 x deck bytes x iterations / time (each iteration reads and
+writes every byte once), with the fraction of the measured HBM copy bandwidth.
+
+One step = one ``povs.shuffle`` call of ITERATIONS iterations over the whole deck, which stays
+resident in HBM (``value``).  ``e2e`` runs the same call through the C ABI with the deck in
+pinned host memory (``povs_shuffle_host_v1``): host->device copy, the iterations, device->host
+copy and a stream sync, every step.
+
+Workloads (synthetic data with the shapes and value distributions of the named configs):
+  bf16_32GiB   134,217,728 x 128 bf16 (32 GiB), uniform [-1, 1) from seed 1, 4 iterations, V=4, P=32  [default]
+  fp16_256MiB  1,048,576 x 128 fp16 (256 MiB), standard normal from seed 0, 4 iterations, V=2, P=64
+  u8_12KiB     1,000,000 x 3x64x64 uint8 (12.3 GB), uniform 0..255 from seed 2, 3 iterations, V=2, P=16
+With --gpus N > 1 every rank shuffles its own deck of the workload (independent replicas on each GPU).
+
+``--impl reference`` times the CPU implementation of the same path (the oracle's C restatement,
+all host threads) on a bounded sample of the workload and prints the same JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+for _p in (REPO, REPO / "pov-shuffle_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+METRIC = "effective shuffle GB/s (2×bytes×iters/time), % HBM peak, 1/2/4/8×B200"
+FALLBACK_HBM_GBS = 6650.0
+
+WORKLOADS = {
+    "bf16_32GiB": dict(
+        rows=134_217_728, shape=(128,), dtype="bfloat16", iterations=4, V=4, P=32, seed=1, init="uniform",
+        desc="bf16 deck 134,217,728 x 128 (32 GiB), uniform [-1,1) from seed 1, iterations=4, V=4, P=32",
+    ),
+    "fp16_256MiB": dict(
+        rows=1_048_576, shape=(128,), dtype="float16", iterations=4, V=2, P=64, seed=0, init="normal",
+        desc="fp16 deck 1,048,576 x 128 (256 MiB), standard normal from seed 0, iterations=4, V=2, P=64",
+    ),
+    "u8_12KiB": dict(
+        rows=1_000_000, shape=(3, 64, 64), dtype="uint8", iterations=3, V=2, P=16, seed=2, init="bytes",
+        desc="uint8 deck 1,000,000 x 3x64x64 (12,288 B rows, 12.3 GB), uniform 0..255 from seed 2, iterations=3, V=2, P=16",
+    ),
+}
+
+
+def measured_peaks() -> tuple[float, str]:
+    path = REPO / "MEASURED_PEAKS.json"
+    try:
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def row_bytes_of(w: dict) -> int:
+    import numpy as np
+
+    elem = {"bfloat16": 2, "float16": 2, "uint8": 1, "float32": 4}[w["dtype"]]
+    return int(np.prod(w["shape"])) * elem
+
+
+def traffic_per_launch(kernel: str, workload: str) -> int | None:
+    """DRAM bytes per launch of ``kernel`` from the committed ncu summary, if one exists."""
+    path = REPO / "profiles" / f"{kernel}__{workload}.md"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            return int(line.split(":", 1)[1].strip().replace(",", ""))
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = (
+        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+        "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu_index)],
+                stdout=self.file, stderr=subprocess.DEVNULL,
+            )
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.file.flush()
+        self.file.seek(0)
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.file.read().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                maxes.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        os.unlink(self.file.name)
+        return {
+            "sm_mhz": statistics.median(sms) if sms else None,
+            "sm_max_mhz": max(maxes) if maxes else None,
+            "reasons": sorted(reasons),
+            "samples": len(sms),
+        }
+
+
+def make_deck(w: dict, device):
+    import torch
+
+    dtype = getattr(torch, w["dtype"])
+    shape = (w["rows"], *w["shape"])
+    g = torch.Generator(device=device).manual_seed(w["seed"])
+    if w["init"] == "uniform":
+        return torch.rand(shape, generator=g, device=device, dtype=dtype) * 2 - 1
+    if w["init"] == "normal":
+        return torch.randn(shape, generator=g, device=device, dtype=dtype)
+    return torch.randint(0, 256, shape, generator=g, device=device, dtype=torch.uint8)
+
+
+def run_ours(args, w: dict, wname: str) -> None:
+    import torch
+    import torch.distributed as dist
+
+    import povs
+    from povs import _native
+    from povs.common import choose_offsets
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+
+    R = row_bytes_of(w)
+    N, P, V, iters = w["rows"], w["P"], w["V"], w["iterations"]
+    offsets = choose_offsets(N, int(R // {"bfloat16": 2, "float16": 2, "uint8": 1}[w["dtype"]]),
+                             {"bfloat16": 2, "float16": 2, "uint8": 1}[w["dtype"]], P)
+    opts = povs.Options(virtual_block_size=V, physical_block_size=P, offsets=offsets, gpu_thread_block_size=64)
+    deck = make_deck(w, device)
+    plan = _native.describe_plan(deck, R, P, V)
+    stream = torch.cuda.current_stream(device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    for s in range(args.warmup):
+        povs.shuffle(deck, iterations=iters, options=opts, seed=1000 + s)
+    torch.cuda.synchronize(device)
+    povs.check_device_status(device)
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    barrier()
+    torch.cuda.synchronize(device)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for s in range(args.steps):
+        povs.shuffle(deck, iterations=iters, options=opts, seed=s)
+    stop.record(stream)
+    torch.cuda.synchronize(device)
+    barrier()
+    clocks = sampler.stop()
+    ms = start.elapsed_time(stop)
+    povs.check_device_status(device)
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    deck_bytes = N * R
+    alg_bytes_per_step = 2 * deck_bytes * iters
+    ms_per_step = ms / args.steps
+    value = world * alg_bytes_per_step / (ms_per_step / 1e3) / 1e9
+    launches = args.steps * iters
+    per_launch_s = (ms / 1e3) / launches
+    achieved = 2 * deck_bytes / per_launch_s / 1e9
+    peak, peak_kind = measured_peaks()
+
+    # End to end: the same call with the deck in pinned host memory, copies inside the timed region.
+    e2e = None
+    if not args.no_e2e:
+        import ctypes
+
+        host = torch.empty(deck_bytes, dtype=torch.uint8, pin_memory=True)
+        host.copy_(deck.view(torch.uint8).reshape(-1))
+        staging = deck.view(torch.uint8).reshape(-1)
+        lib = _native.load()
+        offs = (ctypes.c_int64 * len(offsets))(*offsets)
+        e2e_steps = max(1, min(args.steps, args.e2e_steps))
+        rc = lib.povs_shuffle_host_v1(ctypes.c_void_p(host.data_ptr()), ctypes.c_void_p(staging.data_ptr()), N, R,
+                                      offs, len(offsets), iters, P, V, 7, local,
+                                      ctypes.c_void_p(stream.cuda_stream), 0)
+        _native.check(rc, "povs_shuffle_host_v1")
+        barrier()
+        e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e_start.record(stream)
+        for s in range(e2e_steps):
+            rc = lib.povs_shuffle_host_v1(ctypes.c_void_p(host.data_ptr()), ctypes.c_void_p(staging.data_ptr()), N,
+                                          R, offs, len(offsets), iters, P, V, 100 + s, local,
+                                          ctypes.c_void_p(stream.cuda_stream), 0)
+            _native.check(rc, "povs_shuffle_host_v1")
+        e_stop.record(stream)
+        torch.cuda.synchronize(device)
+        e_ms = e_start.elapsed_time(e_stop)
+        if world > 1:
+            t = torch.tensor([e_ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = float(t.item())
+        e2e = {
+            "value": round(world * alg_bytes_per_step / (e_ms / e2e_steps / 1e3) / 1e9, 3),
+            "unit": "GB/s",
+            "h2d_bytes_per_step": deck_bytes,
+            "d2h_bytes_per_step": deck_bytes,
+            "steps": e2e_steps,
+            "ms_per_step": round(e_ms / e2e_steps, 3),
+            "path": "povs_shuffle_host_v1 (pinned host deck)",
+        }
+        del host
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(w, threads=1, target_s=args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 3),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "u8",
+            "data": "synthetic",
+            "config": {
+                "workload": w["desc"],
+                "name": wname,
+                "rows": N,
+                "row_bytes": R,
+                "deck_dtype": w["dtype"],
+                "iterations": iters,
+                "virtual_block_size": V,
+                "physical_block_size": P,
+                "offsets": offsets,
+                "instances_per_s": round(world * N * iters / (ms_per_step / 1e3)),
+                "l2": "inputs larger than L2 (deck > 126 MB)" if deck_bytes > 126e6 else "deck fits L2",
+                "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                "plan": plan,
+            },
+            "roofline": {
+                "bound": "hbm",
+                "kernel": "povs_iteration_kernel",
+                "achieved": round(achieved, 1),
+                "peak": peak,
+                "peak_kind": peak_kind,
+                "unit": "GB/s",
+                "frac": round(achieved / peak, 4),
+                "traffic": traffic_per_launch("povs_iteration_kernel", wname),
+                "alg_bytes_per_launch": 2 * deck_bytes,
+            },
+            "gpu_launches": launches,
+            "clocks": clocks,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def cpu_baseline(w: dict, threads: int, target_s: float) -> dict:
+    """Times the oracle's C restatement of the path on a bounded sample of the workload."""
+    import numpy as np
+
+    from oracle import api as oracle
+    from povs.common import choose_offsets
+
+    R = row_bytes_of(w)
+    elem = {"bfloat16": 2, "float16": 2, "uint8": 1}[w["dtype"]]
+    P, V, iters = w["P"], w["V"], w["iterations"]
+
+    def run(rows: int) -> float:
+        deck = np.random.default_rng(w["seed"]).integers(0, 256, size=(rows, R), dtype=np.uint8)
+        offs = choose_offsets(rows, R // elem, elem, P)
+        t0 = time.perf_counter()
+        if threads == 1:
+            oracle.shuffle(deck, iters, P, V, offs, 11)
+        else:
+            oracle.shuffle_threads(deck, iters, P, V, offs, 11, threads)
+        return time.perf_counter() - t0
+
+    probe_rows = min(w["rows"], max(4096, (64 << 20) // R))
+    t_probe = run(probe_rows)
+    rows = int(min(w["rows"], max(probe_rows, probe_rows * target_s / max(t_probe, 1e-3))))
+    rows = min(rows, max(probe_rows, (8 << 30) // R))  # at most 8 GiB of host memory
+    t = run(rows) if rows != probe_rows else t_probe
+    gbs = 2 * rows * R * iters / t / 1e9
+    return {
+        "value": round(gbs, 3),
+        "unit": "GB/s",
+        "cores": threads,
+        "host_cpus": os.cpu_count(),
+        "kind": "port",
+        "sample": f"{rows:,} of {w['rows']:,} rows x {R} B, {iters} iterations, {t:.2f} s",
+    }
+
+
+def run_reference(args, w: dict, wname: str) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    vals = []
+    cb = None
+    for s in range(args.warmup + args.steps):
+        cb = cpu_baseline(w, threads=threads, target_s=min(5.0, args.cpu_seconds))
+        if s >= args.warmup:
+            vals.append(cb["value"])
+    value = statistics.median(vals) if vals else cb["value"]
+    cb = dict(cb, value=round(value, 3))
+    line = {
+        "metric": METRIC,
+        "impl": "reference",
+        "value": round(value, 3),
+        "unit": "GB/s",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "u8",
+        "data": "synthetic",
+        "config": {"workload": w["desc"], "name": wname},
+        "cpu_baseline": cb,
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "CPU implementation of the path on the host cores: the oracle's C restatement of the POV iteration "
+        "(the reference's own CPU path is Python/NumPy and is not available on this machine)",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="bf16_32GiB", choices=sorted(WORKLOADS))
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    w = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        run_reference(args, w, args.workload)
+    else:
+        run_ours(args, w, args.workload)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,136 @@
+/*
+ * C ABI of the B200-native POV shuffle (libpovs_sm100.so).
+ *
+ * Every entry point takes plain pointers and sizes, returns 0 on success or a
+ * negative POVS_ERR_* code, never terminates the process, and records a
+ * message retrievable with povs_last_error_string() (per calling thread).
+ * Device work is enqueued on the caller's stream (a cudaStream_t passed as
+ * void*; NULL means the legacy default stream) and is asynchronous unless
+ * stated otherwise.  The caller owns every data buffer; the library only keeps
+ * a small per-device context (a status word and cached CUDA graphs), created
+ * on first use and freed by povs_release_v1().
+ *
+ * Rows ("instances") are opaque byte vectors of row_bytes bytes; the deck is
+ * n_rows rows, contiguous.  Shuffling is in place along axis 0.
+ */
+#ifndef POVS_H
+#define POVS_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Return codes. */
+#define POVS_OK 0
+#define POVS_ERR_INVALID_ARGUMENT (-1) /* a size, option or pointer is out of range */
+#define POVS_ERR_UNSUPPORTED (-2)      /* valid for the algorithm but outside this build's limits */
+#define POVS_ERR_CUDA (-3)             /* a CUDA runtime call failed */
+#define POVS_ERR_DEVICE_STATUS (-4)    /* a kernel reported a failure through the device status word */
+
+/* Device status bits reported by povs_device_status_v1(). */
+#define POVS_DEV_WAIT_TIMEOUT 1 /* an async-copy barrier wait gave up after its time limit */
+#define POVS_DEV_BAD_INJECTED 2 /* an injected permutation entry was out of range and was ignored */
+
+/* Flags of povs_shuffle_v1(). */
+#define POVS_FLAG_NO_GRAPH 1u /* launch the iterations one by one instead of replaying a CUDA graph */
+#define POVS_FLAG_SYNC 2u     /* synchronize the stream and check the device status before returning */
+
+/* Limits of this build. */
+#define POVS_MAX_OFFSETS 256 /* offsets are passed to the device inline in the launch parameters */
+#define POVS_MAX_VBLOCK 32   /* one warp lane per member pblock */
+#define POVS_MAX_VP 1024     /* V * P rows per vblock: one warp sorts the permutation in registers */
+
+/*
+ * Shuffle a deck in place: `iterations` POV iterations, all randomness drawn on
+ * the device from `seed` (Philox4x32-10 counters: offset choice, a keyed
+ * bijection of pblocks onto vblock slots, per-vblock permutations).
+ *
+ * Replaces the reference's native entry `torch_binding(X, O, iterations,
+ * pblock, vblock, block_size, seed)` (src/povs/_cuda.pyi:7-15,
+ * src/povs/__cuda/binds/torch.cpp:19-60) and the host loop it dispatches to
+ * (src/povs/__cuda/lib/povs.cu:356-467).  Differences: the device pointer and
+ * the row size replace the typed tensor (any dtype); offsets are a host array;
+ * the GPU thread-block size is not needed; the stream is explicit; errors are
+ * return codes instead of exit().
+ *
+ *   data        device pointer to n_rows * row_bytes bytes
+ *   offsets     host array of n_offsets (1..POVS_MAX_OFFSETS) row offsets, each in [0, n_rows)
+ *   pblock      P, a power of two >= 1;  vblock: V, a power of two in [2, POVS_MAX_VBLOCK]
+ *   device      CUDA ordinal the data lives on
+ *   stream      cudaStream_t of that device, or NULL
+ */
+int povs_shuffle_v1(void* data, int64_t n_rows, int64_t row_bytes, const int64_t* offsets, int32_t n_offsets,
+                    int32_t iterations, int32_t pblock, int32_t vblock, uint64_t seed, int32_t device, void* stream,
+                    uint32_t flags);
+
+/*
+ * Same as povs_shuffle_v1 for a deck in HOST memory: the rows are copied to a
+ * device buffer supplied by the caller (`device_buffer`, at least n_rows *
+ * row_bytes bytes on `device`), shuffled there and copied back, all on
+ * `stream`, and the call returns after the stream has synchronized.  Pinned
+ * host memory gives full PCIe / C2C bandwidth; pageable memory works.
+ *
+ * Serves the reference's CPU route (`povs.shuffle` on a numpy array or a CPU
+ * tensor, src/povs/__init__.py:36-42 -> src/povs/numpy.py:18-61) on the GPU.
+ */
+int povs_shuffle_host_v1(void* host_data, void* device_buffer, int64_t n_rows, int64_t row_bytes,
+                         const int64_t* offsets, int32_t n_offsets, int32_t iterations, int32_t pblock,
+                         int32_t vblock, uint64_t seed, int32_t device, void* stream, uint32_t flags);
+
+/*
+ * Apply externally supplied randomness (test hook for bit-exact parity with the
+ * reference's CPU and CUDA paths).  For each iteration t:
+ *   offsets_per_iter[t]        (host)   the iteration's row offset, in [0, n_rows)
+ *   assign + t*n_v*V           (device) int64 [n_v][V] member pblock ids; values < 0 or
+ *                                       >= ceil(n_rows/P) are padding
+ *   perms  + t*n_v*V*P         (device) int32 [n_v][V*P]; destination slot f of a vblock
+ *                                       receives source slot perms[f] (f < valid rows)
+ * sort_members = 1 orders each vblock's members ascending with padding last, as the
+ * reference kernel does (src/povs/__cuda/lib/povs.cu:203-221); 0 keeps the given order
+ * (the NumPy path, src/povs/numpy.py:120-136), except that padding goes last and a
+ * truncated last pblock is placed after the full ones.
+ * n_v = ceil(ceil(n_rows/P)/V).  Replaces no single reference function: it is the
+ * reference kernel's body (povs.cu:116-349) with the host RNG (povs.cu:415-431) cut out.
+ */
+int povs_apply_v1(void* data, int64_t n_rows, int64_t row_bytes, int32_t pblock, int32_t vblock,
+                  int32_t iterations, const int64_t* offsets_per_iter, const int64_t* assign, const int32_t* perms,
+                  int32_t sort_members, int32_t device, void* stream);
+
+/* Read and clear the device status word of `device` (synchronizes the device's context). Writes bits to *status. */
+int povs_device_status_v1(int32_t device, int32_t* status);
+
+/* Free the per-device context (status word, cached graphs) of every device touched. */
+int povs_release_v1(void);
+
+/* Message describing the last error returned on the calling thread ("" if none). */
+const char* povs_last_error_string(void);
+
+/* Library version: major * 10000 + minor * 100 + patch. */
+int32_t povs_version(void);
+
+/*
+ * Advanced: process-wide launch tuning (no reference counterpart; the reference
+ * fixes these at compile time through template parameters, povs.cu:116,433-436).
+ *   stage_cap   max bytes of one shared-memory stage; vblocks whose V*P rows exceed it are
+ *               processed in column slabs (default 32768)
+ *   n_stages    stages per warp, 2..8 (default 2)
+ *   max_warps   warps per CTA, 1..16 (default 16)
+ *   force_plain 1 = plain vector loads instead of TMA bulk copies
+ */
+int povs_set_tuning_v1(int32_t stage_cap, int32_t n_stages, int32_t max_warps, int32_t force_plain);
+
+/*
+ * Advanced: report the launch plan povs_shuffle_v1 would use, as int64 values
+ * {grid, block, dynamic smem, sort elements per lane, bulk (0/1), slab bytes, slabs,
+ *  stages per warp, stage bytes, vector bytes, vblocks, SM count}; returns how many were written.
+ */
+int povs_describe_plan_v1(void* data, int64_t n_rows, int64_t row_bytes, int32_t pblock, int32_t vblock,
+                          int32_t device, int64_t* out, int32_t n_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* POVS_H */

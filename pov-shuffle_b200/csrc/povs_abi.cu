@@ -1,0 +1,581 @@
+// C ABI of the B200 POV shuffle: argument checks, launch planning, per-device
+// context and CUDA-graph chaining of iterations.  Declarations and the
+// reference interfaces each entry replaces are in include/povs.h.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/povs.h"
+#include "povs_kernel.cuh"
+
+using povs::IterParams;
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...)
+{
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what)
+{
+    return fail(POVS_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+#define POVS_CUDA_TRY(expr)                                \
+    do {                                                   \
+        cudaError_t e_ = (expr);                           \
+        if (e_ != cudaSuccess) return cuda_fail(e_, #expr); \
+    } while (0)
+
+bool is_pow2(int64_t x) { return x > 0 && (x & (x - 1)) == 0; }
+
+int ilog2(int64_t x)
+{
+    int s = 0;
+    while ((int64_t{1} << s) < x) ++s;
+    return s;
+}
+
+// ------------------------------------------------------------------------------------------
+// Kernel table.
+// ------------------------------------------------------------------------------------------
+
+using KernelFn = void (*)(IterParams);
+
+template <bool INJ, bool BULK>
+KernelFn kernel_for_epl(int epl)
+{
+    switch (epl) {
+    case 1: return povs::povs_iteration_kernel<1, INJ, BULK>;
+    case 2: return povs::povs_iteration_kernel<2, INJ, BULK>;
+    case 4: return povs::povs_iteration_kernel<4, INJ, BULK>;
+    case 8: return povs::povs_iteration_kernel<8, INJ, BULK>;
+    case 16: return povs::povs_iteration_kernel<16, INJ, BULK>;
+    case 32: return povs::povs_iteration_kernel<32, INJ, BULK>;
+    default: return nullptr;
+    }
+}
+
+KernelFn select_kernel(int epl, bool injected, bool bulk)
+{
+    if (injected) return bulk ? kernel_for_epl<true, true>(epl) : kernel_for_epl<true, false>(epl);
+    return bulk ? kernel_for_epl<false, true>(epl) : kernel_for_epl<false, false>(epl);
+}
+
+// ------------------------------------------------------------------------------------------
+// Tuning knobs (process-wide; defaults chosen by measurement on B200).
+// ------------------------------------------------------------------------------------------
+
+struct Tuning {
+    int stage_cap = 32 * 1024; // max bytes of one stage; larger vblocks are split into column slabs
+    int n_stages = 2;          // stages per warp
+    int max_warps = 16;        // warps per CTA
+    int force_plain = 0;       // 1 = never use TMA bulk loads
+};
+Tuning g_tuning;
+std::mutex g_tuning_mu;
+
+// ------------------------------------------------------------------------------------------
+// Per-device context.
+// ------------------------------------------------------------------------------------------
+
+struct GraphKey {
+    KernelFn fn;
+    int grid, block, smem, iterations;
+    bool operator==(const GraphKey& o) const
+    {
+        return fn == o.fn && grid == o.grid && block == o.block && smem == o.smem && iterations == o.iterations;
+    }
+};
+struct GraphKeyHash {
+    size_t operator()(const GraphKey& k) const
+    {
+        size_t h = reinterpret_cast<size_t>(k.fn);
+        h = h * 1000003u ^ static_cast<size_t>(k.grid);
+        h = h * 1000003u ^ static_cast<size_t>(k.block);
+        h = h * 1000003u ^ static_cast<size_t>(k.smem);
+        h = h * 1000003u ^ static_cast<size_t>(k.iterations);
+        return h;
+    }
+};
+struct CachedGraph {
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    std::vector<cudaGraphNode_t> nodes;
+};
+
+struct DeviceCtx {
+    bool ready = false;
+    int sm_count = 0;
+    int smem_optin = 0;  // max dynamic shared memory per block
+    int smem_per_sm = 0; // shared memory per multiprocessor
+    int max_threads_per_sm = 0;
+    int* status = nullptr;
+    std::mutex mu; // guards the graph cache and launches that reuse it
+    std::unordered_map<GraphKey, CachedGraph, GraphKeyHash> graphs;
+};
+
+constexpr int MAX_DEVICES = 64;
+DeviceCtx g_ctx[MAX_DEVICES];
+std::mutex g_ctx_mu;
+
+struct DeviceGuard {
+    int prev = -1;
+    bool changed = false;
+    int enter(int dev)
+    {
+        cudaError_t e = cudaGetDevice(&prev);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+        if (prev != dev) {
+            e = cudaSetDevice(dev);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+            changed = true;
+        }
+        return POVS_OK;
+    }
+    ~DeviceGuard()
+    {
+        if (changed) cudaSetDevice(prev);
+    }
+};
+
+int set_smem_attr_all(int smem)
+{
+    for (int inj = 0; inj < 2; ++inj)
+        for (int bulk = 0; bulk < 2; ++bulk)
+            for (int epl = 1; epl <= 32; epl <<= 1) {
+                KernelFn fn = select_kernel(epl, inj != 0, bulk != 0);
+                cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                                                     cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+                if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+            }
+    return POVS_OK;
+}
+
+// Called with the device current.
+int get_ctx(int dev, DeviceCtx** out)
+{
+    if (dev < 0 || dev >= MAX_DEVICES) return fail(POVS_ERR_INVALID_ARGUMENT, "device %d out of range", dev);
+    std::lock_guard<std::mutex> lk(g_ctx_mu);
+    DeviceCtx& c = g_ctx[dev];
+    if (!c.ready) {
+        cudaDeviceProp prop;
+        POVS_CUDA_TRY(cudaGetDeviceProperties(&prop, dev));
+        if (prop.major < 10)
+            return fail(POVS_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a (B200)", dev,
+                        prop.major, prop.minor);
+        c.sm_count = prop.multiProcessorCount;
+        c.smem_optin = static_cast<int>(prop.sharedMemPerBlockOptin);
+        c.smem_per_sm = static_cast<int>(prop.sharedMemPerMultiprocessor);
+        c.max_threads_per_sm = prop.maxThreadsPerMultiProcessor;
+        int r = set_smem_attr_all(c.smem_optin);
+        if (r != POVS_OK) return r;
+        POVS_CUDA_TRY(cudaMalloc(&c.status, sizeof(int)));
+        POVS_CUDA_TRY(cudaMemset(c.status, 0, sizeof(int)));
+        c.ready = true;
+    }
+    *out = &c;
+    return POVS_OK;
+}
+
+// ------------------------------------------------------------------------------------------
+// Launch planning.
+// ------------------------------------------------------------------------------------------
+
+struct Plan {
+    KernelFn fn = nullptr;
+    int grid = 0, block = 0, smem = 0, epl = 0;
+    bool bulk = false;
+};
+
+int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out)
+{
+    Tuning t;
+    {
+        std::lock_guard<std::mutex> lk(g_tuning_mu);
+        t = g_tuning;
+    }
+    const int64_t vp = static_cast<int64_t>(p.vblock) * p.pblock;
+    if (vp > POVS_MAX_VP)
+        return fail(POVS_ERR_UNSUPPORTED, "virtual_block_size * physical_block_size = %lld exceeds %d",
+                    static_cast<long long>(vp), POVS_MAX_VP);
+    int epl = 1;
+    while (32 * epl < vp) epl <<= 1;
+
+    const uintptr_t addr = reinterpret_cast<uintptr_t>(p.data);
+    int vec = 16;
+    while (vec > 1 && ((p.row_bytes % vec) != 0 || (addr % vec) != 0)) vec >>= 1;
+    const bool bulk = (vec == 16) && !t.force_plain;
+
+    // Slab width: whole rows when a vblock fits a stage, else the widest 128-byte (or vec) multiple that does.
+    int64_t slab = p.row_bytes;
+    if (vp * p.row_bytes > t.stage_cap) {
+        const int64_t fit = t.stage_cap / vp;
+        const int64_t gran = fit >= 128 ? 128 : vec;
+        slab = std::max<int64_t>(vec, (fit / gran) * gran);
+    }
+    int nst = std::max(2, std::min(t.n_stages, 8));
+    int64_t stage_bytes = ((vp * slab + 127) / 128) * 128;
+    int warp_bytes = povs::warp_smem_bytes(nst, static_cast<int>(stage_bytes), static_cast<int>(vp));
+    // Shrink the slab until at least one warp fits.
+    while (warp_bytes > c.smem_optin && slab > vec) {
+        slab = std::max<int64_t>(vec, ((slab / 2) / vec) * vec);
+        stage_bytes = ((vp * slab + 127) / 128) * 128;
+        warp_bytes = povs::warp_smem_bytes(nst, static_cast<int>(stage_bytes), static_cast<int>(vp));
+    }
+    if (warp_bytes > c.smem_optin)
+        return fail(POVS_ERR_UNSUPPORTED, "a vblock of %lld rows does not fit shared memory", static_cast<long long>(vp));
+
+    int warps = std::min<int64_t>(std::max(1, t.max_warps), c.smem_optin / warp_bytes);
+    warps = std::max(1, std::min(warps, 16));
+    // No more warps than vblocks.
+    if (p.n_vblocks < warps) warps = static_cast<int>(p.n_vblocks);
+    const int cta_smem = warps * warp_bytes;
+    const int per_sm_by_smem = std::max(1, c.smem_per_sm / (cta_smem + 1024));
+    const int per_sm_by_threads = std::max(1, c.max_threads_per_sm / (warps * 32));
+    const int ctas_per_sm = std::min(per_sm_by_smem, per_sm_by_threads);
+    const int64_t want = (p.n_vblocks + warps - 1) / warps;
+    const int grid = static_cast<int>(std::min<int64_t>(want, static_cast<int64_t>(c.sm_count) * ctas_per_sm));
+
+    p.slab_bytes = static_cast<int32_t>(slab);
+    p.n_slabs = static_cast<int32_t>((p.row_bytes + slab - 1) / slab);
+    p.stage_bytes = static_cast<int32_t>(stage_bytes);
+    p.n_stages = nst;
+    p.warp_bytes = warp_bytes;
+    p.vec_bytes = vec;
+
+    out.fn = select_kernel(epl, injected, bulk);
+    out.grid = std::max(1, grid);
+    out.block = warps * 32;
+    out.smem = cta_smem;
+    out.epl = epl;
+    out.bulk = bulk;
+    return POVS_OK;
+}
+
+int check_common(void* data, int64_t n_rows, int64_t row_bytes, int32_t pblock, int32_t vblock, int32_t iterations)
+{
+    if (data == nullptr) return fail(POVS_ERR_INVALID_ARGUMENT, "data is NULL");
+    if (n_rows < 2) return fail(POVS_ERR_INVALID_ARGUMENT, "deck must have at least 2 rows, has %lld", static_cast<long long>(n_rows));
+    if (row_bytes < 1) return fail(POVS_ERR_INVALID_ARGUMENT, "row_bytes must be positive");
+    if (iterations < 0) return fail(POVS_ERR_INVALID_ARGUMENT, "iterations (%d) must be non-negative", iterations);
+    if (!is_pow2(pblock)) return fail(POVS_ERR_INVALID_ARGUMENT, "pblock size (%d) must be a power of 2", pblock);
+    if (!is_pow2(vblock) || vblock < 2)
+        return fail(POVS_ERR_INVALID_ARGUMENT, "vblock size (%d) must be a power of 2 and at least 2", vblock);
+    if (vblock > POVS_MAX_VBLOCK)
+        return fail(POVS_ERR_UNSUPPORTED, "vblock size (%d) exceeds %d", vblock, POVS_MAX_VBLOCK);
+    if (row_bytes > (int64_t{1} << 40)) return fail(POVS_ERR_UNSUPPORTED, "row_bytes too large");
+    return POVS_OK;
+}
+
+void fill_geometry(IterParams& p, void* data, int64_t n_rows, int64_t row_bytes, int32_t pblock, int32_t vblock,
+                   int* status)
+{
+    std::memset(&p, 0, sizeof(p));
+    p.data = static_cast<uint8_t*>(data);
+    p.n_rows = n_rows;
+    p.row_bytes = row_bytes;
+    p.pblock = pblock;
+    p.pblock_shift = ilog2(pblock);
+    p.vblock = vblock;
+    p.vp = pblock * vblock;
+    p.n_pblocks = (n_rows + pblock - 1) / pblock;
+    p.n_vblocks = (p.n_pblocks + vblock - 1) / vblock;
+    p.status = status;
+}
+
+int launch_direct(const Plan& pl, const IterParams& p, cudaStream_t s)
+{
+    void* args[] = {const_cast<IterParams*>(&p)};
+    cudaError_t e = cudaLaunchKernel(reinterpret_cast<const void*>(pl.fn), dim3(pl.grid), dim3(pl.block), args,
+                                     static_cast<size_t>(pl.smem), s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernel");
+    return POVS_OK;
+}
+
+// Replays `iters` chained iteration kernels as one CUDA graph (cached per launch shape).
+int launch_graph(DeviceCtx& c, const Plan& pl, std::vector<IterParams>& ps, cudaStream_t s)
+{
+    const int iters = static_cast<int>(ps.size());
+    std::lock_guard<std::mutex> lk(c.mu);
+    GraphKey key{pl.fn, pl.grid, pl.block, pl.smem, iters};
+    auto it = c.graphs.find(key);
+    if (it == c.graphs.end()) {
+        CachedGraph g;
+        POVS_CUDA_TRY(cudaGraphCreate(&g.graph, 0));
+        cudaGraphNode_t prev = nullptr;
+        for (int i = 0; i < iters; ++i) {
+            cudaKernelNodeParams kp{};
+            void* args[] = {&ps[i]};
+            kp.func = reinterpret_cast<void*>(pl.fn);
+            kp.gridDim = dim3(pl.grid);
+            kp.blockDim = dim3(pl.block);
+            kp.sharedMemBytes = static_cast<unsigned>(pl.smem);
+            kp.kernelParams = args;
+            cudaGraphNode_t node;
+            POVS_CUDA_TRY(cudaGraphAddKernelNode(&node, g.graph, prev ? &prev : nullptr, prev ? 1 : 0, &kp));
+            g.nodes.push_back(node);
+            prev = node;
+        }
+        POVS_CUDA_TRY(cudaGraphInstantiate(&g.exec, g.graph, 0));
+        it = c.graphs.emplace(key, std::move(g)).first;
+    } else {
+        for (int i = 0; i < iters; ++i) {
+            cudaKernelNodeParams kp{};
+            void* args[] = {&ps[i]};
+            kp.func = reinterpret_cast<void*>(pl.fn);
+            kp.gridDim = dim3(pl.grid);
+            kp.blockDim = dim3(pl.block);
+            kp.sharedMemBytes = static_cast<unsigned>(pl.smem);
+            kp.kernelParams = args;
+            POVS_CUDA_TRY(cudaGraphExecKernelNodeSetParams(it->second.exec, it->second.nodes[i], &kp));
+        }
+    }
+    POVS_CUDA_TRY(cudaGraphLaunch(it->second.exec, s));
+    return POVS_OK;
+}
+
+int read_status(DeviceCtx& c, int32_t* out)
+{
+    POVS_CUDA_TRY(cudaDeviceSynchronize());
+    int v = 0;
+    POVS_CUDA_TRY(cudaMemcpy(&v, c.status, sizeof(int), cudaMemcpyDeviceToHost));
+    POVS_CUDA_TRY(cudaMemset(c.status, 0, sizeof(int)));
+    if (out) *out = v;
+    return POVS_OK;
+}
+
+int shuffle_on_device(void* data, int64_t n_rows, int64_t row_bytes, const int64_t* offsets, int32_t n_offsets,
+                      int32_t iterations, int32_t pblock, int32_t vblock, uint64_t seed, DeviceCtx& c,
+                      cudaStream_t s, uint32_t flags)
+{
+    IterParams base;
+    fill_geometry(base, data, n_rows, row_bytes, pblock, vblock, c.status);
+    base.seed = seed;
+    base.n_offsets = n_offsets;
+    for (int i = 0; i < n_offsets; ++i) base.offsets[i] = offsets[i];
+    Plan pl;
+    int r = plan_launch(base, c, false, pl);
+    if (r != POVS_OK) return r;
+    if (iterations == 0) return POVS_OK;
+    std::vector<IterParams> ps(static_cast<size_t>(iterations), base);
+    for (int i = 0; i < iterations; ++i) ps[i].iteration = static_cast<uint32_t>(i);
+    if (iterations == 1 || (flags & POVS_FLAG_NO_GRAPH)) {
+        for (int i = 0; i < iterations; ++i) {
+            r = launch_direct(pl, ps[i], s);
+            if (r != POVS_OK) return r;
+        }
+    } else {
+        r = launch_graph(c, pl, ps, s);
+        if (r != POVS_OK) return r;
+    }
+    if (flags & POVS_FLAG_SYNC) {
+        POVS_CUDA_TRY(cudaStreamSynchronize(s));
+        int32_t st = 0;
+        r = read_status(c, &st);
+        if (r != POVS_OK) return r;
+        if (st != 0) return fail(POVS_ERR_DEVICE_STATUS, "device status 0x%x after shuffle", st);
+    }
+    return POVS_OK;
+}
+
+int check_offsets(const int64_t* offsets, int32_t n_offsets, int64_t n_rows)
+{
+    if (offsets == nullptr || n_offsets < 1) return fail(POVS_ERR_INVALID_ARGUMENT, "at least one offset is required");
+    if (n_offsets > POVS_MAX_OFFSETS)
+        return fail(POVS_ERR_UNSUPPORTED, "%d offsets exceed the limit of %d", n_offsets, POVS_MAX_OFFSETS);
+    for (int i = 0; i < n_offsets; ++i)
+        if (offsets[i] < 0 || offsets[i] >= n_rows)
+            return fail(POVS_ERR_INVALID_ARGUMENT, "offset at index %d (%lld) must be in [0, %lld)", i,
+                        static_cast<long long>(offsets[i]), static_cast<long long>(n_rows));
+    return POVS_OK;
+}
+
+} // namespace
+
+// ------------------------------------------------------------------------------------------
+// Exported entry points.
+// ------------------------------------------------------------------------------------------
+
+extern "C" int povs_shuffle_v1(void* data, int64_t n_rows, int64_t row_bytes, const int64_t* offsets,
+                               int32_t n_offsets, int32_t iterations, int32_t pblock, int32_t vblock, uint64_t seed,
+                               int32_t device, void* stream, uint32_t flags)
+{
+    g_err[0] = '\0';
+    int r = check_common(data, n_rows, row_bytes, pblock, vblock, iterations);
+    if (r != POVS_OK) return r;
+    r = check_offsets(offsets, n_offsets, n_rows);
+    if (r != POVS_OK) return r;
+    DeviceGuard dg;
+    r = dg.enter(device);
+    if (r != POVS_OK) return r;
+    DeviceCtx* c = nullptr;
+    r = get_ctx(device, &c);
+    if (r != POVS_OK) return r;
+    return shuffle_on_device(data, n_rows, row_bytes, offsets, n_offsets, iterations, pblock, vblock, seed, *c,
+                             static_cast<cudaStream_t>(stream), flags);
+}
+
+extern "C" int povs_shuffle_host_v1(void* host_data, void* device_buffer, int64_t n_rows, int64_t row_bytes,
+                                    const int64_t* offsets, int32_t n_offsets, int32_t iterations, int32_t pblock,
+                                    int32_t vblock, uint64_t seed, int32_t device, void* stream, uint32_t flags)
+{
+    g_err[0] = '\0';
+    if (host_data == nullptr) return fail(POVS_ERR_INVALID_ARGUMENT, "host_data is NULL");
+    int r = check_common(device_buffer, n_rows, row_bytes, pblock, vblock, iterations);
+    if (r != POVS_OK) return r;
+    r = check_offsets(offsets, n_offsets, n_rows);
+    if (r != POVS_OK) return r;
+    DeviceGuard dg;
+    r = dg.enter(device);
+    if (r != POVS_OK) return r;
+    DeviceCtx* c = nullptr;
+    r = get_ctx(device, &c);
+    if (r != POVS_OK) return r;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t bytes = static_cast<size_t>(n_rows) * static_cast<size_t>(row_bytes);
+    POVS_CUDA_TRY(cudaMemcpyAsync(device_buffer, host_data, bytes, cudaMemcpyHostToDevice, s));
+    r = shuffle_on_device(device_buffer, n_rows, row_bytes, offsets, n_offsets, iterations, pblock, vblock, seed, *c,
+                          s, flags & ~POVS_FLAG_SYNC);
+    if (r != POVS_OK) return r;
+    POVS_CUDA_TRY(cudaMemcpyAsync(host_data, device_buffer, bytes, cudaMemcpyDeviceToHost, s));
+    POVS_CUDA_TRY(cudaStreamSynchronize(s));
+    if (flags & POVS_FLAG_SYNC) {
+        int32_t st = 0;
+        r = read_status(*c, &st);
+        if (r != POVS_OK) return r;
+        if (st != 0) return fail(POVS_ERR_DEVICE_STATUS, "device status 0x%x after shuffle", st);
+    }
+    return POVS_OK;
+}
+
+extern "C" int povs_apply_v1(void* data, int64_t n_rows, int64_t row_bytes, int32_t pblock, int32_t vblock,
+                             int32_t iterations, const int64_t* offsets_per_iter, const int64_t* assign,
+                             const int32_t* perms, int32_t sort_members, int32_t device, void* stream)
+{
+    g_err[0] = '\0';
+    int r = check_common(data, n_rows, row_bytes, pblock, vblock, iterations);
+    if (r != POVS_OK) return r;
+    if (iterations > 0 && (offsets_per_iter == nullptr || assign == nullptr || perms == nullptr))
+        return fail(POVS_ERR_INVALID_ARGUMENT, "offsets_per_iter, assign and perms are required");
+    for (int i = 0; i < iterations; ++i)
+        if (offsets_per_iter[i] < 0 || offsets_per_iter[i] >= n_rows)
+            return fail(POVS_ERR_INVALID_ARGUMENT, "offset of iteration %d (%lld) must be in [0, %lld)", i,
+                        static_cast<long long>(offsets_per_iter[i]), static_cast<long long>(n_rows));
+    DeviceGuard dg;
+    r = dg.enter(device);
+    if (r != POVS_OK) return r;
+    DeviceCtx* c = nullptr;
+    r = get_ctx(device, &c);
+    if (r != POVS_OK) return r;
+    IterParams base;
+    fill_geometry(base, data, n_rows, row_bytes, pblock, vblock, c->status);
+    base.sort_members = sort_members ? 1 : 0;
+    Plan pl;
+    r = plan_launch(base, *c, true, pl);
+    if (r != POVS_OK) return r;
+    const int64_t n_slots = base.n_vblocks * vblock;
+    const int64_t n_perm = base.n_vblocks * static_cast<int64_t>(base.vp);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    for (int i = 0; i < iterations; ++i) {
+        IterParams p = base;
+        p.iteration = static_cast<uint32_t>(i);
+        p.offset = offsets_per_iter[i];
+        p.assign = assign + i * n_slots;
+        p.perms = perms + i * n_perm;
+        r = launch_direct(pl, p, s);
+        if (r != POVS_OK) return r;
+    }
+    return POVS_OK;
+}
+
+extern "C" int povs_device_status_v1(int32_t device, int32_t* status)
+{
+    g_err[0] = '\0';
+    DeviceGuard dg;
+    int r = dg.enter(device);
+    if (r != POVS_OK) return r;
+    DeviceCtx* c = nullptr;
+    r = get_ctx(device, &c);
+    if (r != POVS_OK) return r;
+    return read_status(*c, status);
+}
+
+extern "C" int povs_release_v1(void)
+{
+    g_err[0] = '\0';
+    std::lock_guard<std::mutex> lk(g_ctx_mu);
+    int prev = -1;
+    cudaGetDevice(&prev);
+    for (int d = 0; d < MAX_DEVICES; ++d) {
+        DeviceCtx& c = g_ctx[d];
+        if (!c.ready) continue;
+        cudaSetDevice(d);
+        std::lock_guard<std::mutex> lk2(c.mu);
+        for (auto& kv : c.graphs) {
+            if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+            if (kv.second.graph) cudaGraphDestroy(kv.second.graph);
+        }
+        c.graphs.clear();
+        if (c.status) cudaFree(c.status);
+        c.status = nullptr;
+        c.ready = false;
+    }
+    if (prev >= 0) cudaSetDevice(prev);
+    return POVS_OK;
+}
+
+extern "C" const char* povs_last_error_string(void) { return g_err; }
+
+extern "C" int32_t povs_version(void) { return 100; }
+
+// Tuning and introspection.
+extern "C" int povs_set_tuning_v1(int32_t stage_cap, int32_t n_stages, int32_t max_warps, int32_t force_plain)
+{
+    g_err[0] = '\0';
+    if (stage_cap < 1024 || n_stages < 2 || n_stages > 8 || max_warps < 1 || max_warps > 16)
+        return fail(POVS_ERR_INVALID_ARGUMENT, "tuning out of range");
+    std::lock_guard<std::mutex> lk(g_tuning_mu);
+    g_tuning.stage_cap = stage_cap;
+    g_tuning.n_stages = n_stages;
+    g_tuning.max_warps = max_warps;
+    g_tuning.force_plain = force_plain ? 1 : 0;
+    return POVS_OK;
+}
+
+extern "C" int povs_describe_plan_v1(void* data, int64_t n_rows, int64_t row_bytes, int32_t pblock, int32_t vblock,
+                                     int32_t device, int64_t* out, int32_t n_out)
+{
+    g_err[0] = '\0';
+    int r = check_common(data, n_rows, row_bytes, pblock, vblock, 1);
+    if (r != POVS_OK) return r;
+    DeviceGuard dg;
+    r = dg.enter(device);
+    if (r != POVS_OK) return r;
+    DeviceCtx* c = nullptr;
+    r = get_ctx(device, &c);
+    if (r != POVS_OK) return r;
+    IterParams p;
+    fill_geometry(p, data, n_rows, row_bytes, pblock, vblock, c->status);
+    Plan pl;
+    r = plan_launch(p, *c, false, pl);
+    if (r != POVS_OK) return r;
+    const int64_t vals[] = {pl.grid, pl.block, pl.smem, pl.epl, pl.bulk ? 1 : 0, p.slab_bytes, p.n_slabs,
+                            p.n_stages, p.stage_bytes, p.vec_bytes, p.n_vblocks, c->sm_count};
+    const int n = std::min<int>(n_out, static_cast<int>(sizeof(vals) / sizeof(vals[0])));
+    for (int i = 0; i < n; ++i) out[i] = vals[i];
+    return n;
+}

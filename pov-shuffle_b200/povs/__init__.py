@@ -1,0 +1,98 @@
+"""B200-native POV shuffle: a drop-in for the reference's ``povs`` package (src/povs/__init__.py).
+
+Public API kept from the reference: ``shuffle``, ``Options``, ``BuildParams``, ``get_build_params``,
+``optim_options_for_dataset``.  Additions: ``apply_randomness`` (inject offsets, block assignments
+and per-vblock permutations, for bit-exact comparison with other implementations) and
+``check_device_status``.
+"""
+
+from __future__ import annotations
+
+from typing import Any
+
+import numpy as np
+import torch as t
+
+from . import numpy as povs_numpy
+from . import torch as povs_torch
+from .common import get_build_params, get_int_seed
+from .injection import apply_randomness
+from .types import BuildParams, Options
+
+__all__ = [
+    "shuffle",
+    "Options",
+    "BuildParams",
+    "get_build_params",
+    "optim_options_for_dataset",
+    "apply_randomness",
+    "check_device_status",
+]
+
+
+def shuffle(
+    data: np.ndarray | t.Tensor,
+    iterations: int = 1,
+    options: Options | None = None,
+    seed: int | np.random.Generator | Any | None = None,
+) -> None:
+    """POV Shuffle, in place along axis 0.
+
+    :param data: ``torch.Tensor`` (CUDA or CPU) or ``numpy.ndarray``.
+    :param iterations: Number of shuffling iterations.
+    :param options: POV options; partial or missing options are resolved as in ``optim_options_for_dataset``.
+    :param seed: Integer seed, ``np.random.Generator`` or ``torch.Generator`` (None draws fresh entropy).
+    """
+    seed = get_int_seed(seed)
+
+    if isinstance(data, np.ndarray):
+        povs_numpy.shuffle(data, iterations, options, seed)
+        return
+
+    if isinstance(data, t.Tensor):
+        if data.get_device() == -1:
+            shuffle(data.numpy(), iterations, options, seed)
+            return
+        povs_torch.shuffle(data, iterations, options, seed)
+        return
+
+    raise TypeError(f"Unsupported data type: {type(data)}")
+
+
+def optim_options_for_dataset(data: np.ndarray | t.Tensor, options: Options | None = None) -> Options:
+    """Resolve partial or missing options for a dataset.
+
+    :param data: ``torch.Tensor`` or ``numpy.ndarray``.
+    :param options: Starting point.
+    :returns: Complete options for the dataset's route (CUDA options include ``gpu_thread_block_size``).
+    """
+    options = options or Options()
+
+    if isinstance(data, np.ndarray):
+        if povs_numpy.options_is_complete(options):
+            return options
+        return povs_numpy.optim_options_for_dataset(data, options)
+
+    if isinstance(data, t.Tensor):
+        if data.get_device() == -1:
+            return optim_options_for_dataset(data.numpy(), options)
+        if povs_torch.options_is_complete(options):
+            return options
+        return povs_torch.optim_options_for_dataset(data, options)
+
+    raise TypeError(f"Unsupported data type: {type(data)}")
+
+
+def check_device_status(device: int | t.device | None = None) -> None:
+    """Synchronize ``device`` and raise ``RuntimeError`` if a kernel reported a failure since the last check."""
+    from . import _native
+
+    if device is None:
+        index = t.cuda.current_device()
+    elif isinstance(device, t.device):
+        index = device.index if device.index is not None else t.cuda.current_device()
+    else:
+        index = int(device)
+    status = _native.device_status(index)
+    if status:
+        raise RuntimeError(f"povs kernels on cuda:{index} reported device status 0x{status:x}")

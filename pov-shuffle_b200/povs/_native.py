@@ -1,0 +1,230 @@
+"""ctypes binding of the C ABI in include/povs.h (libpovs_sm100.so, built in tree).
+
+This module is the only path to the GPU: if the library is missing or fails to load, every
+call raises instead of falling back to another implementation.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+import torch
+
+from . import _build
+
+_LIB: ctypes.CDLL | None = None
+_LOCK = threading.Lock()
+
+POVS_OK = 0
+ERRORS = {-1: "invalid argument", -2: "unsupported", -3: "CUDA error", -4: "device status"}
+
+FLAG_NO_GRAPH = 1
+FLAG_SYNC = 2
+
+# (name, restype, argtypes) of every exported symbol declared in include/povs.h.
+_c_i32, _c_i64, _c_u32, _c_u64, _c_vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_void_p
+_P_I64 = ctypes.POINTER(ctypes.c_int64)
+_P_I32 = ctypes.POINTER(ctypes.c_int32)
+SIGNATURES: dict[str, tuple] = {
+    "povs_shuffle_v1": (ctypes.c_int, [_c_vp, _c_i64, _c_i64, _P_I64, _c_i32, _c_i32, _c_i32, _c_i32, _c_u64, _c_i32, _c_vp, _c_u32]),
+    "povs_shuffle_host_v1": (
+        ctypes.c_int,
+        [_c_vp, _c_vp, _c_i64, _c_i64, _P_I64, _c_i32, _c_i32, _c_i32, _c_i32, _c_u64, _c_i32, _c_vp, _c_u32],
+    ),
+    "povs_apply_v1": (ctypes.c_int, [_c_vp, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _P_I64, _c_vp, _c_vp, _c_i32, _c_i32, _c_vp]),
+    "povs_device_status_v1": (ctypes.c_int, [_c_i32, _P_I32]),
+    "povs_release_v1": (ctypes.c_int, []),
+    "povs_last_error_string": (ctypes.c_char_p, []),
+    "povs_version": (ctypes.c_int32, []),
+    "povs_set_tuning_v1": (ctypes.c_int, [_c_i32, _c_i32, _c_i32, _c_i32]),
+    "povs_describe_plan_v1": (ctypes.c_int, [_c_vp, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _P_I64, _c_i32]),
+}
+
+
+def library_path() -> Path:
+    return Path(os.environ.get("POVS_LIBRARY", str(_build.LIB_PATH)))
+
+
+def load(build_if_missing: bool = False) -> ctypes.CDLL:
+    """Load (once) the native library; optionally build it first if it is absent or stale."""
+    global _LIB
+    with _LOCK:
+        if _LIB is not None:
+            return _LIB
+        path = library_path()
+        if build_if_missing and "POVS_LIBRARY" not in os.environ and _build.is_stale():
+            _build.build()
+        if not path.exists():
+            raise RuntimeError(
+                f"povs native library not found at {path}; build it with `python -m povs._build` "
+                "(requires nvcc with sm_100a support)"
+            )
+        lib = ctypes.CDLL(str(path))
+        for name, (restype, argtypes) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = restype
+            fn.argtypes = argtypes
+        _LIB = lib
+        return lib
+
+
+def last_error() -> str:
+    return load().povs_last_error_string().decode(errors="replace")
+
+
+def check(code: int, what: str) -> None:
+    if code < 0:
+        raise RuntimeError(f"{what} failed ({ERRORS.get(code, code)}): {last_error()}")
+
+
+def _i64_array(values) -> ctypes.Array:
+    vals = [int(v) for v in values]
+    return (ctypes.c_int64 * max(1, len(vals)))(*vals)
+
+
+def current_stream_handle(device: torch.device) -> int:
+    return int(torch.cuda.current_stream(device).cuda_stream)
+
+
+def shuffle_device(
+    data: torch.Tensor,
+    row_bytes: int,
+    offsets: list[int],
+    iterations: int,
+    pblock: int,
+    vblock: int,
+    seed: int,
+    flags: int = 0,
+) -> None:
+    """Shuffle a contiguous CUDA tensor in place on its device's current stream."""
+    lib = load()
+    dev = data.device
+    offs = _i64_array(offsets)
+    code = lib.povs_shuffle_v1(
+        ctypes.c_void_p(data.data_ptr()),
+        data.shape[0],
+        row_bytes,
+        offs,
+        len(offsets),
+        iterations,
+        pblock,
+        vblock,
+        seed,
+        dev.index,
+        ctypes.c_void_p(current_stream_handle(dev)),
+        flags,
+    )
+    check(code, "povs_shuffle_v1")
+
+
+def shuffle_host(
+    host_ptr: int,
+    device_buffer: torch.Tensor,
+    n_rows: int,
+    row_bytes: int,
+    offsets: list[int],
+    iterations: int,
+    pblock: int,
+    vblock: int,
+    seed: int,
+    flags: int = 0,
+) -> None:
+    """Shuffle rows in host memory through ``device_buffer`` (blocks until the copy back is done)."""
+    lib = load()
+    dev = device_buffer.device
+    offs = _i64_array(offsets)
+    code = lib.povs_shuffle_host_v1(
+        ctypes.c_void_p(host_ptr),
+        ctypes.c_void_p(device_buffer.data_ptr()),
+        n_rows,
+        row_bytes,
+        offs,
+        len(offsets),
+        iterations,
+        pblock,
+        vblock,
+        seed,
+        dev.index,
+        ctypes.c_void_p(current_stream_handle(dev)),
+        flags,
+    )
+    check(code, "povs_shuffle_host_v1")
+
+
+def apply(
+    data: torch.Tensor,
+    row_bytes: int,
+    pblock: int,
+    vblock: int,
+    offsets_per_iter: list[int],
+    assign: torch.Tensor,
+    perms: torch.Tensor,
+    sort_members: bool,
+) -> None:
+    """Apply injected randomness (device int64 assign, device int32 perms) to a CUDA tensor."""
+    lib = load()
+    dev = data.device
+    assert assign.dtype == torch.int64 and assign.is_cuda and assign.is_contiguous()
+    assert perms.dtype == torch.int32 and perms.is_cuda and perms.is_contiguous()
+    offs = _i64_array(offsets_per_iter)
+    code = lib.povs_apply_v1(
+        ctypes.c_void_p(data.data_ptr()),
+        data.shape[0],
+        row_bytes,
+        pblock,
+        vblock,
+        len(offsets_per_iter),
+        offs,
+        ctypes.c_void_p(assign.data_ptr()),
+        ctypes.c_void_p(perms.data_ptr()),
+        1 if sort_members else 0,
+        dev.index,
+        ctypes.c_void_p(current_stream_handle(dev)),
+    )
+    check(code, "povs_apply_v1")
+
+
+def device_status(device: int) -> int:
+    """Read and clear the sticky device status word (synchronizes the device)."""
+    lib = load()
+    out = ctypes.c_int32(0)
+    check(lib.povs_device_status_v1(device, ctypes.byref(out)), "povs_device_status_v1")
+    return int(out.value)
+
+
+def set_tuning(stage_cap: int = 32 * 1024, n_stages: int = 2, max_warps: int = 16, force_plain: bool = False) -> None:
+    check(load().povs_set_tuning_v1(stage_cap, n_stages, max_warps, int(force_plain)), "povs_set_tuning_v1")
+
+
+PLAN_FIELDS = (
+    "grid",
+    "block",
+    "smem",
+    "sort_elems_per_lane",
+    "bulk",
+    "slab_bytes",
+    "n_slabs",
+    "stages_per_warp",
+    "stage_bytes",
+    "vec_bytes",
+    "n_vblocks",
+    "sm_count",
+)
+
+
+def describe_plan(data: torch.Tensor, row_bytes: int, pblock: int, vblock: int) -> dict[str, int]:
+    lib = load()
+    out = (ctypes.c_int64 * len(PLAN_FIELDS))()
+    n = lib.povs_describe_plan_v1(
+        ctypes.c_void_p(data.data_ptr()), data.shape[0], row_bytes, pblock, vblock, data.device.index, out, len(PLAN_FIELDS)
+    )
+    check(n, "povs_describe_plan_v1")
+    return {k: int(out[i]) for i, k in enumerate(PLAN_FIELDS[:n])}
+
+
+def release() -> None:
+    if _LIB is not None:
+        check(_LIB.povs_release_v1(), "povs_release_v1")

@@ -1,0 +1,102 @@
+"""POV shuffle for host data (NumPy arrays and CPU tensors).
+
+The reference runs a pseudo-parallel NumPy version of the algorithm on the CPU for these inputs
+(src/povs/numpy.py:18-61).  Here host data takes the same GPU path as CUDA tensors: the rows are
+copied to a device staging buffer, shuffled by the sm_100a kernels and copied back, in one native
+call (``povs_shuffle_host_v1``).  Option resolution and validation are the reference's NumPy
+rules (numpy.py:70-109): V defaults to 2, P to 16, offsets from ``choose_offsets``.
+A CUDA device is required; without one the call raises ``RuntimeError``.
+"""
+
+from __future__ import annotations
+
+import typing
+import warnings
+
+import numpy as np
+import torch
+
+from . import _native
+from .common import (
+    choose_offsets,
+    get_dtype_bytes,
+    get_instance_size,
+    povs_preflight,
+    purge_dependent_param,
+    seed_to_u64,
+)
+from .constants import DEFAULT_CPU_PBLOCK_SIZE, MIN_VBLOCK_SIZE
+from .types import Options
+
+
+def shuffle(data: np.ndarray, iterations: int, options: Options | None, seed: int, flags: int = 0) -> None:
+    """Shuffle a host array in place along axis 0 on the current CUDA device."""
+    options = typing.cast(
+        "_HostOptions",
+        options if options_is_complete(options) else optim_options_for_dataset(data, options),
+    )
+    preflight(data, iterations, options)
+    row_bytes = get_instance_size(data) * get_dtype_bytes(data)
+    if row_bytes == 0:
+        return
+    if not torch.cuda.is_available():
+        raise RuntimeError("povs requires a CUDA device (B200, sm_100a); none is available")
+
+    contiguous = data.flags.c_contiguous
+    host = data if contiguous else np.ascontiguousarray(data)
+    n_rows = host.shape[0]
+    device = torch.device("cuda", torch.cuda.current_device())
+    staging = torch.empty(n_rows * row_bytes, dtype=torch.uint8, device=device)
+    _native.shuffle_host(
+        host.ctypes.data,
+        staging,
+        n_rows,
+        row_bytes,
+        list(options.offsets),
+        iterations,
+        options.physical_block_size,
+        options.virtual_block_size,
+        seed_to_u64(seed),
+        flags,
+    )
+    if not contiguous:
+        data[...] = host
+
+
+class _HostOptions(Options):
+    virtual_block_size: int
+    physical_block_size: int
+    offsets: list[int]
+
+
+def options_is_complete(options: Options | None) -> bool:
+    return options is not None and None not in (
+        options.virtual_block_size,
+        options.physical_block_size,
+        options.offsets,
+    )
+
+
+def optim_options_for_dataset(data: np.ndarray, options: Options | None) -> Options:
+    """Complete the options for a host dataset."""
+    options = options or Options()
+    if options_is_complete(options):
+        warnings.warn("All parameters already specified, skipping optimization")
+        return options
+    if options.physical_block_size is None and options.offsets is not None:
+        purge_dependent_param(options, "physical_block_size", "offsets")
+    pblk = options.physical_block_size or DEFAULT_CPU_PBLOCK_SIZE
+    return Options(
+        virtual_block_size=options.virtual_block_size or MIN_VBLOCK_SIZE,
+        physical_block_size=pblk,
+        offsets=choose_offsets(
+            deck_size=data.shape[0],
+            instance_size=get_instance_size(data),
+            dtype_bytes=get_dtype_bytes(data),
+            pblock_size=pblk,
+        ),
+    )
+
+
+def preflight(data: np.ndarray, iterations: int, options: Options) -> None:
+    povs_preflight(data, iterations, options)

@@ -1,0 +1,109 @@
+"""CPU checks of the C-ABI library (loads, exports every declared symbol) and of the host-side
+API logic that runs before any device call."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+
+import numpy as np
+import pytest
+import torch
+
+import povs
+from povs import _build, _native
+
+HEADERS = sorted((_build.INCLUDE_DIR).glob("*.h"))
+
+
+def _declared_functions() -> set[str]:
+    names: set[str] = set()
+    for h in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names.update(re.findall(r"^[A-Za-z_][\w \*]*?\b(povs_\w+)\s*\(", text, flags=re.M))
+    return names
+
+
+def test_headers_declare_entry_points():
+    names = _declared_functions()
+    for required in ("povs_shuffle_v1", "povs_apply_v1", "povs_shuffle_host_v1", "povs_last_error_string"):
+        assert required in names
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = ctypes.CDLL(str(_build.LIB_PATH))
+    missing = [n for n in sorted(_declared_functions()) if not hasattr(lib, n)]
+    assert not missing, missing
+    assert set(_native.SIGNATURES) == _declared_functions()
+
+
+def test_library_is_built_for_sm100a():
+    params = povs.get_build_params()
+    assert params.cuda_arch == ["100a"]
+    assert params.cartesian_instancing is False
+
+
+def test_version_and_error_string_without_gpu():
+    lib = _native.load()
+    assert lib.povs_version() >= 100
+    assert isinstance(lib.povs_last_error_string(), bytes)
+
+
+def test_invalid_arguments_are_rejected_before_any_device_call():
+    lib = _native.load()
+    offs = (ctypes.c_int64 * 2)(0, 4)
+    # NULL data, too few rows, bad block sizes, out-of-range offsets: all host-side errors.
+    assert lib.povs_shuffle_v1(None, 64, 4, offs, 2, 1, 16, 2, 0, 0, None, 0) == -1
+    assert b"NULL" in lib.povs_last_error_string()
+    assert lib.povs_shuffle_v1(ctypes.c_void_p(16), 1, 4, offs, 2, 1, 16, 2, 0, 0, None, 0) == -1
+    assert lib.povs_shuffle_v1(ctypes.c_void_p(16), 64, 4, offs, 2, 1, 12, 2, 0, 0, None, 0) == -1
+    assert lib.povs_shuffle_v1(ctypes.c_void_p(16), 64, 4, offs, 2, 1, 16, 3, 0, 0, None, 0) == -1
+    assert lib.povs_shuffle_v1(ctypes.c_void_p(16), 64, 4, offs, 2, 1, 16, 64, 0, 0, None, 0) == -2
+    bad = (ctypes.c_int64 * 2)(0, 64)
+    assert lib.povs_shuffle_v1(ctypes.c_void_p(16), 64, 4, bad, 2, 1, 16, 2, 0, 0, None, 0) == -1
+    assert b"offset" in lib.povs_last_error_string()
+    many = (ctypes.c_int64 * 300)(*([0] * 300))
+    assert lib.povs_shuffle_v1(ctypes.c_void_p(16), 64, 4, many, 300, 1, 16, 2, 0, 0, None, 0) == -2
+
+
+def test_unsupported_container_raises_type_error():
+    with pytest.raises(TypeError):
+        povs.shuffle([1, 2, 3])
+    with pytest.raises(TypeError):
+        povs.optim_options_for_dataset([1, 2, 3])
+
+
+def test_host_options_match_reference_defaults():
+    deck = np.zeros((128, 2, 4), dtype=np.float32)
+    opts = povs.optim_options_for_dataset(deck)
+    assert opts.virtual_block_size == 2 and opts.physical_block_size == 16
+    assert opts.offsets == list(range(16))
+    cpu = torch.zeros(128, 8)
+    assert povs.optim_options_for_dataset(cpu) == povs.optim_options_for_dataset(cpu.numpy())
+
+
+@pytest.mark.parametrize(
+    "kwargs",
+    [
+        dict(iterations=0),
+        dict(options=povs.Options(virtual_block_size=3, physical_block_size=16, offsets=[0, 4])),
+        dict(options=povs.Options(virtual_block_size=2, physical_block_size=16, offsets=[0])),
+        dict(options=povs.Options(virtual_block_size=2, physical_block_size=16, offsets=[0, 16])),
+    ],
+)
+def test_host_preflight_errors(kwargs):
+    deck = np.zeros((64, 4), dtype=np.float32)
+    with pytest.raises(AssertionError):
+        povs.shuffle(deck, seed=1, **{"iterations": 1, **kwargs})
+
+
+def test_single_row_deck_rejected():
+    with pytest.raises(AssertionError):
+        povs.shuffle(np.zeros((1, 4), dtype=np.float32), options=povs.Options(2, 16, [0, 1]), seed=0)
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-GPU error path")
+def test_host_route_requires_a_gpu():
+    deck = np.arange(64 * 4, dtype=np.float32).reshape(64, 4)
+    with pytest.raises(RuntimeError, match="CUDA device"):
+        povs.shuffle(deck, seed=1)

@@ -1,0 +1,253 @@
+"""GPU parity: the CUDA library (called through its C ABI) against the oracle and the reference.
+
+* default mode (device randomness) == the oracle's restatement of it, byte for byte;
+* injected reference randomness (NumPy path, CUDA path) == the reference's output / the oracle;
+* full-size runs keep the multiset of rows (every row intact, each exactly once).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import povs
+from povs import _native
+from oracle import numpy_path
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+
+
+def random_rows(n_rows: int, row_bytes: int, seed: int) -> np.ndarray:
+    return np.random.default_rng(seed).integers(0, 256, size=(n_rows, row_bytes), dtype=np.uint8)
+
+
+def gpu_shuffle_bytes(host: np.ndarray, P: int, V: int, offsets: list[int], iterations: int, seed: int,
+                      flags: int = 0) -> np.ndarray:
+    dev = torch.from_numpy(host.copy()).to(DEV)
+    _native.shuffle_device(dev, host.shape[1], offsets, iterations, P, V, seed, flags)
+    torch.cuda.synchronize()
+    povs.check_device_status(0)
+    return dev.cpu().numpy()
+
+
+# (n_rows, row_bytes, P, V, offsets, iterations): bulk (TMA) and plain-load paths, ragged decks,
+# truncated last pblocks, padding slots, column slabs, every sort width.
+DEFAULT_CASES = [
+    (64, 16, 16, 2, [0, 4], 1),
+    (1000, 64, 8, 2, list(range(8)), 4),
+    (1000, 12, 16, 4, [0, 1, 3], 3),
+    (4099, 256, 32, 4, [0, 1, 2, 5], 2),
+    (5000, 3, 64, 2, [0, 2, 4], 2),
+    (777, 2, 16, 8, [0, 1, 2], 2),
+    (3000, 8, 128, 8, [0, 1, 5], 2),
+    (2048, 4096, 16, 2, [0, 1, 3], 2),
+    (1200, 12288, 16, 2, [0, 1, 2], 3),
+    (100_000, 128, 64, 4, list(range(16)), 4),
+    (2, 4, 8, 2, [0, 1], 3),
+    (4100, 20, 32, 16, [0, 1, 2], 2),
+    (70_000, 48, 32, 32, [0, 7, 9], 2),
+    (50_000, 32, 64, 8, [0, 3, 6, 11], 3),
+    (9999, 24, 16, 2, [0, 5], 2),
+    (1 << 16, 256, 8, 2, [0, 1], 1),
+]
+
+
+@pytest.mark.parametrize("n_rows,row_bytes,P,V,offsets,iterations", DEFAULT_CASES)
+@pytest.mark.parametrize("seed", [0, 2**40 + 17])
+def test_default_mode_matches_oracle(oracle_api, n_rows, row_bytes, P, V, offsets, iterations, seed):
+    host = random_rows(n_rows, row_bytes, seed=n_rows + row_bytes)
+    got = gpu_shuffle_bytes(host, P, V, offsets, iterations, seed)
+    want = host.copy()
+    oracle_api.shuffle(want, iterations, P, V, offsets, seed)
+    assert np.array_equal(got, want)
+
+
+def test_graph_and_direct_launches_agree(oracle_api):
+    host = random_rows(20_000, 64, seed=3)
+    a = gpu_shuffle_bytes(host, 16, 4, [0, 1, 2, 3], 5, seed=9)
+    b = gpu_shuffle_bytes(host, 16, 4, [0, 1, 2, 3], 5, seed=9, flags=_native.FLAG_NO_GRAPH)
+    assert np.array_equal(a, b)
+    c = gpu_shuffle_bytes(host, 16, 4, [0, 1, 2, 3], 5, seed=10)
+    assert not np.array_equal(a, c)
+
+
+def test_misaligned_deck_uses_plain_loads(oracle_api):
+    n_rows, row_bytes, P, V, offsets = 3000, 16, 16, 2, [0, 1, 2]
+    host = random_rows(n_rows, row_bytes, seed=5)
+    buf = torch.zeros(n_rows * row_bytes + 4, dtype=torch.uint8, device=DEV)
+    view = buf[4:].view(n_rows, row_bytes)
+    view.copy_(torch.from_numpy(host))
+    assert view.data_ptr() % 16 == 4
+    plan = _native.describe_plan(view, row_bytes, P, V)
+    assert plan["bulk"] == 0 and plan["vec_bytes"] == 4
+    _native.shuffle_device(view, row_bytes, offsets, 3, P, V, 77)
+    torch.cuda.synchronize()
+    want = host.copy()
+    oracle_api.shuffle(want, 3, P, V, offsets, 77)
+    assert np.array_equal(view.cpu().numpy(), want)
+
+
+def test_plans_cover_bulk_and_slab_paths():
+    t = torch.empty((1200, 12288), dtype=torch.uint8, device=DEV)
+    plan = _native.describe_plan(t, 12288, 16, 2)
+    assert plan["bulk"] == 1 and plan["n_slabs"] > 1
+    t2 = torch.empty((4096, 256), dtype=torch.uint8, device=DEV)
+    plan2 = _native.describe_plan(t2, 256, 32, 4)
+    assert plan2["bulk"] == 1 and plan2["n_slabs"] == 1
+
+
+def test_injected_numpy_path_matches_reference_golden(golden_numpy_path):
+    """Reference NumPy-path randomness injected into the kernels reproduces the reference's output."""
+    for case in golden_numpy_path:
+        offs, assign, perms = numpy_path.numpy_path_randomness(
+            case["seed"], case["n_rows"], case["P"], case["V"], case["offsets"], case["iterations"]
+        )
+        dev = torch.from_numpy(case["input"].copy()).to(DEV)
+        povs.apply_randomness(dev, offs, assign, perms, case["P"], case["V"], sort_members=False)
+        povs.check_device_status(0)
+        assert np.array_equal(dev.cpu().numpy(), case["output"]), case["name"]
+
+
+REFCUDA_CASES = [
+    (64, (4,), np.float32, 16, 2, [0], 1, 13),  # the reference's standalone program (povs.cu:477-520)
+    (128, (8,), np.float32, 16, 2, [4, 8], 3, 42),
+    (1000, (16,), np.int32, 8, 2, list(range(8)), 4, 0),
+    (1000, (5,), np.uint8, 16, 4, [0, 2, 6], 3, 1),  # truncated last pblock + padding
+    (4099, (64,), np.float32, 32, 4, [0, 1, 2, 5], 2, 7),
+    (20_000, (3, 16), np.float16, 64, 8, [0, 8, 16 + 3], 2, 999),
+]
+
+
+@pytest.mark.parametrize("n_rows,shape,dtype,P,V,offsets,iterations,seed", REFCUDA_CASES)
+def test_injected_refcuda_randomness_matches_oracle(oracle_api, n_rows, shape, dtype, P, V, offsets, iterations, seed):
+    rng = np.random.default_rng(seed + 100)
+    deck = (rng.standard_normal((n_rows, *shape)) * 50).astype(dtype)
+    offs, assign, perms = oracle_api.refcuda_randomness(seed, n_rows, P, V, offsets, iterations)
+    want = deck.copy()
+    for t in range(iterations):
+        oracle_api.apply_iteration(want, P, V, int(offs[t]), assign[t], perms[t], sort_members=True)
+    dev = torch.from_numpy(deck.copy()).to(DEV)
+    povs.apply_randomness(dev, offs, assign, perms, P, V, sort_members=True)
+    povs.check_device_status(0)
+    assert np.array_equal(dev.cpu().numpy(), want)
+
+
+def test_injected_out_of_range_permutation_is_reported():
+    n_rows, P, V = 256, 16, 2
+    dev = torch.arange(n_rows * 4, dtype=torch.float32, device=DEV).view(n_rows, 4)
+    n_p = n_rows // P
+    assign = np.arange(n_p, dtype=np.int64).reshape(1, n_p // V, V)
+    perms = np.tile(np.arange(V * P, dtype=np.int32), (1, n_p // V, 1))
+    perms[0, 3, 5] = 4000
+    povs.apply_randomness(dev, [0], assign, perms, P, V, validate=False)
+    with pytest.raises(RuntimeError, match="device status 0x2"):
+        povs.check_device_status(0)
+    povs.check_device_status(0)  # cleared by the read
+
+
+def _integrity(data: torch.Tensor, n_rows: int, k: int) -> None:
+    flat = data.reshape(n_rows, k)
+    ids = flat[:, 0].to(torch.int64) // k
+    assert torch.equal(torch.sort(ids).values, torch.arange(n_rows, device=data.device)), "deck integrity failed"
+    assert not torch.equal(ids, torch.arange(n_rows, device=data.device)), "deck was not shuffled"
+    expected = ids[:, None] * k + torch.arange(k, device=data.device)[None, :]
+    assert torch.equal(flat.to(torch.int64), expected), "instance integrity failed"
+
+
+_OPTS_SMALL = povs.Options(physical_block_size=16, virtual_block_size=2, offsets=[4, 8])
+
+
+@pytest.mark.parametrize("shape", [(8,), (2, 4), (2, 2, 2)])
+@pytest.mark.parametrize("iterations", [1, 3])
+@pytest.mark.parametrize("opts", [_OPTS_SMALL, None])
+@pytest.mark.parametrize("deck", [32, 128])
+def test_reference_integrity_cases_on_cuda(deck, shape, iterations, opts):
+    """The reference's end-to-end integrity test (src/tests/test_pov_shuffle.py:40-96) on CUDA tensors."""
+    k = int(np.prod(shape))
+    data = torch.arange(deck * k, dtype=torch.float32, device=DEV).reshape(deck, *shape)
+    options = povs.optim_options_for_dataset(data) if opts is None else opts
+    povs.shuffle(data, iterations=iterations, options=options, seed=42)
+    torch.cuda.synchronize()
+    _integrity(data, deck, k)
+
+
+@pytest.mark.parametrize("container", ["numpy", "cpu"])
+@pytest.mark.parametrize("shape", [(8,), (2, 4), (2, 2, 2)])
+@pytest.mark.parametrize("iterations", [1, 3])
+@pytest.mark.parametrize("opts", [_OPTS_SMALL, None])
+@pytest.mark.parametrize("deck", [32, 128])
+def test_reference_integrity_cases_host_data(deck, shape, iterations, opts, container):
+    """Host decks (NumPy arrays, CPU tensors) go through the GPU and come back shuffled in place."""
+    k = int(np.prod(shape))
+    flat = np.arange(deck * k, dtype=np.float32).reshape(deck, *shape)
+    data = flat if container == "numpy" else torch.from_numpy(flat)
+    options = povs.optim_options_for_dataset(data) if opts is None else opts
+    povs.shuffle(data, iterations=iterations, options=options, seed=42)
+    arr = flat
+    ids = arr.reshape(deck, k)[:, 0].astype(np.int64) // k
+    assert sorted(ids.tolist()) == list(range(deck))
+    assert ids.tolist() != list(range(deck))
+    assert np.array_equal(arr.reshape(deck, k), (ids[:, None] * k + np.arange(k)).astype(np.float32))
+
+
+def test_host_route_matches_device_route():
+    host = np.random.default_rng(1).standard_normal((5000, 24)).astype(np.float32)
+    opts = povs.Options(virtual_block_size=4, physical_block_size=16, offsets=[0, 1, 2, 3])
+    a = host.copy()
+    povs.shuffle(a, iterations=3, options=opts, seed=5)
+    dev = torch.from_numpy(host.copy()).to(DEV)
+    povs.shuffle(dev, iterations=3, options=opts._replace(gpu_thread_block_size=32), seed=5)
+    assert np.array_equal(a, dev.cpu().numpy())
+    nc = np.asfortranarray(host.copy())
+    povs.shuffle(nc, iterations=3, options=opts, seed=5)
+    assert np.array_equal(nc, a)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.uint8, torch.float16, torch.float64, torch.int16, torch.bool])
+def test_any_dtype_is_shuffled_as_bytes(dtype):
+    n_rows, k = 4096, 32
+    ids = torch.arange(n_rows, device=DEV)
+    data = (ids[:, None] % 2).to(dtype).repeat(1, k) if dtype == torch.bool else ids[:, None].repeat(1, k).to(dtype)
+    raw = data.view(torch.uint8).reshape(n_rows, -1).clone()
+    povs.shuffle(data, iterations=2, options=None, seed=3)
+    torch.cuda.synchronize()
+    got = data.view(torch.uint8).reshape(n_rows, -1)
+    # Every row survives intact: compare the sorted multisets of rows.
+    key = lambda x: torch.unique(x, dim=0, return_counts=True)  # noqa: E731
+    a, ca = key(raw)
+    b, cb = key(got)
+    assert torch.equal(a, b) and torch.equal(ca, cb)
+
+
+def test_full_size_cfg1_matches_oracle(oracle_api):
+    """1,048,576 x 128 fp16 (256 MiB), 4 iterations, V=2, P=64, auto offsets: bit-exact with the oracle."""
+    rng = np.random.default_rng(0)
+    deck = rng.standard_normal((1_048_576, 128)).astype(np.float16)
+    offsets = povs.common.choose_offsets(1_048_576, 128, 2, 64)
+    dev = torch.from_numpy(deck).to(DEV)
+    povs.shuffle(dev, iterations=4, options=povs.Options(2, 64, offsets, 64), seed=0)
+    want = deck.copy()
+    oracle_api.shuffle(want, 4, 64, 2, offsets, 0)
+    assert np.array_equal(dev.cpu().numpy(), want)
+
+
+def test_full_size_cfg3_keeps_every_row():
+    """134,217,728 x 128 bf16 (32 GiB), 4 iterations, V=4, P=32: every row intact, each exactly once."""
+    n_rows, k = 134_217_728, 128
+    data = torch.empty((n_rows, k), dtype=torch.bfloat16, device=DEV)
+    words = data.view(torch.int64)  # 32 int64 per row
+    ids = torch.arange(n_rows, device=DEV, dtype=torch.int64)
+    words.copy_((ids[:, None] * 1_000_003 + torch.arange(32, device=DEV)[None, :]))
+    offsets = povs.common.choose_offsets(n_rows, k, 2, 32)
+    povs.shuffle(data, iterations=4, options=povs.Options(4, 32, offsets, 64), seed=1)
+    torch.cuda.synchronize()
+    povs.check_device_status(0)
+    got_ids = torch.div(words[:, 0], 1_000_003, rounding_mode="floor")
+    assert torch.equal(words - got_ids[:, None] * 1_000_003, torch.arange(32, device=DEV).expand(n_rows, 32))
+    del words
+    assert torch.equal(torch.sort(got_ids).values, ids)
+    moved = (got_ids != ids).float().mean().item()
+    assert moved > 0.99
