@@ -189,6 +189,7 @@ def run_ours(args, w: dict, wname: str) -> None:
 
     sampler = ClockSampler(local)
     sampler.start()
+    time.sleep(0.5)  # let nvidia-smi start sampling before the timed region
     barrier()
     torch.cuda.synchronize(device)
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -385,7 +386,7 @@ def run_reference(args, w: dict, wname: str) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="bf16_32GiB", choices=sorted(WORKLOADS))
@@ -393,10 +394,14 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--rows", type=int, default=None, help="override the workload's row count (profiling captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
-    w = WORKLOADS[args.workload]
+    w = dict(WORKLOADS[args.workload])
+    if args.rows:
+        w["desc"] = w["desc"] + f" [rows overridden: {args.rows:,}]"
+        w["rows"] = args.rows
     if args.impl == "reference":
         run_reference(args, w, args.workload)
     else:

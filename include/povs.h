@@ -113,18 +113,22 @@ int32_t povs_version(void);
 /*
  * Advanced: process-wide launch tuning (no reference counterpart; the reference
  * fixes these at compile time through template parameters, povs.cu:116,433-436).
- *   stage_cap   max bytes of one shared-memory stage; vblocks whose V*P rows exceed it are
- *               processed in column slabs (default 32768)
- *   n_stages    stages per warp, 2..8 (default 2)
- *   max_warps   warps per CTA, 1..16 (default 16)
+ *   stage_cap   max bytes of one shared-memory data stage; vblocks whose V*P rows exceed it
+ *               are processed in column slabs (default 32768)
+ *   n_stages    max data stages in a CTA's ring, 2..16 (default 8; fewer when shared memory is short)
+ *   movers      warps per CTA that copy rows (default 4)
+ *   permuters   warps per CTA that compute members and permutations (default 4); movers + permuters <= 16
  *   force_plain 1 = plain vector loads instead of TMA bulk copies
+ *   copy_bytes  target bytes of one bulk copy when whole rows are staged (default 8192)
  */
-int povs_set_tuning_v1(int32_t stage_cap, int32_t n_stages, int32_t max_warps, int32_t force_plain);
+int povs_set_tuning_v1(int32_t stage_cap, int32_t n_stages, int32_t movers, int32_t permuters, int32_t force_plain,
+                       int32_t copy_bytes);
 
 /*
  * Advanced: report the launch plan povs_shuffle_v1 would use, as int64 values
  * {grid, block, dynamic smem, sort elements per lane, bulk (0/1), slab bytes, slabs,
- *  stages per warp, stage bytes, vector bytes, vblocks, SM count}; returns how many were written.
+ *  stages per CTA, stage bytes, vector bytes, vblocks, SM count, rows per bulk copy,
+ *  permutation slots, mover warps, permuter warps}; returns how many were written.
  */
 int povs_describe_plan_v1(void* data, int64_t n_rows, int64_t row_bytes, int32_t pblock, int32_t vblock,
                           int32_t device, int64_t* out, int32_t n_out);

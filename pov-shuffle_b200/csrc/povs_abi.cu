@@ -81,9 +81,11 @@ KernelFn select_kernel(int epl, bool injected, bool bulk)
 
 struct Tuning {
     int stage_cap = 32 * 1024; // max bytes of one stage; larger vblocks are split into column slabs
-    int n_stages = 2;          // stages per warp
-    int max_warps = 16;        // warps per CTA
+    int n_stages = 8;          // max shared-memory data stages per CTA
+    int movers = 4;            // warps that copy rows
+    int permuters = 4;         // warps that compute members and permutations
     int force_plain = 0;       // 1 = never use TMA bulk loads
+    int copy_bytes = 8192;     // target bytes per bulk copy on the whole-row path
 };
 Tuning g_tuning;
 std::mutex g_tuning_mu;
@@ -227,35 +229,45 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out)
         const int64_t gran = fit >= 128 ? 128 : vec;
         slab = std::max<int64_t>(vec, (fit / gran) * gran);
     }
-    int nst = std::max(2, std::min(t.n_stages, 8));
-    int64_t stage_bytes = ((vp * slab + 127) / 128) * 128;
-    int warp_bytes = povs::warp_smem_bytes(nst, static_cast<int>(stage_bytes), static_cast<int>(vp));
-    // Shrink the slab until at least one warp fits.
-    while (warp_bytes > c.smem_optin && slab > vec) {
+    const int max_stages = std::max(2, std::min(t.n_stages, povs::MAX_STAGES));
+    const int movers = std::max(1, std::min(t.movers, 15));
+    const int permuters = std::max(1, std::min(t.permuters, 16 - movers));
+    // Permutation slots: the stages' worth plus room for every permuter to work ahead.
+    auto slots_for = [&](int stages) { return std::min(povs::MAX_SLOTS, stages + 2 * permuters); };
+    auto stages_for = [&](int64_t sl, int64_t& stage_bytes) {
+        stage_bytes = ((vp * sl + 127) / 128) * 128;
+        const int kp = slots_for(max_stages);
+        const int64_t fixed = povs::cta_smem_bytes(0, 0, kp, static_cast<int>(vp));
+        const int64_t per_stage = stage_bytes + 16;
+        return static_cast<int>(std::min<int64_t>(max_stages, (c.smem_optin - fixed) / per_stage));
+    };
+    int64_t stage_bytes = 0;
+    int nst = stages_for(slab, stage_bytes);
+    // Shrink the slab until at least two stages fit.
+    while (nst < 2 && slab > vec) {
         slab = std::max<int64_t>(vec, ((slab / 2) / vec) * vec);
-        stage_bytes = ((vp * slab + 127) / 128) * 128;
-        warp_bytes = povs::warp_smem_bytes(nst, static_cast<int>(stage_bytes), static_cast<int>(vp));
+        nst = stages_for(slab, stage_bytes);
     }
-    if (warp_bytes > c.smem_optin)
+    if (nst < 2)
         return fail(POVS_ERR_UNSUPPORTED, "a vblock of %lld rows does not fit shared memory", static_cast<long long>(vp));
+    const int kp = slots_for(nst);
 
-    int warps = std::min<int64_t>(std::max(1, t.max_warps), c.smem_optin / warp_bytes);
-    warps = std::max(1, std::min(warps, 16));
-    // No more warps than vblocks.
-    if (p.n_vblocks < warps) warps = static_cast<int>(p.n_vblocks);
-    const int cta_smem = warps * warp_bytes;
+    const int warps = movers + permuters;
+    const int cta_smem = povs::cta_smem_bytes(nst, static_cast<int>(stage_bytes), kp, static_cast<int>(vp));
     const int per_sm_by_smem = std::max(1, c.smem_per_sm / (cta_smem + 1024));
     const int per_sm_by_threads = std::max(1, c.max_threads_per_sm / (warps * 32));
     const int ctas_per_sm = std::min(per_sm_by_smem, per_sm_by_threads);
-    const int64_t want = (p.n_vblocks + warps - 1) / warps;
-    const int grid = static_cast<int>(std::min<int64_t>(want, static_cast<int64_t>(c.sm_count) * ctas_per_sm));
+    const int grid = static_cast<int>(std::min<int64_t>(p.n_vblocks, static_cast<int64_t>(c.sm_count) * ctas_per_sm));
 
     p.slab_bytes = static_cast<int32_t>(slab);
     p.n_slabs = static_cast<int32_t>((p.row_bytes + slab - 1) / slab);
     p.stage_bytes = static_cast<int32_t>(stage_bytes);
     p.n_stages = nst;
-    p.warp_bytes = warp_bytes;
     p.vec_bytes = vec;
+    p.copy_rows = static_cast<int32_t>(std::max<int64_t>(1, std::min<int64_t>(p.pblock, t.copy_bytes / p.row_bytes)));
+    p.n_slots = kp;
+    p.n_movers = movers;
+    p.n_permuters = permuters;
 
     out.fn = select_kernel(epl, injected, bulk);
     out.grid = std::max(1, grid);
@@ -543,15 +555,19 @@ extern "C" const char* povs_last_error_string(void) { return g_err; }
 extern "C" int32_t povs_version(void) { return 100; }
 
 // Tuning and introspection.
-extern "C" int povs_set_tuning_v1(int32_t stage_cap, int32_t n_stages, int32_t max_warps, int32_t force_plain)
+extern "C" int povs_set_tuning_v1(int32_t stage_cap, int32_t n_stages, int32_t movers, int32_t permuters,
+                                  int32_t force_plain, int32_t copy_bytes)
 {
     g_err[0] = '\0';
-    if (stage_cap < 1024 || n_stages < 2 || n_stages > 8 || max_warps < 1 || max_warps > 16)
+    if (stage_cap < 1024 || n_stages < 2 || n_stages > povs::MAX_STAGES || movers < 1 || permuters < 1 ||
+        movers + permuters > 16 || copy_bytes < 16)
         return fail(POVS_ERR_INVALID_ARGUMENT, "tuning out of range");
     std::lock_guard<std::mutex> lk(g_tuning_mu);
     g_tuning.stage_cap = stage_cap;
     g_tuning.n_stages = n_stages;
-    g_tuning.max_warps = max_warps;
+    g_tuning.movers = movers;
+    g_tuning.permuters = permuters;
+    g_tuning.copy_bytes = copy_bytes;
     g_tuning.force_plain = force_plain ? 1 : 0;
     return POVS_OK;
 }
@@ -573,8 +589,10 @@ extern "C" int povs_describe_plan_v1(void* data, int64_t n_rows, int64_t row_byt
     Plan pl;
     r = plan_launch(p, *c, false, pl);
     if (r != POVS_OK) return r;
-    const int64_t vals[] = {pl.grid, pl.block, pl.smem, pl.epl, pl.bulk ? 1 : 0, p.slab_bytes, p.n_slabs,
-                            p.n_stages, p.stage_bytes, p.vec_bytes, p.n_vblocks, c->sm_count};
+    const int64_t vals[] = {pl.grid,      pl.block,       pl.smem,        pl.epl,      pl.bulk ? 1 : 0,
+                            p.slab_bytes, p.n_slabs,      p.n_stages,     p.stage_bytes, p.vec_bytes,
+                            p.n_vblocks,  c->sm_count,    p.copy_rows,    p.n_slots,     p.n_movers,
+                            p.n_permuters};
     const int n = std::min<int>(n_out, static_cast<int>(sizeof(vals) / sizeof(vals[0])));
     for (int i = 0; i < n; ++i) out[i] = vals[i];
     return n;

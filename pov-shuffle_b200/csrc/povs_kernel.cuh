@@ -9,23 +9,30 @@
 //   * slot f = r*P + i is row i of the r-th member; after the iteration
 //     slot f holds what slot perm[f] held before (povs.cu:325-348).
 //
-// B200 design.  The kernel is persistent and every warp is an independent
-// worker with its own ring of shared-memory stages.  For a work unit (one
-// vblock, or one column slab of one vblock when V*P rows do not fit a stage)
-// the warp
-//   1. computes the member pblocks (device Feistel bijection, or the injected
-//      assignment), orders them and derives each member's storage run;
-//   2. issues cp.async.bulk (TMA, non-multicast, local HBM only) copies of the
-//      <= 2 wrapped runs per member into the stage, completing on an mbarrier;
-//   3. builds the permutation of the unit's rows with a register bitonic sort
-//      of Philox keys over warp shuffles (or copies the injected one);
-//   4. once the stage's mbarrier flips, writes every destination row from
-//      shared memory with 16-byte vector stores, lanes covering consecutive
-//      bytes of consecutive destination rows (full 128-byte lines).
-// Steps 1-3 of unit j+NST-1 overlap the loads in flight for units j..j+NST-2.
+// B200 design (warp-specialized persistent CTA).
+//   * Permuter warps compute, for each unit (a vblock, or one column slab of a
+//     vblock whose V*P rows do not fit a stage), the member pblocks (device
+//     Feistel bijection, or the injected assignment), their order and storage
+//     runs, and the permutation (register bitonic sort of Philox keys over warp
+//     shuffles, or the injected one) into a ring of KP small slots, running up
+//     to KP units ahead (mbarriers pfull / pempty).
+//   * Mover warps own a ring of NST shared-memory data stages.  Unit u is issued
+//     by mover u % n_movers: it waits for its permutation slot and for every
+//     mover to have read the stage's previous unit (mbarrier `empty`), then
+//     starts cp.async.bulk copies (TMA, non-multicast, local HBM only) of the
+//     <= 2 wrapped runs per member into the stage, completing on `full`.
+//     Every mover then takes its share of every unit: it waits for `full` and
+//     writes its destination rows from shared memory with 16-byte vector stores
+//     (lanes cover consecutive bytes of consecutive destination rows, so each
+//     warp store is 4 full 128-byte lines), and arrives on `empty` and `pempty`.
+//     Issuing runs NST-1 units ahead, so NST-1 stages are normally loading while
+//     one is being written.
 // Rows whose size is not a multiple of 16 bytes (or decks that are not 16-byte
-// aligned) take the same pipeline with plain vector loads of the widest
-// aligned width instead of TMA.
+// aligned) take the same pipeline with plain vector loads by the issuing mover.
+//
+// Every wait is bounded (WAIT_LIMIT_NS); a wait that gives up records
+// DEV_ERR_WAIT_TIMEOUT in the status word, waits once more (bounded) for the
+// copies this warp started, and the warp returns.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -37,6 +44,8 @@ namespace povs {
 
 constexpr int MAX_INLINE_OFFSETS = 256;
 constexpr int MAX_VBLOCK = 32;
+constexpr int MAX_STAGES = 16;
+constexpr int MAX_SLOTS = 32;
 constexpr unsigned FULL_MASK = 0xffffffffu;
 
 // Device status bits (sticky, OR-ed into the per-device status word).
@@ -45,7 +54,7 @@ enum : int {
     DEV_ERR_BAD_INJECTED = 2, // an injected permutation entry was out of range (identity used instead)
 };
 
-constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull; // 2 s: far beyond any legitimate copy
+constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull; // 2 s: far beyond any legitimate wait
 
 struct IterParams {
     uint8_t* data;
@@ -55,14 +64,17 @@ struct IterParams {
     int64_t n_vblocks; // ceil(n_pblocks / V)
     int32_t pblock;    // P, power of two
     int32_t pblock_shift;
-    int32_t vblock; // V, power of two <= MAX_VBLOCK
-    int32_t vp;     // V * P
+    int32_t vblock;     // V, power of two <= MAX_VBLOCK
+    int32_t vp;         // V * P
     int32_t slab_bytes; // S: bytes of each row staged per unit (== R when rows fit)
     int32_t n_slabs;    // ceil(R / S)
-    int32_t stage_bytes;   // bytes of one data stage (>= vp * S, 128-aligned)
-    int32_t n_stages;      // NST
-    int32_t warp_bytes;    // bytes of shared memory owned by one warp
-    int32_t vec_bytes;     // chunk width of the plain-load path (1, 2, 4, 8 or 16)
+    int32_t stage_bytes; // bytes of one data stage (>= vp * S, 128-aligned)
+    int32_t n_stages;    // NST
+    int32_t vec_bytes;   // chunk width of the plain-load path (1, 2, 4, 8 or 16)
+    int32_t copy_rows;   // whole-row path: rows per bulk copy (runs are split into pieces this long)
+    int32_t n_slots;     // KP: permutation slots in the CTA's permutation ring
+    int32_t n_movers;    // warps that issue copies and write rows
+    int32_t n_permuters; // warps that compute members and permutations
     uint32_t iteration;
     uint64_t seed;
     int32_t n_offsets;
@@ -94,10 +106,15 @@ __device__ __forceinline__ void mbar_fence_init()
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes)
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes)
 {
-    asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
                  : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar)
+{
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
@@ -108,6 +125,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
                  "selp.u32 %0, 1, 0, p;\n\t}"
                  : "=r"(ok)
                  : "r"(smem_addr(bar)), "r"(parity)
+                 : "memory");
+    return ok != 0;
+}
+
+// Same, but the thread may sleep up to `hint_ns` waiting for the phase instead of returning at once.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns)
+{
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok)
+                 : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
                  : "memory");
     return ok != 0;
 }
@@ -132,14 +162,15 @@ __device__ __forceinline__ unsigned long long global_timer_ns()
     return t;
 }
 
-// Warp-uniform bounded wait on one phase of a stage barrier.  Returns false (and
-// records DEV_ERR_WAIT_TIMEOUT) if the phase did not complete within the limit.
-__device__ __forceinline__ bool warp_wait_stage(uint64_t* bar, uint32_t parity, int* status)
+// Warp-uniform bounded wait on one phase of a barrier.  Returns false (and records
+// DEV_ERR_WAIT_TIMEOUT) if the phase did not complete within the limit.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* status)
 {
     if (__all_sync(FULL_MASK, mbar_try_wait(bar, parity))) return true;
     const unsigned long long t0 = global_timer_ns();
     while (true) {
-        if (__all_sync(FULL_MASK, mbar_try_wait(bar, parity))) return true;
+        // Sleeping waits leave the issue slots to the warps that have work.
+        if (__all_sync(FULL_MASK, mbar_try_wait_sleep(bar, parity, 20000u))) return true;
         const unsigned long long dt = __shfl_sync(FULL_MASK, global_timer_ns() - t0, 0);
         if (dt > WAIT_LIMIT_NS) {
             if ((threadIdx.x & 31) == 0) atomicOr(status, DEV_ERR_WAIT_TIMEOUT);
@@ -149,44 +180,60 @@ __device__ __forceinline__ bool warp_wait_stage(uint64_t* bar, uint32_t parity, 
 }
 
 // ---------------------------------------------------------------------------------------------
-// Register bitonic sort over one warp: n = 32 * EPL 64-bit values, lane l owns
-// elements l*EPL .. l*EPL+EPL-1.  Ascending.
+// Register bitonic sort over one warp: n = 32 * EPL 64-bit values, lane l owns elements
+// l*EPL .. l*EPL+EPL-1.  Ascending.  For distances j >= EPL the partner is in lane l ^ (j/EPL)
+// at the same register; the direction bits of the element index then depend on the lane only.
 // ---------------------------------------------------------------------------------------------
+
+// Compare-exchange of registers r and r|j inside one lane (ascending when `up`).
+template <int EPL>
+__device__ __forceinline__ void cx_regs(uint64_t (&x)[EPL], int r, int j, bool up)
+{
+    const uint64_t a = x[r], b = x[r | j];
+    const bool swap = up ? (a > b) : (a < b);
+    x[r] = swap ? b : a;
+    x[r | j] = swap ? a : b;
+}
 
 template <int EPL>
 __device__ __forceinline__ void warp_bitonic_sort(uint64_t (&x)[EPL], int lane)
 {
-    constexpr int N = 32 * EPL;
+    const int base = lane * EPL; // element index of register 0 (its low log2(EPL) bits are zero)
+    // Phases k = 2 .. EPL sort within each lane's registers (compile-time network).
 #pragma unroll
-    for (int k = 2; k <= N; k <<= 1) {
+    for (int k = 2; k <= EPL; k <<= 1) {
 #pragma unroll
         for (int j = k >> 1; j > 0; j >>= 1) {
-            if (j >= EPL) {
-                const int lm = j / EPL;
 #pragma unroll
-                for (int r = 0; r < EPL; ++r) {
-                    const uint64_t y = __shfl_xor_sync(FULL_MASK, x[r], lm);
-                    const int e = lane * EPL + r;
-                    const bool up = (e & k) == 0;
-                    const bool lower = (e & j) == 0;
-                    const bool take_min = (lower == up);
-                    const uint64_t lo = x[r] < y ? x[r] : y;
-                    const uint64_t hi = x[r] < y ? y : x[r];
-                    x[r] = take_min ? lo : hi;
-                }
-            } else {
-#pragma unroll
-                for (int r = 0; r < EPL; ++r) {
-                    if ((r & j) == 0) {
-                        const int e = lane * EPL + r;
-                        const bool up = (e & k) == 0;
-                        const uint64_t a = x[r], b = x[r | j];
-                        const bool swap = up ? (a > b) : (a < b);
-                        x[r] = swap ? b : a;
-                        x[r | j] = swap ? a : b;
-                    }
+            for (int r = 0; r < EPL; ++r) {
+                if ((r & j) == 0) {
+                    const bool up = (k == EPL) ? ((base & k) == 0) : ((r & k) == 0);
+                    cx_regs<EPL>(x, r, j, up);
                 }
             }
+        }
+    }
+    // Phases k = 2*EPL .. 32*EPL: a runtime loop, so the code stays small for large EPL.  Distances
+    // j >= EPL pair register r with the same register of lane ^ (j / EPL); the sort direction and
+    // the side of the pair then depend on the lane only.  Distances j < EPL stay inside the lane.
+#pragma unroll 1
+    for (int k = 2 * EPL; k <= 32 * EPL; k <<= 1) {
+        const bool up = (base & k) == 0;
+#pragma unroll 1
+        for (int j = k >> 1; j >= EPL; j >>= 1) {
+            const bool keep_min = ((base & j) == 0) == up;
+            const int lm = j / EPL;
+#pragma unroll
+            for (int r = 0; r < EPL; ++r) {
+                const uint64_t y = __shfl_xor_sync(FULL_MASK, x[r], lm);
+                x[r] = ((x[r] < y) == keep_min) ? x[r] : y;
+            }
+        }
+#pragma unroll
+        for (int j = EPL >> 1; j > 0; j >>= 1) {
+#pragma unroll
+            for (int r = 0; r < EPL; ++r)
+                if ((r & j) == 0) cx_regs<EPL>(x, r, j, up);
         }
     }
 }
@@ -206,7 +253,8 @@ __device__ __forceinline__ void warp_make_perm(const IterParams& p, uint64_t vbl
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
                 const uint32_t e = quad * 4u + t;
-                x[4 * q + t] = (static_cast<int>(e) < n_valid) ? ((static_cast<uint64_t>(w[t]) << 32) | e) : ~uint64_t{0};
+                x[4 * q + t] =
+                    (static_cast<int>(e) < n_valid) ? ((static_cast<uint64_t>(w[t]) << 32) | e) : ~uint64_t{0};
             }
         }
     } else {
@@ -215,8 +263,9 @@ __device__ __forceinline__ void warp_make_perm(const IterParams& p, uint64_t vbl
 #pragma unroll
         for (int r = 0; r < EPL; ++r) {
             const uint32_t e = e0 + r;
-            x[r] = (static_cast<int>(e) < n_valid) ? ((static_cast<uint64_t>(pick_word(k, static_cast<int>(e & 3u))) << 32) | e)
-                                                   : ~uint64_t{0};
+            x[r] = (static_cast<int>(e) < n_valid)
+                       ? ((static_cast<uint64_t>(pick_word(k, static_cast<int>(e & 3u))) << 32) | e)
+                       : ~uint64_t{0};
         }
     }
     warp_bitonic_sort<EPL>(x, lane);
@@ -228,7 +277,9 @@ __device__ __forceinline__ void warp_make_perm(const IterParams& p, uint64_t vbl
 }
 
 // ---------------------------------------------------------------------------------------------
-// Per-warp shared-memory layout.
+// CTA shared-memory layout:
+//   [NST data stages][KP permutations][KP metas][NST full][NST empty][KP pfull][KP pempty]
+// Data stage u % NST and permutation slot u % KP belong to unit u.
 // ---------------------------------------------------------------------------------------------
 
 struct StageMeta {
@@ -237,37 +288,44 @@ struct StageMeta {
     int32_t pad;
 };
 
-struct WarpSmem {
-    uint8_t* data;     // n_stages * stage_bytes
-    uint16_t* perm;    // n_stages * vp
-    StageMeta* meta;   // n_stages
-    uint64_t* bars;    // n_stages
-};
+__host__ __device__ inline int perm_bytes_per_slot(int vp) { return ((vp * 2 + 15) / 16) * 16; }
 
-__host__ __device__ inline int perm_bytes_per_stage(int vp) { return ((vp * 2 + 15) / 16) * 16; }
-
-__host__ __device__ inline int warp_smem_bytes(int n_stages, int stage_bytes, int vp)
+__host__ __device__ inline int cta_smem_bytes(int n_stages, int stage_bytes, int n_slots, int vp)
 {
-    const int bytes = n_stages * stage_bytes + n_stages * perm_bytes_per_stage(vp) +
-                      n_stages * static_cast<int>(sizeof(StageMeta)) + n_stages * 8;
-    return ((bytes + 127) / 128) * 128;
+    return n_stages * stage_bytes + n_slots * (perm_bytes_per_slot(vp) + static_cast<int>(sizeof(StageMeta))) +
+           (2 * n_stages + 2 * n_slots) * 8;
 }
 
-__device__ __forceinline__ WarpSmem carve_warp_smem(uint8_t* base, const IterParams& p)
+struct CtaSmem {
+    uint8_t* data;
+    uint16_t* perm;
+    StageMeta* meta;
+    uint64_t* full;   // data stage loaded (TMA bytes + issuer arrivals)
+    uint64_t* empty;  // data stage read by every mover thread
+    uint64_t* pfull;  // permutation slot written by its permuter warp
+    uint64_t* pempty; // permutation slot read by every mover thread
+    int perm_stride;  // uint16 entries per slot
+};
+
+__device__ __forceinline__ CtaSmem carve_smem(uint8_t* base, const IterParams& p)
 {
-    WarpSmem w;
-    w.data = base;
+    CtaSmem s;
+    s.data = base;
     uint8_t* q = base + static_cast<size_t>(p.n_stages) * p.stage_bytes;
-    w.perm = reinterpret_cast<uint16_t*>(q);
-    q += static_cast<size_t>(p.n_stages) * perm_bytes_per_stage(p.vp);
-    w.meta = reinterpret_cast<StageMeta*>(q);
-    q += static_cast<size_t>(p.n_stages) * sizeof(StageMeta);
-    w.bars = reinterpret_cast<uint64_t*>(q);
-    return w;
+    s.perm = reinterpret_cast<uint16_t*>(q);
+    s.perm_stride = perm_bytes_per_slot(p.vp) / 2;
+    q += static_cast<size_t>(p.n_slots) * perm_bytes_per_slot(p.vp);
+    s.meta = reinterpret_cast<StageMeta*>(q);
+    q += static_cast<size_t>(p.n_slots) * sizeof(StageMeta);
+    s.full = reinterpret_cast<uint64_t*>(q);
+    s.empty = s.full + p.n_stages;
+    s.pfull = s.empty + p.n_stages;
+    s.pempty = s.pfull + p.n_slots;
+    return s;
 }
 
 // ---------------------------------------------------------------------------------------------
-// Vector chunk copies of the plain-load path.
+// Vector chunks.
 // ---------------------------------------------------------------------------------------------
 
 template <int W>
@@ -296,19 +354,17 @@ struct VecOf<1> {
 __device__ __forceinline__ int64_t slot_row(const StageMeta& m, int f, int pshift, int pmask, int64_t n_rows)
 {
     int64_t row = m.start[f >> pshift] + (f & pmask);
-    if (row >= n_rows) row -= n_rows;
-    return row;
+    return row >= n_rows ? row - n_rows : row;
 }
 
-// Identity-order copy global -> stage of the unit's valid rows (plain loads).
+// Identity-order copy global -> stage of the unit's valid rows by one warp (plain loads).
 template <int W>
-__device__ __forceinline__ void lsu_load_unit(const IterParams& p, const StageMeta& m, uint8_t* stage, int slab,
+__device__ __forceinline__ void lsu_load_unit(const IterParams& p, const StageMeta& m, uint8_t* stage, int64_t col,
                                               int slen, int lane)
 {
     using T = typename VecOf<W>::T;
     const int cpr = slen / W;
     const int pmask = p.pblock - 1;
-    const int64_t col = static_cast<int64_t>(slab) * p.slab_bytes;
     const int n_valid = m.n_valid;
     if (cpr >= 32) {
         for (int f = 0; f < n_valid; ++f) {
@@ -321,6 +377,7 @@ __device__ __forceinline__ void lsu_load_unit(const IterParams& p, const StageMe
         const int g = 32 / cpr;
         const int lrow = lane / cpr, lq = lane - lrow * cpr;
         if (lrow < g) {
+#pragma unroll 4
             for (int f = lrow; f < n_valid; f += g) {
                 const int64_t row = slot_row(m, f, p.pblock_shift, pmask, p.n_rows);
                 const T* src = reinterpret_cast<const T*>(p.data + row * p.row_bytes + col);
@@ -331,56 +388,59 @@ __device__ __forceinline__ void lsu_load_unit(const IterParams& p, const StageMe
     }
 }
 
-// Permuted copy stage -> global: destination slot f receives source slot perm[f].
+// This warp's share of the permuted copy stage -> global: destination slot f receives source
+// slot perm[f].  Work items are interleaved over the W warps of the CTA.
 template <int W>
-__device__ __forceinline__ void store_unit(const IterParams& p, const StageMeta& m, const uint8_t* stage,
-                                           const uint16_t* perm, int slab, int slen, int lane)
+__device__ __forceinline__ void store_share(const IterParams& p, const StageMeta& m, const uint8_t* stage,
+                                            const uint16_t* perm, int64_t col, int slen, int lane, int warp,
+                                            int n_warps)
 {
     using T = typename VecOf<W>::T;
     const int cpr = slen / W;
     const int pmask = p.pblock - 1;
-    const int64_t col = static_cast<int64_t>(slab) * p.slab_bytes;
     const int n_valid = m.n_valid;
+    uint8_t* const data = p.data + col;
     if (cpr >= 32) {
-        for (int f = 0; f < n_valid; ++f) {
+        for (int f = warp; f < n_valid; f += n_warps) {
             const int64_t row = slot_row(m, f, p.pblock_shift, pmask, p.n_rows);
             const T* src = reinterpret_cast<const T*>(stage + static_cast<size_t>(perm[f]) * p.slab_bytes);
-            T* dst = reinterpret_cast<T*>(p.data + row * p.row_bytes + col);
+            T* dst = reinterpret_cast<T*>(data + row * p.row_bytes);
 #pragma unroll 4
             for (int q = lane; q < cpr; q += 32) dst[q] = src[q];
         }
     } else {
         const int g = 32 / cpr;
         const int lrow = lane / cpr, lq = lane - lrow * cpr;
-        if (lrow < g) {
-            constexpr int U = 4;
-            int f = lrow;
-            for (; f + (U - 1) * g < n_valid; f += U * g) {
-                T v[U];
-                int64_t rows[U];
+        if (lrow >= g) return;
+        const int n_pass = (n_valid + g - 1) / g;
+        constexpr int U = 4;
+        int t = warp;
+        for (; t + (U - 1) * n_warps < n_pass; t += U * n_warps) {
+            T v[U];
+            T* dst[U];
+            bool ok[U];
 #pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    const int fu = f + u * g;
-                    rows[u] = slot_row(m, fu, p.pblock_shift, pmask, p.n_rows);
-                    v[u] = reinterpret_cast<const T*>(stage + static_cast<size_t>(perm[fu]) * p.slab_bytes)[lq];
-                }
-#pragma unroll
-                for (int u = 0; u < U; ++u) reinterpret_cast<T*>(p.data + rows[u] * p.row_bytes + col)[lq] = v[u];
+            for (int u = 0; u < U; ++u) {
+                const int f = (t + u * n_warps) * g + lrow;
+                ok[u] = f < n_valid;
+                const int fs = ok[u] ? f : 0;
+                const int64_t row = slot_row(m, fs, p.pblock_shift, pmask, p.n_rows);
+                dst[u] = reinterpret_cast<T*>(data + row * p.row_bytes) + lq;
+                v[u] = reinterpret_cast<const T*>(stage + static_cast<size_t>(perm[fs]) * p.slab_bytes)[lq];
             }
-            for (; f < n_valid; f += g) {
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+                if (ok[u]) *dst[u] = v[u];
+        }
+        for (; t < n_pass; t += n_warps) {
+            const int f = t * g + lrow;
+            if (f < n_valid) {
                 const int64_t row = slot_row(m, f, p.pblock_shift, pmask, p.n_rows);
                 const T v = reinterpret_cast<const T*>(stage + static_cast<size_t>(perm[f]) * p.slab_bytes)[lq];
-                reinterpret_cast<T*>(p.data + row * p.row_bytes + col)[lq] = v;
+                reinterpret_cast<T*>(data + row * p.row_bytes)[lq] = v;
             }
         }
     }
-}
-
-template <int W>
-__device__ __forceinline__ void store_unit_dispatch(const IterParams& p, const StageMeta& m, const uint8_t* stage,
-                                                    const uint16_t* perm, int slab, int slen, int lane)
-{
-    store_unit<W>(p, m, stage, perm, slab, slen, lane);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -388,49 +448,58 @@ __device__ __forceinline__ void store_unit_dispatch(const IterParams& p, const S
 // EPL: elements per lane of the permutation sort (32 * EPL >= V * P).
 // INJECTED: members, permutation and offset come from the caller instead of the device RNG.
 // BULK: rows are 16-byte multiples on a 16-byte aligned deck -> TMA bulk loads.
+//
+// Warps 0 .. n_movers-1 move data; warps n_movers .. n_movers+n_permuters-1 compute, for unit
+// u (permuter (u % n_permuters)), the ordered members, their storage runs and the permutation
+// into slot u % KP, running up to KP units ahead of the movers.
 // ---------------------------------------------------------------------------------------------
 
 template <int EPL, bool INJECTED, bool BULK>
-__global__ void __launch_bounds__(512) povs_iteration_kernel(const __grid_constant__ IterParams p)
+__global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_constant__ IterParams p)
 {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
-    const int warps_per_cta = blockDim.x >> 5;
-    WarpSmem ws = carve_warp_smem(smem_raw + static_cast<size_t>(warp) * p.warp_bytes, p);
-
-    if (BULK) {
-        if (lane < p.n_stages) mbar_init(&ws.bars[lane], 1);
-        mbar_fence_init();
-    }
-    __syncwarp();
-
-    // Iteration-wide randomness.
-    int64_t offset;
-    if constexpr (INJECTED) {
-        offset = p.offset;
-    } else {
-        offset = p.offsets[reduce_range(offset_draw(p.seed, p.iteration), static_cast<uint32_t>(p.n_offsets))];
-    }
-    Feistel pi;
-    if constexpr (!INJECTED) pi.init(p.seed, p.iteration, static_cast<uint64_t>(p.n_vblocks) * p.vblock);
-
-    const int64_t gw = static_cast<int64_t>(blockIdx.x) * warps_per_cta + warp;
-    const int64_t total_warps = static_cast<int64_t>(gridDim.x) * warps_per_cta;
-    if (gw >= p.n_vblocks) return;
-    const int64_t my_vblocks = (p.n_vblocks - gw + total_warps - 1) / total_warps;
-    const int64_t n_units = my_vblocks * p.n_slabs;
+    const int n_movers = p.n_movers;
     const int nst = p.n_stages;
+    const int kp = p.n_slots;
+    const uint32_t mover_threads = static_cast<uint32_t>(n_movers) * 32u;
+    CtaSmem sm = carve_smem(smem_raw, p);
+
+    for (int i = threadIdx.x; i < nst; i += blockDim.x) {
+        mbar_init(&sm.full[i], 32);
+        mbar_init(&sm.empty[i], mover_threads);
+    }
+    for (int i = threadIdx.x; i < kp; i += blockDim.x) {
+        mbar_init(&sm.pfull[i], 32);
+        mbar_init(&sm.pempty[i], mover_threads);
+    }
+    mbar_fence_init();
+    __syncthreads();
+
+    if (blockIdx.x >= p.n_vblocks) return;
+    const int64_t my_vblocks = (p.n_vblocks - blockIdx.x + gridDim.x - 1) / gridDim.x;
+    const int64_t n_units = my_vblocks * p.n_slabs;
     const int pmask = p.pblock - 1;
 
-    // Prepares unit j in stage j % nst: metadata, permutation, and (bulk path) the async loads.
-    auto issue = [&](int64_t j) {
-        const int st = static_cast<int>(j % nst);
-        const int64_t v = gw + (j / p.n_slabs) * total_warps;
-        const int slab = static_cast<int>(j % p.n_slabs);
-        StageMeta& m = ws.meta[st];
-        uint16_t* perm = ws.perm + static_cast<size_t>(st) * (perm_bytes_per_stage(p.vp) / 2);
-        if (slab == 0) {
+    if (warp >= n_movers) {
+        // ------------------------------------------------------------------ permuter warps
+        int64_t offset;
+        if constexpr (INJECTED) {
+            offset = p.offset;
+        } else {
+            offset = p.offsets[reduce_range(offset_draw(p.seed, p.iteration), static_cast<uint32_t>(p.n_offsets))];
+        }
+        Feistel pi;
+        if constexpr (!INJECTED) pi.init(p.seed, p.iteration, static_cast<uint64_t>(p.n_vblocks) * p.vblock);
+        const int q = warp - n_movers;
+        for (int64_t u = q; u < n_units; u += p.n_permuters) {
+            const int k = static_cast<int>(u % kp);
+            if (u >= kp && !warp_wait(&sm.pempty[k], static_cast<uint32_t>(((u / kp) - 1) & 1), p.status)) return;
+            const int64_t v = blockIdx.x + (u / p.n_slabs) * static_cast<int64_t>(gridDim.x);
+            StageMeta& m = sm.meta[k];
+            uint16_t* perm = sm.perm + static_cast<size_t>(k) * sm.perm_stride;
+
             int64_t mem = -1;
             if (lane < p.vblock) {
                 const int64_t slot = v * p.vblock + lane;
@@ -483,105 +552,132 @@ __global__ void __launch_bounds__(512) povs_iteration_kernel(const __grid_consta
             } else {
                 warp_make_perm<EPL>(p, static_cast<uint64_t>(v), n_valid, perm, lane);
             }
-        } else {
-            // Same vblock as unit j-1, whose stage still holds its metadata and permutation.
-            const int prev = static_cast<int>((j - 1) % nst);
-            const StageMeta& pm = ws.meta[prev];
-            const uint16_t* pp = ws.perm + static_cast<size_t>(prev) * (perm_bytes_per_stage(p.vp) / 2);
-            if (lane < p.vblock) m.start[lane] = pm.start[lane];
-            if (lane == 0) m.n_valid = pm.n_valid;
-            for (int f = lane; f < pm.n_valid; f += 32) perm[f] = pp[f];
+            __syncwarp();
+            mbar_arrive(&sm.pfull[k]); // each lane publishes its writes to the slot
         }
-        __syncwarp();
+        return;
+    }
+
+    // ---------------------------------------------------------------------- mover warps
+    const int mw = warp;
+
+    // Issues unit u into stage u % nst (called by mover u % n_movers).  Returns false on a timeout.
+    auto issue = [&](int64_t u) -> bool {
+        const int st = static_cast<int>(u % nst);
+        const int k = static_cast<int>(u % kp);
+        if (!warp_wait(&sm.pfull[k], static_cast<uint32_t>((u / kp) & 1), p.status)) return false;
+        if (u >= nst && !warp_wait(&sm.empty[st], static_cast<uint32_t>(((u / nst) - 1) & 1), p.status))
+            return false;
+        fence_proxy_async_smem();
+        const StageMeta& m = sm.meta[k];
         const int n_valid = m.n_valid;
+        const int slab = static_cast<int>(u % p.n_slabs);
         const int64_t col = static_cast<int64_t>(slab) * p.slab_bytes;
         const int slen = static_cast<int>(min(static_cast<int64_t>(p.slab_bytes), p.row_bytes - col));
-        uint8_t* stage = ws.data + static_cast<size_t>(st) * p.stage_bytes;
+        uint8_t* stage = sm.data + static_cast<size_t>(st) * p.stage_bytes;
         if constexpr (BULK) {
-            if (lane == 0) mbar_arrive_expect_tx(&ws.bars[st], static_cast<uint32_t>(n_valid) * static_cast<uint32_t>(slen));
+            if (lane == 0) mbar_expect_tx(&sm.full[st], static_cast<uint32_t>(n_valid) * static_cast<uint32_t>(slen));
             __syncwarp();
             if (p.n_slabs == 1) {
-                // Whole rows: each member is <= 2 contiguous runs (split where the offset wraps).
+                // Whole rows: each member is <= 2 contiguous runs (split where the offset wraps),
+                // copied in pieces of at most copy_rows rows; pieces are spread over the lanes.
+                const int pieces_per_member = (p.pblock + p.copy_rows - 1) / p.copy_rows;
                 const int n_mem = (n_valid + pmask) >> p.pblock_shift;
-                if (lane < n_mem) {
-                    const int first = lane << p.pblock_shift;
-                    const int rows = min(p.pblock, n_valid - first);
-                    const int64_t s0 = m.start[lane];
+                for (int q = lane; q < n_mem * pieces_per_member; q += 32) {
+                    const int r = q / pieces_per_member;
+                    const int i0 = (q - r * pieces_per_member) * p.copy_rows;
+                    const int first = r << p.pblock_shift;
+                    const int rows_r = min(p.pblock, n_valid - first);
+                    if (i0 >= rows_r) continue;
+                    const int len = min(p.copy_rows, rows_r - i0);
+                    int64_t s0 = m.start[r] + i0;
+                    if (s0 >= p.n_rows) s0 -= p.n_rows;
                     const int64_t until_end = p.n_rows - s0;
-                    const int n1 = until_end < rows ? static_cast<int>(until_end) : rows;
-                    bulk_load(stage + static_cast<size_t>(first) * p.slab_bytes, p.data + s0 * p.row_bytes,
-                              static_cast<uint32_t>(n1) * static_cast<uint32_t>(p.row_bytes), &ws.bars[st]);
-                    if (rows > n1)
-                        bulk_load(stage + static_cast<size_t>(first + n1) * p.slab_bytes, p.data,
-                                  static_cast<uint32_t>(rows - n1) * static_cast<uint32_t>(p.row_bytes), &ws.bars[st]);
+                    const int n1 = until_end < len ? static_cast<int>(until_end) : len;
+                    uint8_t* dst = stage + static_cast<size_t>(first + i0) * p.slab_bytes;
+                    bulk_load(dst, p.data + s0 * p.row_bytes, static_cast<uint32_t>(n1) * static_cast<uint32_t>(p.row_bytes),
+                              &sm.full[st]);
+                    if (len > n1)
+                        bulk_load(dst + static_cast<size_t>(n1) * p.slab_bytes, p.data,
+                                  static_cast<uint32_t>(len - n1) * static_cast<uint32_t>(p.row_bytes), &sm.full[st]);
                 }
             } else {
                 for (int f = lane; f < n_valid; f += 32) {
                     const int64_t row = slot_row(m, f, p.pblock_shift, pmask, p.n_rows);
                     bulk_load(stage + static_cast<size_t>(f) * p.slab_bytes, p.data + row * p.row_bytes + col,
-                              static_cast<uint32_t>(slen), &ws.bars[st]);
+                              static_cast<uint32_t>(slen), &sm.full[st]);
                 }
             }
-        }
-    };
-
-    auto consume = [&](int64_t j) -> bool {
-        const int st = static_cast<int>(j % nst);
-        const int slab = static_cast<int>(j % p.n_slabs);
-        const StageMeta& m = ws.meta[st];
-        const uint16_t* perm = ws.perm + static_cast<size_t>(st) * (perm_bytes_per_stage(p.vp) / 2);
-        uint8_t* stage = ws.data + static_cast<size_t>(st) * p.stage_bytes;
-        const int64_t col = static_cast<int64_t>(slab) * p.slab_bytes;
-        const int slen = static_cast<int>(min(static_cast<int64_t>(p.slab_bytes), p.row_bytes - col));
-        if constexpr (BULK) {
-            if (!warp_wait_stage(&ws.bars[st], static_cast<uint32_t>((j / nst) & 1), p.status)) return false;
-            store_unit<16>(p, m, stage, perm, slab, slen, lane);
         } else {
             switch (p.vec_bytes) {
-            case 16:
-                lsu_load_unit<16>(p, m, stage, slab, slen, lane);
-                __syncwarp();
-                store_unit<16>(p, m, stage, perm, slab, slen, lane);
-                break;
-            case 8:
-                lsu_load_unit<8>(p, m, stage, slab, slen, lane);
-                __syncwarp();
-                store_unit<8>(p, m, stage, perm, slab, slen, lane);
-                break;
-            case 4:
-                lsu_load_unit<4>(p, m, stage, slab, slen, lane);
-                __syncwarp();
-                store_unit<4>(p, m, stage, perm, slab, slen, lane);
-                break;
-            case 2:
-                lsu_load_unit<2>(p, m, stage, slab, slen, lane);
-                __syncwarp();
-                store_unit<2>(p, m, stage, perm, slab, slen, lane);
-                break;
-            default:
-                lsu_load_unit<1>(p, m, stage, slab, slen, lane);
-                __syncwarp();
-                store_unit<1>(p, m, stage, perm, slab, slen, lane);
-                break;
+            case 16: lsu_load_unit<16>(p, m, stage, col, slen, lane); break;
+            case 8: lsu_load_unit<8>(p, m, stage, col, slen, lane); break;
+            case 4: lsu_load_unit<4>(p, m, stage, col, slen, lane); break;
+            case 2: lsu_load_unit<2>(p, m, stage, col, slen, lane); break;
+            default: lsu_load_unit<1>(p, m, stage, col, slen, lane); break;
             }
+            __syncwarp();
         }
-        __syncwarp();
-        // The stage is reused by a later async copy: order this warp's shared reads before it.
-        fence_proxy_async_smem();
+        mbar_arrive(&sm.full[st]);
         return true;
     };
 
-    const int64_t ahead = nst - 1;
-    for (int64_t j = 0; j < ahead && j < n_units; ++j) issue(j);
-    for (int64_t j = 0; j < n_units; ++j) {
-        if (j + ahead < n_units) issue(j + ahead);
-        if (!consume(j)) {
-            // A stage never completed: stop, after giving the other in-flight stages the same bounded wait.
-            if constexpr (BULK) {
-                for (int64_t k = j + 1; k < n_units && k <= j + ahead; ++k)
-                    warp_wait_stage(&ws.bars[k % nst], static_cast<uint32_t>((k / nst) & 1), p.status);
+    auto store = [&](int64_t j) -> bool {
+        const int st = static_cast<int>(j % nst);
+        const int k = static_cast<int>(j % kp);
+        if (!warp_wait(&sm.full[st], static_cast<uint32_t>((j / nst) & 1), p.status)) return false;
+        const StageMeta& m = sm.meta[k];
+        const uint16_t* perm = sm.perm + static_cast<size_t>(k) * sm.perm_stride;
+        const uint8_t* stage = sm.data + static_cast<size_t>(st) * p.stage_bytes;
+        const int slab = static_cast<int>(j % p.n_slabs);
+        const int64_t col = static_cast<int64_t>(slab) * p.slab_bytes;
+        const int slen = static_cast<int>(min(static_cast<int64_t>(p.slab_bytes), p.row_bytes - col));
+        if constexpr (BULK) {
+            store_share<16>(p, m, stage, perm, col, slen, lane, mw, n_movers);
+        } else {
+            switch (p.vec_bytes) {
+            case 16: store_share<16>(p, m, stage, perm, col, slen, lane, mw, n_movers); break;
+            case 8: store_share<8>(p, m, stage, perm, col, slen, lane, mw, n_movers); break;
+            case 4: store_share<4>(p, m, stage, perm, col, slen, lane, mw, n_movers); break;
+            case 2: store_share<2>(p, m, stage, perm, col, slen, lane, mw, n_movers); break;
+            default: store_share<1>(p, m, stage, perm, col, slen, lane, mw, n_movers); break;
             }
+        }
+        mbar_arrive(&sm.empty[st]);  // this thread's reads of the data stage are done
+        mbar_arrive(&sm.pempty[k]);  // ... and of the permutation slot
+        return true;
+    };
+
+    // On a timeout: wait (bounded) for the copies of the units this warp issued and stop.
+    auto drain_and_stop = [&](int64_t from, int64_t last_issued) {
+        if constexpr (BULK) {
+            for (int64_t u = from; u <= last_issued; ++u)
+                if (u % n_movers == mw) warp_wait(&sm.full[u % nst], static_cast<uint32_t>((u / nst) & 1), p.status);
+        }
+    };
+
+    const int64_t ahead = nst - 1;
+    int64_t last_issued = -1;
+    for (int64_t u = mw; u < ahead && u < n_units; u += n_movers) {
+        if (!issue(u)) {
+            drain_and_stop(0, last_issued);
             return;
+        }
+        last_issued = u;
+    }
+    // Store before issuing: the issue of unit j+NST-1 waits for every mover's share of unit j-1.
+    for (int64_t j = 0; j < n_units; ++j) {
+        if (!store(j)) {
+            drain_and_stop(j, last_issued);
+            return;
+        }
+        const int64_t u = j + ahead;
+        if (u < n_units && u % n_movers == mw) {
+            if (!issue(u)) {
+                drain_and_stop(j + 1, last_issued);
+                return;
+            }
+            last_issued = u;
         }
     }
 }

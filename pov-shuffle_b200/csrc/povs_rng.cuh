@@ -165,10 +165,34 @@ struct Feistel {
         return (L << wr) | R;
     }
 
+    // Same network when both halves fit 32 bits: the high word of the round function is
+    // masked away there, so only the low hash is needed.
+    POVS_HD uint32_t round_trip32(uint32_t x) const
+    {
+        int wl = lbits, wr = rbits;
+        uint32_t L = x >> wr;
+        uint32_t R = x & ((1u << wr) - 1u);
+#pragma unroll
+        for (int i = 0; i < FEISTEL_ROUNDS; ++i) {
+            const uint32_t nr = (L ^ lowbias32(R ^ keys[i])) & ((1u << wl) - 1u);
+            L = R;
+            R = nr;
+            const int t = wl;
+            wl = wr;
+            wr = t;
+        }
+        return (L << wr) | R;
+    }
+
     // pi(x) for x in [0, domain): cycle-walk until the image falls inside the domain.
     // Terminates because round_trip is a permutation of [0, 2^bits) and x is inside the domain.
     POVS_HD uint64_t operator()(uint64_t x) const
     {
+        if (lbits + rbits <= 32) {
+            uint32_t y = round_trip32(static_cast<uint32_t>(x));
+            while (y >= domain) y = round_trip32(y);
+            return y;
+        }
         uint64_t y = round_trip(x);
         while (y >= domain) y = round_trip(y);
         return y;

@@ -39,7 +39,7 @@ SIGNATURES: dict[str, tuple] = {
     "povs_release_v1": (ctypes.c_int, []),
     "povs_last_error_string": (ctypes.c_char_p, []),
     "povs_version": (ctypes.c_int32, []),
-    "povs_set_tuning_v1": (ctypes.c_int, [_c_i32, _c_i32, _c_i32, _c_i32]),
+    "povs_set_tuning_v1": (ctypes.c_int, [_c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32]),
     "povs_describe_plan_v1": (ctypes.c_int, [_c_vp, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _P_I64, _c_i32]),
 }
 
@@ -195,8 +195,19 @@ def device_status(device: int) -> int:
     return int(out.value)
 
 
-def set_tuning(stage_cap: int = 32 * 1024, n_stages: int = 2, max_warps: int = 16, force_plain: bool = False) -> None:
-    check(load().povs_set_tuning_v1(stage_cap, n_stages, max_warps, int(force_plain)), "povs_set_tuning_v1")
+def set_tuning(
+    stage_cap: int = 32 * 1024,
+    n_stages: int = 8,
+    movers: int = 4,
+    permuters: int = 4,
+    force_plain: bool = False,
+    copy_bytes: int = 8192,
+) -> None:
+    """Process-wide launch tuning (see include/povs.h); the defaults restore the built-in plan."""
+    check(
+        load().povs_set_tuning_v1(stage_cap, n_stages, movers, permuters, int(force_plain), copy_bytes),
+        "povs_set_tuning_v1",
+    )
 
 
 PLAN_FIELDS = (
@@ -207,11 +218,15 @@ PLAN_FIELDS = (
     "bulk",
     "slab_bytes",
     "n_slabs",
-    "stages_per_warp",
+    "stages_per_cta",
     "stage_bytes",
     "vec_bytes",
     "n_vblocks",
     "sm_count",
+    "copy_rows",
+    "perm_slots",
+    "movers",
+    "permuters",
 )
 
 
