@@ -36,6 +36,10 @@ extern "C" {
 /* Flags of povs_shuffle_v1(). */
 #define POVS_FLAG_NO_GRAPH 1u /* launch the iterations one by one instead of replaying a CUDA graph */
 #define POVS_FLAG_SYNC 2u     /* synchronize the stream and check the device status before returning */
+/* Draw the randomness with the distribution of the reference's CUDA path (per-vblock seeds 1..999,
+ * xorshift32 forward Fisher-Yates, padding in the last vblock; src/povs/__cuda/lib/povs.cu:396-430,
+ * 294-316) instead of uniform per-vblock permutations.  For statistical comparisons with it. */
+#define POVS_FLAG_REFERENCE_RNG 4u
 
 /* Limits of this build. */
 #define POVS_MAX_OFFSETS 256 /* offsets are passed to the device inline in the launch parameters */

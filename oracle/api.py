@@ -33,10 +33,10 @@ def lib() -> ctypes.CDLL:
                                                  ctypes.c_int64, _P, _P, ctypes.c_int]
             L.oracle_apply_iteration.restype = ctypes.c_int
             L.oracle_device_randomness.argtypes = [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_int64, ctypes.c_int,
-                                                   ctypes.c_int, _P, ctypes.c_int, _P, _P, _P]
+                                                   ctypes.c_int, _P, ctypes.c_int, _P, _P, _P, ctypes.c_int]
             L.oracle_device_randomness.restype = ctypes.c_int
             L.oracle_shuffle.argtypes = [_P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_int, _P,
-                                         ctypes.c_int, ctypes.c_int, ctypes.c_uint64]
+                                         ctypes.c_int, ctypes.c_int, ctypes.c_uint64, ctypes.c_int]
             L.oracle_shuffle.restype = ctypes.c_int
             L.oracle_shuffle_threads.argtypes = [_P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_int, _P,
                                                  ctypes.c_int, ctypes.c_int, ctypes.c_uint64, ctypes.c_int]
@@ -103,8 +103,11 @@ def apply_iteration(deck: np.ndarray, pblock: int, vblock: int, offset: int, ass
         raise ValueError(f"oracle_apply_iteration failed ({rc})")
 
 
+MODES = {"uniform": 0, "reference_cuda": 1}
+
+
 def device_randomness(seed: int, iteration: int, n_rows: int, pblock: int, vblock: int,
-                      offsets: list[int]) -> tuple[int, np.ndarray, np.ndarray]:
+                      offsets: list[int], mode: str = "uniform") -> tuple[int, np.ndarray, np.ndarray]:
     """This build's device randomness for one iteration: (offset, assign [n_v,V], perms [n_v,V*P])."""
     n_p, n_v = block_counts(n_rows, pblock, vblock)
     offs = np.array(offsets, dtype=np.int64)
@@ -112,19 +115,20 @@ def device_randomness(seed: int, iteration: int, n_rows: int, pblock: int, vbloc
     assign = np.zeros((n_v, vblock), dtype=np.int64)
     perms = np.zeros((n_v, vblock * pblock), dtype=np.int32)
     rc = lib().oracle_device_randomness(seed & (2**64 - 1), iteration, n_rows, pblock, vblock, _ptr(offs), len(offs),
-                                        _ptr(off), _ptr(assign), _ptr(perms))
+                                        _ptr(off), _ptr(assign), _ptr(perms), MODES[mode])
     if rc != 0:
         raise ValueError(f"oracle_device_randomness failed ({rc})")
     return int(off[0]), assign, perms
 
 
-def shuffle(deck: np.ndarray, iterations: int, pblock: int, vblock: int, offsets: list[int], seed: int) -> None:
+def shuffle(deck: np.ndarray, iterations: int, pblock: int, vblock: int, offsets: list[int], seed: int,
+            mode: str = "uniform") -> None:
     """This build's full shuffle (device randomness of ``seed``), in place on a host deck."""
     rows = as_rows(deck)
     n, r = rows.shape
     offs = np.array(offsets, dtype=np.int64)
     rc = lib().oracle_shuffle(_ptr(rows), n, r, pblock, vblock, _ptr(offs), len(offs), iterations,
-                              seed & (2**64 - 1))
+                              seed & (2**64 - 1), MODES[mode])
     if rc != 0:
         raise ValueError(f"oracle_shuffle failed ({rc})")
 

@@ -52,7 +52,10 @@ void oracle_philox4x32_10(const uint32_t ctr_in[4], const uint32_t key_in[2], ui
     out[3] = c3;
 }
 
-enum { DOM_OFFSET = 1, DOM_ASSIGN = 2, DOM_PERM = 3, N_FEISTEL = 12 };
+enum { DOM_OFFSET = 1, DOM_ASSIGN = 2, DOM_PERM = 3, DOM_VSEED = 4, N_FEISTEL = 12 };
+
+/* Randomness modes: 0 = uniform permutations; 1 = the reference CUDA path's distribution. */
+enum { MODE_UNIFORM = 0, MODE_REFERENCE_CUDA = 1 };
 
 static void draw(uint64_t seed, uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, uint32_t out[4])
 {
@@ -225,6 +228,30 @@ int oracle_apply_iteration(uint8_t* data, int64_t N, int64_t R, int P, int V, in
 
 /* ---------------------------------------------------------------- this build's device randomness */
 
+/* Seed in [1, 999] of vblock v (reference-CUDA mode). */
+static uint32_t vblock_seed(uint64_t seed, uint32_t iteration, uint64_t v)
+{
+    uint32_t w[4];
+    draw(seed, 0u, (uint32_t)v, ((uint32_t)(v >> 32) & 0x00FFFFFFu) | ((uint32_t)DOM_VSEED << 24), iteration, w);
+    return 1u + (uint32_t)(((uint64_t)w[0] * 999u) >> 32);
+}
+
+/* The reference kernel's single-thread shuffle of the gap-free slots (povs.cu:282-321). */
+static void xorshift_fisher_yates(uint32_t r, int n_valid, int32_t* perm)
+{
+    for (int f = 0; f < n_valid; ++f) perm[f] = f;
+    const int last = n_valid - 1;
+    for (int i = 0; i <= last; ++i) {
+        r ^= r << 13;
+        r ^= r >> 17;
+        r ^= r << 5;
+        int j = i + (int)(((uint64_t)r * (uint64_t)(last - i + 1)) >> 32);
+        int32_t t = perm[i];
+        perm[i] = perm[j];
+        perm[j] = t;
+    }
+}
+
 typedef struct {
     uint64_t key;
     int32_t e;
@@ -243,7 +270,7 @@ static int cmp_keyed(const void* a, const void* b)
  * (padding = -1) and the permutations [n_v][V*P] (entries beyond each vblock's valid rows = -1).
  */
 int oracle_device_randomness(uint64_t seed, uint32_t iteration, int64_t N, int P, int V, const int64_t* offsets,
-                             int n_offsets, int64_t* out_offset, int64_t* out_assign, int32_t* out_perms)
+                             int n_offsets, int64_t* out_offset, int64_t* out_assign, int32_t* out_perms, int mode)
 {
     const int64_t n_p = (N + P - 1) / P;
     const int64_t n_v = (n_p + V - 1) / V;
@@ -255,8 +282,13 @@ int oracle_device_randomness(uint64_t seed, uint32_t iteration, int64_t N, int P
     *out_offset = offset;
 
     bijection_t b;
-    bijection_init(&b, seed, iteration, (uint64_t)(n_v * V));
+    /* mode 1: the bijection covers the n_p pblocks only; slots n_p.. stay padding (last vblock). */
+    bijection_init(&b, seed, iteration, mode == MODE_REFERENCE_CUDA ? (uint64_t)n_p : (uint64_t)(n_v * V));
     for (int64_t s = 0; s < n_v * V; ++s) {
+        if (mode == MODE_REFERENCE_CUDA && s >= n_p) {
+            out_assign[s] = -1;
+            continue;
+        }
         uint64_t a = bijection_apply(&b, (uint64_t)s);
         out_assign[s] = (int64_t)a < n_p ? (int64_t)a : -1;
     }
@@ -267,6 +299,12 @@ int oracle_device_randomness(uint64_t seed, uint32_t iteration, int64_t N, int P
     for (int64_t v = 0; v < n_v; ++v) {
         int nm = 0;
         int n_valid = order_members(out_assign + v * V, V, N, P, n_p, offset, 1, starts, &nm);
+        if (mode == MODE_REFERENCE_CUDA) {
+            int32_t* pv = out_perms + v * VP;
+            xorshift_fisher_yates(vblock_seed(seed, iteration, (uint64_t)v), n_valid, pv);
+            for (int f = n_valid; f < VP; ++f) pv[f] = -1;
+            continue;
+        }
         for (int e = 0; e < n_valid; ++e) {
             uint32_t w[4];
             draw(seed, (uint32_t)e >> 2, (uint32_t)v, ((uint32_t)((uint64_t)v >> 32) & 0x00FFFFFFu) | ((uint32_t)DOM_PERM << 24),
@@ -282,9 +320,9 @@ int oracle_device_randomness(uint64_t seed, uint32_t iteration, int64_t N, int P
     return 0;
 }
 
-/* Full shuffle with this build's device randomness: iterations 0..iterations-1 of `seed`. */
+/* Full shuffle with this build's device randomness: iterations 0..iterations-1 of `seed` in `mode`. */
 int oracle_shuffle(uint8_t* data, int64_t N, int64_t R, int P, int V, const int64_t* offsets, int n_offsets,
-                   int iterations, uint64_t seed)
+                   int iterations, uint64_t seed, int mode)
 {
     const int64_t n_p = (N + P - 1) / P;
     const int64_t n_v = (n_p + V - 1) / V;
@@ -298,7 +336,7 @@ int oracle_shuffle(uint8_t* data, int64_t N, int64_t R, int P, int V, const int6
     int rc = 0;
     for (int it = 0; it < iterations && rc == 0; ++it) {
         int64_t offset = 0;
-        rc = oracle_device_randomness(seed, (uint32_t)it, N, P, V, offsets, n_offsets, &offset, assign, perms);
+        rc = oracle_device_randomness(seed, (uint32_t)it, N, P, V, offsets, n_offsets, &offset, assign, perms, mode);
         if (rc == 0) rc = oracle_apply_iteration(data, N, R, P, V, offset, assign, perms, 1);
     }
     free(assign);

@@ -377,6 +377,7 @@ int shuffle_on_device(void* data, int64_t n_rows, int64_t row_bytes, const int64
     IterParams base;
     fill_geometry(base, data, n_rows, row_bytes, pblock, vblock, c.status);
     base.seed = seed;
+    base.rng_mode = (flags & POVS_FLAG_REFERENCE_RNG) ? povs::RNG_REFERENCE_CUDA : povs::RNG_UNIFORM;
     base.n_offsets = n_offsets;
     for (int i = 0; i < n_offsets; ++i) base.offsets[i] = offsets[i];
     Plan pl;

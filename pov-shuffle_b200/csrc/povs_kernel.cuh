@@ -79,6 +79,7 @@ struct IterParams {
     uint64_t seed;
     int32_t n_offsets;
     int32_t sort_members; // injected mode: 1 = ascending, padding last (CUDA path); 0 = given order (NumPy path)
+    int32_t rng_mode;     // RNG_UNIFORM or RNG_REFERENCE_CUDA (device randomness only)
     int64_t offset;       // injected mode: this iteration's offset
     const int64_t* assign; // injected mode: [n_vblocks][V] pblock ids, padding < 0 or >= n_pblocks
     const int32_t* perms;  // injected mode: [n_vblocks][V*P] source slot of each destination slot
@@ -274,6 +275,30 @@ __device__ __forceinline__ void warp_make_perm(const IterParams& p, uint64_t vbl
         const int f = lane * EPL + r;
         if (f < n_valid) perm[f] = static_cast<uint16_t>(x[r] & 0xffffu);
     }
+}
+
+// The reference kernel's permutation (src/povs/__cuda/lib/povs.cu:282-321): identity over the
+// gap-free slots 0..n_valid-1, then a forward Fisher-Yates on one thread with xorshift32
+// (13, 17, 5) seeded by the vblock seed and Lemire's multiply-shift range reduction.
+__device__ __forceinline__ void warp_make_perm_xorshift(const IterParams& p, uint64_t vblock, int n_valid,
+                                                        uint16_t* perm, int lane)
+{
+    for (int f = lane; f < n_valid; f += 32) perm[f] = static_cast<uint16_t>(f);
+    __syncwarp();
+    if (lane == 0) {
+        uint32_t r = vblock_seed(p.seed, p.iteration, vblock);
+        const int last = n_valid - 1;
+        for (int i = 0; i <= last; ++i) {
+            r ^= r << 13;
+            r ^= r >> 17;
+            r ^= r << 5;
+            const int j = i + static_cast<int>((static_cast<uint64_t>(r) * static_cast<uint64_t>(last - i + 1)) >> 32);
+            const uint16_t t = perm[i];
+            perm[i] = perm[j];
+            perm[j] = t;
+        }
+    }
+    __syncwarp();
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -491,7 +516,11 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
             offset = p.offsets[reduce_range(offset_draw(p.seed, p.iteration), static_cast<uint32_t>(p.n_offsets))];
         }
         Feistel pi;
-        if constexpr (!INJECTED) pi.init(p.seed, p.iteration, static_cast<uint64_t>(p.n_vblocks) * p.vblock);
+        // Uniform mode maps all n_v*V slots (padding ids anywhere); the reference-CUDA mode maps
+        // slots [0, n_p) and leaves the padding in the last slots, as the reference does.
+        const bool ref_rng = p.rng_mode == RNG_REFERENCE_CUDA;
+        if constexpr (!INJECTED)
+            pi.init(p.seed, p.iteration, ref_rng ? static_cast<uint64_t>(p.n_pblocks) : static_cast<uint64_t>(p.n_vblocks) * p.vblock);
         const int q = warp - n_movers;
         for (int64_t u = q; u < n_units; u += p.n_permuters) {
             const int k = static_cast<int>(u % kp);
@@ -507,7 +536,7 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
                 if constexpr (INJECTED) {
                     a = p.assign[slot];
                 } else {
-                    a = static_cast<int64_t>(pi(static_cast<uint64_t>(slot)));
+                    a = (ref_rng && slot >= p.n_pblocks) ? -1 : static_cast<int64_t>(pi(static_cast<uint64_t>(slot)));
                 }
                 mem = (a >= 0 && a < p.n_pblocks) ? a : -1;
             }
@@ -550,7 +579,10 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
                     perm[f] = static_cast<uint16_t>(sf);
                 }
             } else {
-                warp_make_perm<EPL>(p, static_cast<uint64_t>(v), n_valid, perm, lane);
+                if (ref_rng)
+                    warp_make_perm_xorshift(p, static_cast<uint64_t>(v), n_valid, perm, lane);
+                else
+                    warp_make_perm<EPL>(p, static_cast<uint64_t>(v), n_valid, perm, lane);
             }
             __syncwarp();
             mbar_arrive(&sm.pfull[k]); // each lane publishes its writes to the slot

@@ -38,6 +38,14 @@ enum : uint32_t {
     DOMAIN_OFFSET = 1u,
     DOMAIN_ASSIGN = 2u,
     DOMAIN_PERM = 3u,
+    DOMAIN_VSEED = 4u,
+};
+
+// Randomness modes.
+enum : int {
+    RNG_UNIFORM = 0,        // uniform per-vblock permutations (sorted Philox keys), padding anywhere
+    RNG_REFERENCE_CUDA = 1, // the reference CUDA path's distribution: per-vblock seeds 1..999,
+                            // xorshift32 forward Fisher-Yates, padding in the last vblock
 };
 
 constexpr int FEISTEL_ROUNDS = 12;
@@ -107,6 +115,15 @@ POVS_HD U32x4 perm_key4(uint64_t seed, uint32_t iteration, uint64_t vblock, uint
     const U32x4 c{quad, static_cast<uint32_t>(vblock),
                   (static_cast<uint32_t>(vblock >> 32) & 0x00FFFFFFu) | (DOMAIN_PERM << 24), iteration};
     return philox4x32_10(c, seed_lo(seed), seed_hi(seed));
+}
+
+// Per-vblock seed in [1, 999] of the reference-CUDA mode (the reference draws
+// uniform_int_distribution(1, 999), src/povs/__cuda/lib/povs.cu:398,425-426).
+POVS_HD uint32_t vblock_seed(uint64_t seed, uint32_t iteration, uint64_t vblock)
+{
+    const U32x4 c{0u, static_cast<uint32_t>(vblock),
+                  (static_cast<uint32_t>(vblock >> 32) & 0x00FFFFFFu) | (DOMAIN_VSEED << 24), iteration};
+    return 1u + reduce_range(philox4x32_10(c, seed_lo(seed), seed_hi(seed)).x, 999u);
 }
 
 POVS_HD uint32_t lowbias32(uint32_t x)

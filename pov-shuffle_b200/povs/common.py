@@ -54,6 +54,16 @@ def seed_to_u64(seed: int) -> int:
     return int(seed) & 0xFFFF_FFFF_FFFF_FFFF
 
 
+RANDOMNESS_MODES = ("uniform", "reference_cuda")
+
+
+def randomness_flags(options: Options) -> int:
+    """Native flags selecting the randomness mode of ``options`` (AssertionError if unknown)."""
+    mode = options.randomness or "uniform"
+    assert mode in RANDOMNESS_MODES, f"randomness ({mode!r}) must be one of {RANDOMNESS_MODES}"
+    return 4 if mode == "reference_cuda" else 0
+
+
 def get_dtype_bytes(dataset: np.ndarray | torch.Tensor) -> int:
     return dataset.element_size() if isinstance(dataset, torch.Tensor) else dataset.itemsize
 

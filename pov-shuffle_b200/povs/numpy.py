@@ -23,6 +23,7 @@ from .common import (
     get_instance_size,
     povs_preflight,
     purge_dependent_param,
+    randomness_flags,
     seed_to_u64,
 )
 from .constants import DEFAULT_CPU_PBLOCK_SIZE, MIN_VBLOCK_SIZE
@@ -57,7 +58,7 @@ def shuffle(data: np.ndarray, iterations: int, options: Options | None, seed: in
         options.physical_block_size,
         options.virtual_block_size,
         seed_to_u64(seed),
-        flags,
+        flags | randomness_flags(options),
     )
     if not contiguous:
         data[...] = host
@@ -87,6 +88,7 @@ def optim_options_for_dataset(data: np.ndarray, options: Options | None) -> Opti
         purge_dependent_param(options, "physical_block_size", "offsets")
     pblk = options.physical_block_size or DEFAULT_CPU_PBLOCK_SIZE
     return Options(
+        randomness=options.randomness,
         virtual_block_size=options.virtual_block_size or MIN_VBLOCK_SIZE,
         physical_block_size=pblk,
         offsets=choose_offsets(

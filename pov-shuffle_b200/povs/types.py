@@ -28,6 +28,10 @@ class Options(NamedTuple):
     :param physical_block_size: Physical block size, in number of instances.
     :param offsets: List of valid offsets to sample at random in each shuffling iteration, in number of instances.
     :param gpu_thread_block_size: Accepted for compatibility; the B200 kernels size their launch themselves.
+    :param randomness: ``"uniform"`` (default: uniformly random permutation of every virtual block) or
+                       ``"reference_cuda"`` (the reference CUDA implementation's distribution: per-block seeds
+                       1..999 and an xorshift32 Fisher-Yates, padding in the last virtual block), for
+                       statistical comparisons with it.  Not part of the reference's options.
     """
 
     virtual_block_size: int | None = None
@@ -35,3 +39,5 @@ class Options(NamedTuple):
     offsets: list[int] | None = None
 
     gpu_thread_block_size: int | None = None
+
+    randomness: str | None = None

@@ -65,6 +65,30 @@ def test_default_mode_matches_oracle(oracle_api, n_rows, row_bytes, P, V, offset
     assert np.array_equal(got, want)
 
 
+@pytest.mark.parametrize(
+    "n_rows,row_bytes,P,V,offsets,iterations",
+    [(1000, 64, 8, 2, list(range(8)), 4), (4099, 256, 32, 4, [0, 1, 2, 5], 3), (20_000, 12, 16, 8, [0, 1, 3], 2),
+     (3000, 8, 128, 8, [0, 1, 5], 2)],
+)
+def test_reference_cuda_randomness_mode_matches_oracle(oracle_api, n_rows, row_bytes, P, V, offsets, iterations):
+    host = random_rows(n_rows, row_bytes, seed=11)
+    got = gpu_shuffle_bytes(host, P, V, offsets, iterations, 77, flags=_native.FLAG_REFERENCE_RNG)
+    want = host.copy()
+    oracle_api.shuffle(want, iterations, P, V, offsets, 77, "reference_cuda")
+    assert np.array_equal(got, want)
+
+
+def test_randomness_option_selects_the_mode():
+    deck = torch.arange(4096 * 4, dtype=torch.float32, device=DEV).view(4096, 4)
+    a, b = deck.clone(), deck.clone()
+    opts = povs.Options(2, 16, [0, 4], 32)
+    povs.shuffle(a, iterations=2, options=opts, seed=5)
+    povs.shuffle(b, iterations=2, options=opts._replace(randomness="reference_cuda"), seed=5)
+    assert not torch.equal(a, b)
+    with pytest.raises(AssertionError):
+        povs.shuffle(deck, iterations=1, options=opts._replace(randomness="bogus"), seed=5)
+
+
 def test_graph_and_direct_launches_agree(oracle_api):
     host = random_rows(20_000, 64, seed=3)
     a = gpu_shuffle_bytes(host, 16, 4, [0, 1, 2, 3], 5, seed=9)
