@@ -137,6 +137,34 @@ int povs_set_tuning_v1(int32_t stage_cap, int32_t n_stages, int32_t movers, int3
 int povs_describe_plan_v1(void* data, int64_t n_rows, int64_t row_bytes, int32_t pblock, int32_t vblock,
                           int32_t device, int64_t* out, int32_t n_out);
 
+/*
+ * Allocation-free variant of povs_apply_v1 (no counterpart in the reference).
+ *
+ * For callers that cannot allocate GPU memory while they run - for example a process whose
+ * memory pool has already reserved the GPU's free memory, or a service that forbids allocation
+ * after start-up to keep its footprint fixed.  The injected randomness is passed in HOST memory
+ * (same layouts as povs_apply_v1: assign_host int64 [iterations][n_v][V], perms_host int32
+ * [iterations][n_v][V*P]) and staged, one iteration at a time, in a scratch array that is part
+ * of the library image: POVS_STATIC_SCRATCH_BYTES of device memory that every GPU which loads
+ * the library holds until the process exits.  The call allocates nothing (no cudaMalloc, no
+ * CUDA graph); it launches the same kernels as povs_apply_v1 and gives the same bytes.
+ *
+ * Limit: one iteration needs 256 + round_up(8 * n_v * V, 256) + 4 * n_v * V * P bytes; larger
+ * decks are rejected with POVS_ERR_UNSUPPORTED (use povs_apply_v1 then).
+ * The first call on a device looks up the scratch array's device address (with that device
+ * current) and reads its limits; make that first call before any stream capture.
+ * Every call shares the one array, which keeps the last call's contents (the status word in it is
+ * cleared at the start of each call): calls that overlap on the GPU race.  With POVS_FLAG_SYNC the
+ * call synchronizes `stream` and returns POVS_ERR_DEVICE_STATUS if a kernel reported a failure;
+ * otherwise it returns after enqueueing, and the host arrays must stay unchanged until the stream
+ * has run the work (pinned host memory is read asynchronously).
+ */
+#define POVS_STATIC_SCRATCH_BYTES (8u * 1024u * 1024u)
+int povs_apply_static_v1(void* data, int64_t n_rows, int64_t row_bytes, int32_t pblock, int32_t vblock,
+                         int32_t iterations, const int64_t* offsets_per_iter, const int64_t* assign_host,
+                         const int32_t* perms_host, int32_t sort_members, int32_t device, void* stream,
+                         uint32_t flags);
+
 #ifdef __cplusplus
 }
 #endif

@@ -598,3 +598,131 @@ extern "C" int povs_describe_plan_v1(void* data, int64_t n_rows, int64_t row_byt
     for (int i = 0; i < n; ++i) out[i] = vals[i];
     return n;
 }
+
+// ------------------------------------------------------------------------------------------
+// Allocation-free injected-randomness entry (povs_apply_static_v1).
+//
+// Some callers cannot call cudaMalloc once they are running: a process whose memory pool has
+// already reserved the GPU's memory (a framework caching allocator holding every free byte), or
+// a service that allows no allocation after start-up so that its memory use stays fixed.  For
+// them this entry point stages the injected randomness in a fixed scratch array that is part of
+// the library image (a file-scope __device__ array, present on every GPU that loads the library
+// until the process exits) instead of in buffers the caller would have to allocate, keeps its
+// status word there too, and launches the kernels directly (no CUDA graph, no per-device context).
+//
+// Layout of the array: [status word, 256 bytes][assignment, int64][permutations, int32].  Every
+// call reuses it and it keeps the last call's contents; the status word is cleared at the start
+// of every call.  Calls that overlap on the GPU (different streams, or different host threads
+// without ordering) race on the array.
+// ------------------------------------------------------------------------------------------
+
+namespace {
+
+constexpr size_t STATIC_SCRATCH_BYTES = size_t{POVS_STATIC_SCRATCH_BYTES};
+constexpr size_t STATIC_STATUS_BYTES = 256;
+
+static __device__ __align__(256) unsigned char g_static_scratch[STATIC_SCRATCH_BYTES];
+
+struct StaticDevice {
+    bool ready = false;
+    unsigned char* scratch = nullptr; // device address of g_static_scratch on this device
+    DeviceCtx props;                  // SM count and shared-memory limits only (nothing allocated)
+};
+StaticDevice g_static_dev[MAX_DEVICES];
+std::mutex g_static_mu;
+
+// First call on a device: look up the scratch array's device address (with that device current)
+// and read the launch limits.  No allocation happens here or later.
+int static_setup(int dev, StaticDevice** out)
+{
+    if (dev < 0 || dev >= MAX_DEVICES) return fail(POVS_ERR_INVALID_ARGUMENT, "device %d out of range", dev);
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    StaticDevice& s = g_static_dev[dev];
+    if (!s.ready) {
+        cudaDeviceProp prop;
+        POVS_CUDA_TRY(cudaGetDeviceProperties(&prop, dev));
+        if (prop.major < 10)
+            return fail(POVS_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a (B200)", dev,
+                        prop.major, prop.minor);
+        void* ptr = nullptr;
+        POVS_CUDA_TRY(cudaGetSymbolAddress(&ptr, g_static_scratch));
+        s.props.sm_count = prop.multiProcessorCount;
+        s.props.smem_optin = static_cast<int>(prop.sharedMemPerBlockOptin);
+        s.props.smem_per_sm = static_cast<int>(prop.sharedMemPerMultiprocessor);
+        s.props.max_threads_per_sm = prop.maxThreadsPerMultiProcessor;
+        int r = set_smem_attr_all(s.props.smem_optin);
+        if (r != POVS_OK) return r;
+        s.scratch = static_cast<unsigned char*>(ptr);
+        s.ready = true;
+    }
+    *out = &s;
+    return POVS_OK;
+}
+
+} // namespace
+
+extern "C" int povs_apply_static_v1(void* data, int64_t n_rows, int64_t row_bytes, int32_t pblock, int32_t vblock,
+                                    int32_t iterations, const int64_t* offsets_per_iter, const int64_t* assign_host,
+                                    const int32_t* perms_host, int32_t sort_members, int32_t device, void* stream,
+                                    uint32_t flags)
+{
+    g_err[0] = '\0';
+    int r = check_common(data, n_rows, row_bytes, pblock, vblock, iterations);
+    if (r != POVS_OK) return r;
+    if (iterations > 0 && (offsets_per_iter == nullptr || assign_host == nullptr || perms_host == nullptr))
+        return fail(POVS_ERR_INVALID_ARGUMENT, "offsets_per_iter, assign_host and perms_host are required");
+    for (int i = 0; i < iterations; ++i)
+        if (offsets_per_iter[i] < 0 || offsets_per_iter[i] >= n_rows)
+            return fail(POVS_ERR_INVALID_ARGUMENT, "offset of iteration %d (%lld) must be in [0, %lld)", i,
+                        static_cast<long long>(offsets_per_iter[i]), static_cast<long long>(n_rows));
+    const int64_t n_pblocks = (n_rows + pblock - 1) / pblock;
+    const int64_t n_vblocks = (n_pblocks + vblock - 1) / vblock;
+    const int64_t n_slots = n_vblocks * vblock;
+    const int64_t n_perm = n_vblocks * static_cast<int64_t>(pblock) * vblock;
+    const size_t assign_bytes = static_cast<size_t>(n_slots) * sizeof(int64_t);
+    const size_t perm_offset = STATIC_STATUS_BYTES + ((assign_bytes + 255) / 256) * 256;
+    const size_t need = perm_offset + static_cast<size_t>(n_perm) * sizeof(int32_t);
+    if (need > STATIC_SCRATCH_BYTES)
+        return fail(POVS_ERR_UNSUPPORTED,
+                    "one iteration's injected randomness needs %zu bytes of scratch; povs_apply_static_v1 holds at "
+                    "most %zu (use povs_apply_v1 with caller-allocated device buffers)",
+                    need, STATIC_SCRATCH_BYTES);
+    DeviceGuard dg;
+    r = dg.enter(device);
+    if (r != POVS_OK) return r;
+    StaticDevice* sd = nullptr;
+    r = static_setup(device, &sd);
+    if (r != POVS_OK) return r;
+
+    int* status = reinterpret_cast<int*>(sd->scratch);
+    int64_t* assign_dev = reinterpret_cast<int64_t*>(sd->scratch + STATIC_STATUS_BYTES);
+    int32_t* perms_dev = reinterpret_cast<int32_t*>(sd->scratch + perm_offset);
+    IterParams base;
+    fill_geometry(base, data, n_rows, row_bytes, pblock, vblock, status);
+    base.sort_members = sort_members ? 1 : 0;
+    Plan pl;
+    r = plan_launch(base, sd->props, true, pl);
+    if (r != POVS_OK) return r;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    POVS_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), s));
+    for (int i = 0; i < iterations; ++i) {
+        // Stream order keeps each iteration's copies behind the previous iteration's kernel.
+        POVS_CUDA_TRY(cudaMemcpyAsync(assign_dev, assign_host + i * n_slots, assign_bytes, cudaMemcpyHostToDevice, s));
+        POVS_CUDA_TRY(cudaMemcpyAsync(perms_dev, perms_host + i * n_perm, static_cast<size_t>(n_perm) * sizeof(int32_t),
+                                      cudaMemcpyHostToDevice, s));
+        IterParams p = base;
+        p.iteration = static_cast<uint32_t>(i);
+        p.offset = offsets_per_iter[i];
+        p.assign = assign_dev;
+        p.perms = perms_dev;
+        r = launch_direct(pl, p, s);
+        if (r != POVS_OK) return r;
+    }
+    if (flags & POVS_FLAG_SYNC) {
+        POVS_CUDA_TRY(cudaStreamSynchronize(s));
+        int v = 0;
+        POVS_CUDA_TRY(cudaMemcpy(&v, status, sizeof(int), cudaMemcpyDeviceToHost));
+        if (v != 0) return fail(POVS_ERR_DEVICE_STATUS, "device status 0x%x after povs_apply_static_v1", v);
+    }
+    return POVS_OK;
+}

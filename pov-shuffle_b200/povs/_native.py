@@ -42,6 +42,10 @@ SIGNATURES: dict[str, tuple] = {
     "povs_version": (ctypes.c_int32, []),
     "povs_set_tuning_v1": (ctypes.c_int, [_c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32]),
     "povs_describe_plan_v1": (ctypes.c_int, [_c_vp, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _P_I64, _c_i32]),
+    "povs_apply_static_v1": (
+        ctypes.c_int,
+        [_c_vp, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _P_I64, _c_vp, _c_vp, _c_i32, _c_i32, _c_vp, _c_u32],
+    ),
 }
 
 
@@ -186,6 +190,47 @@ def apply(
         ctypes.c_void_p(current_stream_handle(dev)),
     )
     check(code, "povs_apply_v1")
+
+
+def apply_static(
+    data: torch.Tensor,
+    row_bytes: int,
+    pblock: int,
+    vblock: int,
+    offsets_per_iter: list[int],
+    assign_host,
+    perms_host,
+    sort_members: bool,
+    flags: int = FLAG_SYNC,
+) -> None:
+    """Allocation-free injection: host int64 assign / int32 perms staged in the library's fixed scratch.
+
+    For callers that may not allocate device memory (see include/povs.h); by default the call
+    synchronizes the stream, so the host arrays may be reused as soon as it returns.
+    """
+    import numpy as np
+
+    lib = load()
+    dev = data.device
+    a = np.ascontiguousarray(assign_host, dtype=np.int64)
+    p = np.ascontiguousarray(perms_host, dtype=np.int32)
+    offs = _i64_array(offsets_per_iter)
+    code = lib.povs_apply_static_v1(
+        ctypes.c_void_p(data.data_ptr()),
+        data.shape[0],
+        row_bytes,
+        pblock,
+        vblock,
+        len(offsets_per_iter),
+        offs,
+        ctypes.c_void_p(a.ctypes.data),
+        ctypes.c_void_p(p.ctypes.data),
+        1 if sort_members else 0,
+        dev.index,
+        ctypes.c_void_p(current_stream_handle(dev)),
+        flags,
+    )
+    check(code, "povs_apply_static_v1")
 
 
 def device_status(device: int) -> int:
