@@ -12,7 +12,10 @@ Workloads (synthetic data with the shapes and value distributions of the named c
   bf16_32GiB   134,217,728 x 128 bf16 (32 GiB), uniform [-1, 1) from seed 1, 4 iterations, V=4, P=32  [default]
   fp16_256MiB  1,048,576 x 128 fp16 (256 MiB), standard normal from seed 0, 4 iterations, V=2, P=64
   u8_12KiB     1,000,000 x 3x64x64 uint8 (12.3 GB), uniform 0..255 from seed 2, 3 iterations, V=2, P=16
-With --gpus N > 1 every rank shuffles its own deck of the workload (independent replicas on each GPU).
+  f32_128GiB   1,073,741,824 x 32 fp32 (128 GiB), standard normal from seed 3, 4 iterations, V=4, P=64
+With --gpus N > 1 (torchrun, one process per GPU) the workload's deck is split along axis 0 into N
+shards, one per GPU, and shuffled as one deck (povs.ShardedDeck: member rows move over NVLink):
+the total work is fixed, so the scaling is strong.
 
 ``--impl reference`` times the CPU implementation of the same path (the oracle's C restatement,
 all host threads) on a bounded sample of the workload and prints the same JSON line.
@@ -28,6 +31,7 @@ import subprocess
 import sys
 import tempfile
 import time
+from datetime import timedelta
 from pathlib import Path
 
 REPO = Path(__file__).resolve().parent
@@ -37,6 +41,7 @@ for _p in (REPO, REPO / "pov-shuffle_b200"):
 
 METRIC = "effective shuffle GB/s (2×bytes×iters/time), % HBM peak, 1/2/4/8×B200"
 FALLBACK_HBM_GBS = 6650.0
+NVLINK_PEER_GBS = 770.0  # measured peer copy per direction per GPU on this pool
 
 WORKLOADS = {
     "bf16_32GiB": dict(
@@ -47,11 +52,18 @@ WORKLOADS = {
         rows=1_048_576, shape=(128,), dtype="float16", iterations=4, V=2, P=64, seed=0, init="normal",
         desc="fp16 deck 1,048,576 x 128 (256 MiB), standard normal from seed 0, iterations=4, V=2, P=64",
     ),
+    "f32_128GiB": dict(
+        rows=1_073_741_824, shape=(32,), dtype="float32", iterations=4, V=4, P=64, seed=3, init="normal",
+        desc="fp32 deck 1,073,741,824 x 32 (128 GiB), standard normal from seed 3, iterations=4, V=4, P=64",
+    ),
     "u8_12KiB": dict(
         rows=1_000_000, shape=(3, 64, 64), dtype="uint8", iterations=3, V=2, P=16, seed=2, init="bytes",
         desc="uint8 deck 1,000,000 x 3x64x64 (12,288 B rows, 12.3 GB), uniform 0..255 from seed 2, iterations=3, V=2, P=16",
     ),
 }
+
+
+ELEM_BYTES = {"bfloat16": 2, "float16": 2, "uint8": 1, "float32": 4}
 
 
 def measured_peaks() -> tuple[float, str]:
@@ -66,7 +78,7 @@ def measured_peaks() -> tuple[float, str]:
 def row_bytes_of(w: dict) -> int:
     import numpy as np
 
-    elem = {"bfloat16": 2, "float16": 2, "uint8": 1, "float32": 4}[w["dtype"]]
+    elem = ELEM_BYTES[w["dtype"]]
     return int(np.prod(w["shape"])) * elem
 
 
@@ -139,12 +151,12 @@ class ClockSampler:
         }
 
 
-def make_deck(w: dict, device):
+def make_deck(w: dict, device, rows: int | None = None, seed_offset: int = 0):
     import torch
 
     dtype = getattr(torch, w["dtype"])
-    shape = (w["rows"], *w["shape"])
-    g = torch.Generator(device=device).manual_seed(w["seed"])
+    shape = (w["rows"] if rows is None else rows, *w["shape"])
+    g = torch.Generator(device=device).manual_seed(w["seed"] + seed_offset)
     if w["init"] == "uniform":
         return torch.rand(shape, generator=g, device=device, dtype=dtype) * 2 - 1
     if w["init"] == "normal":
@@ -164,26 +176,42 @@ def run_ours(args, w: dict, wname: str) -> None:
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
+        # The group only broadcasts seeds; NVLink multicast (NVLS) is not needed for that.
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=timedelta(seconds=300))
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
 
     R = row_bytes_of(w)
     N, P, V, iters = w["rows"], w["P"], w["V"], w["iterations"]
-    offsets = choose_offsets(N, int(R // {"bfloat16": 2, "float16": 2, "uint8": 1}[w["dtype"]]),
-                             {"bfloat16": 2, "float16": 2, "uint8": 1}[w["dtype"]], P)
+    elem = ELEM_BYTES[w["dtype"]]
+    offsets = choose_offsets(N, R // elem, elem, P)
     opts = povs.Options(virtual_block_size=V, physical_block_size=P, offsets=offsets, gpu_thread_block_size=64)
-    deck = make_deck(w, device)
-    plan = _native.describe_plan(deck, R, P, V)
     stream = torch.cuda.current_stream(device)
+    if world > 1:
+        # One deck of N rows split into `world` shards; every rank times the same collective steps.
+        rows = [N // world] * world
+        rows[-1] += N - sum(rows)
+        deck = make_deck(w, device, rows=rows[rank], seed_offset=rank)
+        sharded = povs.ShardedDeck(deck)
+        plan = {"shard_rows": rows}
+
+        def step(seed: int) -> None:
+            sharded.shuffle(iterations=iters, options=opts, seed=seed)
+    else:
+        deck = make_deck(w, device)
+        plan = _native.describe_plan(deck, R, P, V)
+
+        def step(seed: int) -> None:
+            povs.shuffle(deck, iterations=iters, options=opts, seed=seed)
 
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[local])
 
     for s in range(args.warmup):
-        povs.shuffle(deck, iterations=iters, options=opts, seed=1000 + s)
+        step(1000 + s)
     torch.cuda.synchronize(device)
     povs.check_device_status(device)
 
@@ -195,7 +223,7 @@ def run_ours(args, w: dict, wname: str) -> None:
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(stream)
     for s in range(args.steps):
-        povs.shuffle(deck, iterations=iters, options=opts, seed=s)
+        step(s)
     stop.record(stream)
     torch.cuda.synchronize(device)
     barrier()
@@ -207,55 +235,26 @@ def run_ours(args, w: dict, wname: str) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
 
-    deck_bytes = N * R
+    deck_bytes = N * R  # the whole deck (all shards)
     alg_bytes_per_step = 2 * deck_bytes * iters
     ms_per_step = ms / args.steps
-    value = world * alg_bytes_per_step / (ms_per_step / 1e3) / 1e9
-    launches = args.steps * iters
-    per_launch_s = (ms / 1e3) / launches
-    achieved = 2 * deck_bytes / per_launch_s / 1e9
+    value = alg_bytes_per_step / (ms_per_step / 1e3) / 1e9
+    per_launch_s = (ms / 1e3) / (args.steps * iters)
     peak, peak_kind = measured_peaks()
+    if world == 1:
+        bound, achieved, roof_peak, roof_kind = "hbm", 2 * deck_bytes / per_launch_s / 1e9, peak, peak_kind
+    else:
+        # Per GPU and iteration, (world-1)/world of the rows it reads come from peers and as many of
+        # the rows written into its shard come from peers: 2 (world-1)/world x shard bytes each way.
+        link_bytes = 2 * (world - 1) / world * (deck_bytes / world)
+        bound, achieved, roof_peak, roof_kind = "nvlink", link_bytes / per_launch_s / 1e9, NVLINK_PEER_GBS, (
+            "measured peer copy per direction on this pool")
 
-    # End to end: the same call with the deck in pinned host memory, copies inside the timed region.
+    # End to end: the same work with the deck in pinned host memory, copies inside the timed region.
     e2e = None
     if not args.no_e2e:
-        import ctypes
-
-        host = torch.empty(deck_bytes, dtype=torch.uint8, pin_memory=True)
-        host.copy_(deck.view(torch.uint8).reshape(-1))
-        staging = deck.view(torch.uint8).reshape(-1)
-        lib = _native.load()
-        offs = (ctypes.c_int64 * len(offsets))(*offsets)
-        e2e_steps = max(1, min(args.steps, args.e2e_steps))
-        rc = lib.povs_shuffle_host_v1(ctypes.c_void_p(host.data_ptr()), ctypes.c_void_p(staging.data_ptr()), N, R,
-                                      offs, len(offsets), iters, P, V, 7, local,
-                                      ctypes.c_void_p(stream.cuda_stream), 0)
-        _native.check(rc, "povs_shuffle_host_v1")
-        barrier()
-        e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e_start.record(stream)
-        for s in range(e2e_steps):
-            rc = lib.povs_shuffle_host_v1(ctypes.c_void_p(host.data_ptr()), ctypes.c_void_p(staging.data_ptr()), N,
-                                          R, offs, len(offsets), iters, P, V, 100 + s, local,
-                                          ctypes.c_void_p(stream.cuda_stream), 0)
-            _native.check(rc, "povs_shuffle_host_v1")
-        e_stop.record(stream)
-        torch.cuda.synchronize(device)
-        e_ms = e_start.elapsed_time(e_stop)
-        if world > 1:
-            t = torch.tensor([e_ms], device=device)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e_ms = float(t.item())
-        e2e = {
-            "value": round(world * alg_bytes_per_step / (e_ms / e2e_steps / 1e3) / 1e9, 3),
-            "unit": "GB/s",
-            "h2d_bytes_per_step": deck_bytes,
-            "d2h_bytes_per_step": deck_bytes,
-            "steps": e2e_steps,
-            "ms_per_step": round(e_ms / e2e_steps, 3),
-            "path": "povs_shuffle_host_v1 (pinned host deck)",
-        }
-        del host
+        e2e = run_e2e(args, w, deck, opts, offsets, iters, world, rank, local, stream,
+                      sharded if world > 1 else None, dist)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -271,7 +270,7 @@ def run_ours(args, w: dict, wname: str) -> None:
             "warmup": args.warmup,
             "ms_per_step": round(ms_per_step, 4),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong",
             "vs_baseline": None,
             "dtype": "u8",
             "data": "synthetic",
@@ -285,30 +284,99 @@ def run_ours(args, w: dict, wname: str) -> None:
                 "virtual_block_size": V,
                 "physical_block_size": P,
                 "offsets": offsets,
-                "instances_per_s": round(world * N * iters / (ms_per_step / 1e3)),
+                "instances_per_s": round(N * iters / (ms_per_step / 1e3)),
                 "l2": "inputs larger than L2 (deck > 126 MB)" if deck_bytes > 126e6 else "deck fits L2",
-                "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                "parallelism": f"sharded x{world} (NVLink P2P, one process per GPU)" if world > 1 else "single GPU",
                 "plan": plan,
             },
             "roofline": {
-                "bound": "hbm",
+                "bound": bound,
                 "kernel": "povs_iteration_kernel",
                 "achieved": round(achieved, 1),
-                "peak": peak,
-                "peak_kind": peak_kind,
+                "peak": roof_peak,
+                "peak_kind": roof_kind,
                 "unit": "GB/s",
-                "frac": round(achieved / peak, 4),
-                "traffic": traffic_per_launch("povs_iteration_kernel", wname),
-                "alg_bytes_per_launch": 2 * deck_bytes,
+                "frac": round(achieved / roof_peak, 4),
+                "traffic": traffic_per_launch("povs_iteration_kernel", wname) if world == 1 else None,
+                "alg_bytes_per_launch": 2 * deck_bytes // world,
+                "hbm_frac_per_gpu": round(2 * deck_bytes / world / per_launch_s / 1e9 / peak, 4),
             },
-            "gpu_launches": launches,
+            "gpu_launches": args.steps * iters if world == 1 else args.steps * (2 * iters + 1),
             "clocks": clocks,
             "e2e": e2e,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        sharded.close()
         dist.destroy_process_group()
+
+
+def run_e2e(args, w, deck, opts, offsets, iters, world, rank, local, stream, sharded, dist) -> dict | None:
+    """Same metric with the deck (or this rank's shard) in pinned host memory, copies timed."""
+    import ctypes
+
+    import psutil
+    import torch
+
+    import povs
+    from povs import _native
+
+    shard_bytes = deck.numel() * deck.element_size()
+    total_bytes = w["rows"] * row_bytes_of(w)
+    # Decide once (rank 0, before anything is pinned) so that every rank takes the same steps.
+    ok = torch.tensor([1 if psutil.virtual_memory().available >= 1.5 * total_bytes else 0], device=deck.device)
+    if world > 1:
+        dist.broadcast(ok, src=0)
+    if not int(ok.item()):
+        return {"value": None, "unit": "GB/s", "skipped": "not enough host memory for a pinned copy of the deck"}
+    host = torch.empty(shard_bytes, dtype=torch.uint8, pin_memory=True)
+    flat = deck.view(torch.uint8).reshape(-1)
+    host.copy_(flat)
+    R = row_bytes_of(w)
+    P, V = w["P"], w["V"]
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    if world == 1:
+        lib = _native.load()
+        offs = (ctypes.c_int64 * len(offsets))(*offsets)
+
+        def step(seed: int) -> None:
+            rc = lib.povs_shuffle_host_v1(ctypes.c_void_p(host.data_ptr()), ctypes.c_void_p(flat.data_ptr()),
+                                          deck.shape[0], R, offs, len(offsets), iters, P, V, seed, local,
+                                          ctypes.c_void_p(stream.cuda_stream), 0)
+            _native.check(rc, "povs_shuffle_host_v1")
+        path = "povs_shuffle_host_v1 (pinned host deck)"
+    else:
+        def step(seed: int) -> None:
+            flat.copy_(host, non_blocking=True)
+            sharded.shuffle(iterations=iters, options=opts, seed=seed)
+            host.copy_(flat, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+        path = "per rank: pinned host shard -> ShardedDeck.shuffle -> host"
+    step(7)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for s in range(e2e_steps):
+        step(100 + s)
+    e_stop.record(stream)
+    torch.cuda.synchronize()
+    e_ms = e_start.elapsed_time(e_stop)
+    if world > 1:
+        t = torch.tensor([e_ms], device=deck.device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_ms = float(t.item())
+    povs.check_device_status(deck.device)
+    return {
+        "value": round(2 * total_bytes * iters / (e_ms / e2e_steps / 1e3) / 1e9, 3),
+        "unit": "GB/s",
+        "h2d_bytes_per_step": total_bytes,
+        "d2h_bytes_per_step": total_bytes,
+        "steps": e2e_steps,
+        "ms_per_step": round(e_ms / e2e_steps, 3),
+        "path": path,
+    }
 
 
 def cpu_baseline(w: dict, threads: int, target_s: float) -> dict:
@@ -319,7 +387,7 @@ def cpu_baseline(w: dict, threads: int, target_s: float) -> dict:
     from povs.common import choose_offsets
 
     R = row_bytes_of(w)
-    elem = {"bfloat16": 2, "float16": 2, "uint8": 1}[w["dtype"]]
+    elem = ELEM_BYTES[w["dtype"]]
     P, V, iters = w["P"], w["V"], w["iterations"]
 
     def run(rows: int) -> float:

@@ -1,6 +1,7 @@
 // C ABI of the B200 POV shuffle: argument checks, launch planning, per-device
 // context and CUDA-graph chaining of iterations.  Declarations and the
 // reference interfaces each entry replaces are in include/povs.h.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -217,7 +218,8 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out)
     int epl = 1;
     while (32 * epl < vp) epl <<= 1;
 
-    const uintptr_t addr = reinterpret_cast<uintptr_t>(p.data);
+    uintptr_t addr = 0;
+    for (int i = 0; i < p.n_shards; ++i) addr |= reinterpret_cast<uintptr_t>(p.shard_base[i]);
     int vec = 16;
     while (vec > 1 && ((p.row_bytes % vec) != 0 || (addr % vec) != 0)) vec >>= 1;
     const bool bulk = (vec == 16) && !t.force_plain;
@@ -257,7 +259,8 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out)
     const int per_sm_by_smem = std::max(1, c.smem_per_sm / (cta_smem + 1024));
     const int per_sm_by_threads = std::max(1, c.max_threads_per_sm / (warps * 32));
     const int ctas_per_sm = std::min(per_sm_by_smem, per_sm_by_threads);
-    const int grid = static_cast<int>(std::min<int64_t>(p.n_vblocks, static_cast<int64_t>(c.sm_count) * ctas_per_sm));
+    const int64_t n_mine = p.vb_begin < p.n_vblocks ? (p.n_vblocks - p.vb_begin + p.vb_step - 1) / p.vb_step : 0;
+    const int grid = static_cast<int>(std::min<int64_t>(std::max<int64_t>(1, n_mine), static_cast<int64_t>(c.sm_count) * ctas_per_sm));
 
     p.slab_bytes = static_cast<int32_t>(slab);
     p.n_slabs = static_cast<int32_t>((p.row_bytes + slab - 1) / slab);
@@ -293,6 +296,13 @@ int check_common(void* data, int64_t n_rows, int64_t row_bytes, int32_t pblock, 
     return POVS_OK;
 }
 
+int64_t sum_rows(const int64_t* shard_rows, int32_t n_shards)
+{
+    int64_t n = 0;
+    for (int i = 0; i < n_shards; ++i) n += shard_rows[i] > 0 ? shard_rows[i] : 0;
+    return n;
+}
+
 void fill_geometry(IterParams& p, void* data, int64_t n_rows, int64_t row_bytes, int32_t pblock, int32_t vblock,
                    int* status)
 {
@@ -307,6 +317,12 @@ void fill_geometry(IterParams& p, void* data, int64_t n_rows, int64_t row_bytes,
     p.n_pblocks = (n_rows + pblock - 1) / pblock;
     p.n_vblocks = (p.n_pblocks + vblock - 1) / vblock;
     p.status = status;
+    p.n_shards = 1;
+    p.shard_base[0] = p.data;
+    p.shard_start[0] = 0;
+    p.shard_start[1] = n_rows;
+    p.vb_begin = 0;
+    p.vb_step = 1;
 }
 
 int launch_direct(const Plan& pl, const IterParams& p, cudaStream_t s)
@@ -370,12 +386,38 @@ int read_status(DeviceCtx& c, int32_t* out)
     return POVS_OK;
 }
 
+// Applies a shard table (pointers + row counts) to launch parameters; checks the layout.
+int set_shards(IterParams& p, void* const* shard_ptrs, const int64_t* shard_rows, int32_t n_shards)
+{
+    if (shard_ptrs == nullptr || shard_rows == nullptr || n_shards < 1 || n_shards > povs::MAX_SHARDS)
+        return fail(POVS_ERR_INVALID_ARGUMENT, "between 1 and %d shards are supported", povs::MAX_SHARDS);
+    int64_t start = 0;
+    for (int i = 0; i < n_shards; ++i) {
+        if (shard_ptrs[i] == nullptr) return fail(POVS_ERR_INVALID_ARGUMENT, "shard %d pointer is NULL", i);
+        if (shard_rows[i] < p.pblock)
+            return fail(POVS_ERR_UNSUPPORTED, "shard %d has %lld rows; every shard needs at least P = %d rows", i,
+                        static_cast<long long>(shard_rows[i]), p.pblock);
+        p.shard_base[i] = static_cast<uint8_t*>(shard_ptrs[i]);
+        p.shard_start[i] = start;
+        start += shard_rows[i];
+    }
+    p.shard_start[n_shards] = start;
+    p.n_shards = n_shards;
+    p.data = p.shard_base[0];
+    return POVS_OK;
+}
+
 int shuffle_on_device(void* data, int64_t n_rows, int64_t row_bytes, const int64_t* offsets, int32_t n_offsets,
                       int32_t iterations, int32_t pblock, int32_t vblock, uint64_t seed, DeviceCtx& c,
-                      cudaStream_t s, uint32_t flags)
+                      cudaStream_t s, uint32_t flags, void* const* shard_ptrs = nullptr,
+                      const int64_t* shard_rows = nullptr, int32_t n_shards = 1)
 {
     IterParams base;
     fill_geometry(base, data, n_rows, row_bytes, pblock, vblock, c.status);
+    if (shard_ptrs != nullptr) {
+        int rs = set_shards(base, shard_ptrs, shard_rows, n_shards);
+        if (rs != POVS_OK) return rs;
+    }
     base.seed = seed;
     base.rng_mode = (flags & POVS_FLAG_REFERENCE_RNG) ? povs::RNG_REFERENCE_CUDA : povs::RNG_UNIFORM;
     base.n_offsets = n_offsets;
@@ -724,5 +766,180 @@ extern "C" int povs_apply_static_v1(void* data, int64_t n_rows, int64_t row_byte
         POVS_CUDA_TRY(cudaMemcpy(&v, status, sizeof(int), cudaMemcpyDeviceToHost));
         if (v != 0) return fail(POVS_ERR_DEVICE_STATUS, "device status 0x%x after povs_apply_static_v1", v);
     }
+    return POVS_OK;
+}
+
+// ------------------------------------------------------------------------------------------
+// Decks split into shards.
+// ------------------------------------------------------------------------------------------
+
+extern "C" int povs_shuffle_shards_v1(void* const* shard_ptrs, const int64_t* shard_rows, int32_t n_shards,
+                                      int64_t row_bytes, const int64_t* offsets, int32_t n_offsets,
+                                      int32_t iterations, int32_t pblock, int32_t vblock, uint64_t seed,
+                                      int32_t device, void* stream, uint32_t flags)
+{
+    g_err[0] = '\0';
+    if (shard_ptrs == nullptr || shard_rows == nullptr || n_shards < 1 || n_shards > povs::MAX_SHARDS)
+        return fail(POVS_ERR_INVALID_ARGUMENT, "between 1 and %d shards are supported", povs::MAX_SHARDS);
+    const int64_t n_rows = sum_rows(shard_rows, n_shards);
+    int r = check_common(shard_ptrs[0], n_rows, row_bytes, pblock, vblock, iterations);
+    if (r != POVS_OK) return r;
+    r = check_offsets(offsets, n_offsets, n_rows);
+    if (r != POVS_OK) return r;
+    DeviceGuard dg;
+    r = dg.enter(device);
+    if (r != POVS_OK) return r;
+    DeviceCtx* c = nullptr;
+    r = get_ctx(device, &c);
+    if (r != POVS_OK) return r;
+    return shuffle_on_device(shard_ptrs[0], n_rows, row_bytes, offsets, n_offsets, iterations, pblock, vblock, seed,
+                             *c, static_cast<cudaStream_t>(stream), flags, shard_ptrs, shard_rows, n_shards);
+}
+
+extern "C" int povs_shuffle_sharded_v1(void* const* shard_ptrs, const int64_t* shard_rows, int32_t n_shards,
+                                       int32_t rank, int64_t row_bytes, const int64_t* offsets, int32_t n_offsets,
+                                       int32_t iterations, int32_t pblock, int32_t vblock, uint64_t seed,
+                                       void* const* peer_flags, uint32_t epoch_base, int32_t device, void* stream,
+                                       uint32_t flags)
+{
+    g_err[0] = '\0';
+    if (shard_ptrs == nullptr || shard_rows == nullptr || n_shards < 1 || n_shards > povs::MAX_SHARDS)
+        return fail(POVS_ERR_INVALID_ARGUMENT, "between 1 and %d shards are supported", povs::MAX_SHARDS);
+    if (rank < 0 || rank >= n_shards) return fail(POVS_ERR_INVALID_ARGUMENT, "rank %d out of range", rank);
+    if (peer_flags == nullptr) return fail(POVS_ERR_INVALID_ARGUMENT, "peer_flags is NULL");
+    for (int i = 0; i < n_shards; ++i)
+        if (peer_flags[i] == nullptr) return fail(POVS_ERR_INVALID_ARGUMENT, "flag array of rank %d is NULL", i);
+    const int64_t n_rows = sum_rows(shard_rows, n_shards);
+    int r = check_common(shard_ptrs[rank], n_rows, row_bytes, pblock, vblock, iterations);
+    if (r != POVS_OK) return r;
+    r = check_offsets(offsets, n_offsets, n_rows);
+    if (r != POVS_OK) return r;
+    DeviceGuard dg;
+    r = dg.enter(device);
+    if (r != POVS_OK) return r;
+    DeviceCtx* c = nullptr;
+    r = get_ctx(device, &c);
+    if (r != POVS_OK) return r;
+
+    IterParams base;
+    fill_geometry(base, shard_ptrs[rank], n_rows, row_bytes, pblock, vblock, c->status);
+    r = set_shards(base, shard_ptrs, shard_rows, n_shards);
+    if (r != POVS_OK) return r;
+    base.seed = seed;
+    base.rng_mode = (flags & POVS_FLAG_REFERENCE_RNG) ? povs::RNG_REFERENCE_CUDA : povs::RNG_UNIFORM;
+    base.n_offsets = n_offsets;
+    for (int i = 0; i < n_offsets; ++i) base.offsets[i] = offsets[i];
+    base.vb_begin = rank;
+    base.vb_step = n_shards;
+    Plan pl;
+    r = plan_launch(base, *c, false, pl);
+    if (r != POVS_OK) return r;
+
+    povs::PeerBarrierParams q{};
+    for (int i = 0; i < n_shards; ++i) q.flags[i] = static_cast<uint32_t*>(peer_flags[i]);
+    q.n_ranks = n_shards;
+    q.rank = rank;
+    q.status = c->status;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    auto barrier = [&](uint32_t epoch) -> int {
+        q.epoch = epoch;
+        void* args[] = {&q};
+        cudaError_t e = cudaLaunchKernel(reinterpret_cast<const void*>(povs::povs_peer_barrier_kernel), dim3(1),
+                                         dim3(32), args, 0, s);
+        return e == cudaSuccess ? POVS_OK : cuda_fail(e, "cudaLaunchKernel(barrier)");
+    };
+    // Every shard must be ready before any rank reads it, and every rank must have finished writing
+    // before anyone goes on: a barrier before the first iteration and after each one.
+    r = barrier(epoch_base + 1);
+    if (r != POVS_OK) return r;
+    for (int i = 0; i < iterations; ++i) {
+        IterParams p = base;
+        p.iteration = static_cast<uint32_t>(i);
+        r = launch_direct(pl, p, s);
+        if (r != POVS_OK) return r;
+        r = barrier(epoch_base + 2 + static_cast<uint32_t>(i));
+        if (r != POVS_OK) return r;
+    }
+    if (flags & POVS_FLAG_SYNC) {
+        POVS_CUDA_TRY(cudaStreamSynchronize(s));
+        int32_t st = 0;
+        r = read_status(*c, &st);
+        if (r != POVS_OK) return r;
+        if (st != 0) return fail(POVS_ERR_DEVICE_STATUS, "device status 0x%x after sharded shuffle", st);
+    }
+    return POVS_OK;
+}
+
+// ------------------------------------------------------------------------------------------
+// CUDA IPC: map another process's shard (or flag array) into this one.
+// ------------------------------------------------------------------------------------------
+
+namespace {
+using GetAddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+int address_range(const void* ptr, CUdeviceptr* base)
+{
+    static GetAddressRangeFn fn = nullptr;
+    static std::mutex mu;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (fn == nullptr) {
+            void* f = nullptr;
+            cudaDriverEntryPointQueryResult q;
+            cudaError_t e = cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q);
+            if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || f == nullptr)
+                return fail(POVS_ERR_CUDA, "cuMemGetAddressRange entry point unavailable");
+            fn = reinterpret_cast<GetAddressRangeFn>(f);
+        }
+    }
+    size_t size = 0;
+    if (fn(base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+        return fail(POVS_ERR_INVALID_ARGUMENT, "pointer %p is not device memory", ptr);
+    return POVS_OK;
+}
+} // namespace
+
+extern "C" int povs_ipc_export_v1(const void* ptr, int32_t device, void* handle_out, int64_t* offset_out)
+{
+    g_err[0] = '\0';
+    if (ptr == nullptr || handle_out == nullptr || offset_out == nullptr)
+        return fail(POVS_ERR_INVALID_ARGUMENT, "NULL argument");
+    DeviceGuard dg;
+    int r = dg.enter(device);
+    if (r != POVS_OK) return r;
+    CUdeviceptr base = 0;
+    r = address_range(ptr, &base);
+    if (r != POVS_OK) return r;
+    cudaIpcMemHandle_t h;
+    POVS_CUDA_TRY(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
+    std::memcpy(handle_out, &h, sizeof(h));
+    *offset_out = static_cast<int64_t>(reinterpret_cast<uintptr_t>(ptr) - static_cast<uintptr_t>(base));
+    return POVS_OK;
+}
+
+extern "C" int povs_ipc_import_v1(const void* handle, int64_t offset, int32_t device, void** ptr_out, void** base_out)
+{
+    g_err[0] = '\0';
+    if (handle == nullptr || ptr_out == nullptr || base_out == nullptr || offset < 0)
+        return fail(POVS_ERR_INVALID_ARGUMENT, "invalid argument");
+    DeviceGuard dg;
+    int r = dg.enter(device);
+    if (r != POVS_OK) return r;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    void* base = nullptr;
+    POVS_CUDA_TRY(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess));
+    *base_out = base;
+    *ptr_out = static_cast<uint8_t*>(base) + offset;
+    return POVS_OK;
+}
+
+extern "C" int povs_ipc_close_v1(void* base, int32_t device)
+{
+    g_err[0] = '\0';
+    DeviceGuard dg;
+    int r = dg.enter(device);
+    if (r != POVS_OK) return r;
+    POVS_CUDA_TRY(cudaIpcCloseMemHandle(base));
     return POVS_OK;
 }

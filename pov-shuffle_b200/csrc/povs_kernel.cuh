@@ -46,13 +46,17 @@ constexpr int MAX_INLINE_OFFSETS = 256;
 constexpr int MAX_VBLOCK = 32;
 constexpr int MAX_STAGES = 16;
 constexpr int MAX_SLOTS = 32;
+constexpr int MAX_SHARDS = 8;
 constexpr unsigned FULL_MASK = 0xffffffffu;
 
 // Device status bits (sticky, OR-ed into the per-device status word).
 enum : int {
     DEV_ERR_WAIT_TIMEOUT = 1, // an mbarrier wait gave up after the time limit
     DEV_ERR_BAD_INJECTED = 2, // an injected permutation entry was out of range (identity used instead)
+    DEV_ERR_PEER_TIMEOUT = 4, // a cross-GPU barrier gave up waiting for a peer
 };
+
+constexpr unsigned long long PEER_WAIT_LIMIT_NS = 20000000000ull; // 20 s for a peer GPU to reach the barrier
 
 constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull; // 2 s: far beyond any legitimate wait
 
@@ -84,6 +88,14 @@ struct IterParams {
     const int64_t* assign; // injected mode: [n_vblocks][V] pblock ids, padding < 0 or >= n_pblocks
     const int32_t* perms;  // injected mode: [n_vblocks][V*P] source slot of each destination slot
     int* status;
+    // The deck as a table of shards: rows [shard_start[s], shard_start[s+1]) live at shard_base[s]
+    // (one shard for a single-GPU deck; the shards of other GPUs are peer addresses).
+    int32_t n_shards;
+    uint8_t* shard_base[MAX_SHARDS];
+    int64_t shard_start[MAX_SHARDS + 1];
+    // vblocks handled by this launch: vb_begin, vb_begin + vb_step, ...
+    int64_t vb_begin;
+    int64_t vb_step;
     int64_t offsets[MAX_INLINE_OFFSETS];
 };
 
@@ -308,8 +320,10 @@ __device__ __forceinline__ void warp_make_perm_xorshift(const IterParams& p, uin
 // ---------------------------------------------------------------------------------------------
 
 struct StageMeta {
-    int64_t start[MAX_VBLOCK]; // storage row of the first row of the r-th ordered member
-    int32_t n_valid;           // valid rows (slots) of the unit
+    uint8_t* run_a[MAX_VBLOCK]; // address of the first row of the r-th ordered member
+    uint8_t* run_b[MAX_VBLOCK]; // address of its row n_a[r], where the run continues past a shard or deck end
+    int32_t n_a[MAX_VBLOCK];    // rows of the member stored contiguously from run_a
+    int32_t n_valid;            // valid rows (slots) of the unit
     int32_t pad;
 };
 
@@ -376,10 +390,12 @@ struct VecOf<1> {
     using T = uint8_t;
 };
 
-__device__ __forceinline__ int64_t slot_row(const StageMeta& m, int f, int pshift, int pmask, int64_t n_rows)
+// Address of the first byte of destination/source slot f's row.
+__device__ __forceinline__ uint8_t* slot_ptr(const StageMeta& m, int f, int pshift, int pmask, int64_t row_bytes)
 {
-    int64_t row = m.start[f >> pshift] + (f & pmask);
-    return row >= n_rows ? row - n_rows : row;
+    const int r = f >> pshift, i = f & pmask;
+    const int na = m.n_a[r];
+    return i < na ? m.run_a[r] + static_cast<int64_t>(i) * row_bytes : m.run_b[r] + static_cast<int64_t>(i - na) * row_bytes;
 }
 
 // Identity-order copy global -> stage of the unit's valid rows by one warp (plain loads).
@@ -393,8 +409,7 @@ __device__ __forceinline__ void lsu_load_unit(const IterParams& p, const StageMe
     const int n_valid = m.n_valid;
     if (cpr >= 32) {
         for (int f = 0; f < n_valid; ++f) {
-            const int64_t row = slot_row(m, f, p.pblock_shift, pmask, p.n_rows);
-            const T* src = reinterpret_cast<const T*>(p.data + row * p.row_bytes + col);
+            const T* src = reinterpret_cast<const T*>(slot_ptr(m, f, p.pblock_shift, pmask, p.row_bytes) + col);
             T* dst = reinterpret_cast<T*>(stage + static_cast<size_t>(f) * p.slab_bytes);
             for (int q = lane; q < cpr; q += 32) dst[q] = src[q];
         }
@@ -404,8 +419,7 @@ __device__ __forceinline__ void lsu_load_unit(const IterParams& p, const StageMe
         if (lrow < g) {
 #pragma unroll 4
             for (int f = lrow; f < n_valid; f += g) {
-                const int64_t row = slot_row(m, f, p.pblock_shift, pmask, p.n_rows);
-                const T* src = reinterpret_cast<const T*>(p.data + row * p.row_bytes + col);
+                const T* src = reinterpret_cast<const T*>(slot_ptr(m, f, p.pblock_shift, pmask, p.row_bytes) + col);
                 T* dst = reinterpret_cast<T*>(stage + static_cast<size_t>(f) * p.slab_bytes);
                 dst[lq] = src[lq];
             }
@@ -424,12 +438,10 @@ __device__ __forceinline__ void store_share(const IterParams& p, const StageMeta
     const int cpr = slen / W;
     const int pmask = p.pblock - 1;
     const int n_valid = m.n_valid;
-    uint8_t* const data = p.data + col;
     if (cpr >= 32) {
         for (int f = warp; f < n_valid; f += n_warps) {
-            const int64_t row = slot_row(m, f, p.pblock_shift, pmask, p.n_rows);
             const T* src = reinterpret_cast<const T*>(stage + static_cast<size_t>(perm[f]) * p.slab_bytes);
-            T* dst = reinterpret_cast<T*>(data + row * p.row_bytes);
+            T* dst = reinterpret_cast<T*>(slot_ptr(m, f, p.pblock_shift, pmask, p.row_bytes) + col);
 #pragma unroll 4
             for (int q = lane; q < cpr; q += 32) dst[q] = src[q];
         }
@@ -449,8 +461,7 @@ __device__ __forceinline__ void store_share(const IterParams& p, const StageMeta
                 const int f = (t + u * n_warps) * g + lrow;
                 ok[u] = f < n_valid;
                 const int fs = ok[u] ? f : 0;
-                const int64_t row = slot_row(m, fs, p.pblock_shift, pmask, p.n_rows);
-                dst[u] = reinterpret_cast<T*>(data + row * p.row_bytes) + lq;
+                dst[u] = reinterpret_cast<T*>(slot_ptr(m, fs, p.pblock_shift, pmask, p.row_bytes) + col) + lq;
                 v[u] = reinterpret_cast<const T*>(stage + static_cast<size_t>(perm[fs]) * p.slab_bytes)[lq];
             }
 #pragma unroll
@@ -460,9 +471,8 @@ __device__ __forceinline__ void store_share(const IterParams& p, const StageMeta
         for (; t < n_pass; t += n_warps) {
             const int f = t * g + lrow;
             if (f < n_valid) {
-                const int64_t row = slot_row(m, f, p.pblock_shift, pmask, p.n_rows);
                 const T v = reinterpret_cast<const T*>(stage + static_cast<size_t>(perm[f]) * p.slab_bytes)[lq];
-                reinterpret_cast<T*>(data + row * p.row_bytes)[lq] = v;
+                reinterpret_cast<T*>(slot_ptr(m, f, p.pblock_shift, pmask, p.row_bytes) + col)[lq] = v;
             }
         }
     }
@@ -502,8 +512,10 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
     mbar_fence_init();
     __syncthreads();
 
-    if (blockIdx.x >= p.n_vblocks) return;
-    const int64_t my_vblocks = (p.n_vblocks - blockIdx.x + gridDim.x - 1) / gridDim.x;
+    // This launch handles vblocks vb_begin + vb_step * k, k = 0 .. n_mine-1; CTA b takes k = b, b + grid, ...
+    const int64_t n_mine = p.vb_begin < p.n_vblocks ? (p.n_vblocks - p.vb_begin + p.vb_step - 1) / p.vb_step : 0;
+    if (blockIdx.x >= n_mine) return;
+    const int64_t my_vblocks = (n_mine - blockIdx.x + gridDim.x - 1) / gridDim.x;
     const int64_t n_units = my_vblocks * p.n_slabs;
     const int pmask = p.pblock - 1;
 
@@ -525,7 +537,7 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
         for (int64_t u = q; u < n_units; u += p.n_permuters) {
             const int k = static_cast<int>(u % kp);
             if (u >= kp && !warp_wait(&sm.pempty[k], static_cast<uint32_t>(((u / kp) - 1) & 1), p.status)) return;
-            const int64_t v = blockIdx.x + (u / p.n_slabs) * static_cast<int64_t>(gridDim.x);
+            const int64_t v = p.vb_begin + p.vb_step * (blockIdx.x + (u / p.n_slabs) * static_cast<int64_t>(gridDim.x));
             StageMeta& m = sm.meta[k];
             uint16_t* perm = sm.perm + static_cast<size_t>(k) * sm.perm_stride;
 
@@ -563,9 +575,16 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
             }
             const int n_valid = __reduce_add_sync(FULL_MASK, rows);
             if (lane < p.vblock && valid) {
+                // Storage run of the member: from row s0, split at most once where its shard (or the
+                // deck) ends; the continuation starts at row 0 of the next shard (shard 0 after the end).
                 int64_t s0 = mem * p.pblock + offset;
                 if (s0 >= p.n_rows) s0 -= p.n_rows;
-                m.start[rank] = s0;
+                int sa = 0;
+                while (sa + 1 < p.n_shards && s0 >= p.shard_start[sa + 1]) ++sa;
+                const int64_t until_end = p.shard_start[sa + 1] - s0;
+                m.run_a[rank] = p.shard_base[sa] + (s0 - p.shard_start[sa]) * p.row_bytes;
+                m.run_b[rank] = p.shard_base[sa + 1 == p.n_shards ? 0 : sa + 1];
+                m.n_a[rank] = until_end < rows ? static_cast<int>(until_end) : rows;
             }
             if (lane == 0) m.n_valid = n_valid;
             if constexpr (INJECTED) {
@@ -622,23 +641,23 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
                     const int rows_r = min(p.pblock, n_valid - first);
                     if (i0 >= rows_r) continue;
                     const int len = min(p.copy_rows, rows_r - i0);
-                    int64_t s0 = m.start[r] + i0;
-                    if (s0 >= p.n_rows) s0 -= p.n_rows;
-                    const int64_t until_end = p.n_rows - s0;
-                    const int n1 = until_end < len ? static_cast<int>(until_end) : len;
+                    const int na = m.n_a[r];
+                    // Rows [i0, i0+len) of the member: the part before n_a from run_a, the rest from run_b.
+                    const int n1 = i0 < na ? min(len, na - i0) : 0;
                     uint8_t* dst = stage + static_cast<size_t>(first + i0) * p.slab_bytes;
-                    bulk_load(dst, p.data + s0 * p.row_bytes, static_cast<uint32_t>(n1) * static_cast<uint32_t>(p.row_bytes),
-                              &sm.full[st]);
+                    if (n1 > 0)
+                        bulk_load(dst, m.run_a[r] + static_cast<int64_t>(i0) * p.row_bytes,
+                                  static_cast<uint32_t>(n1) * static_cast<uint32_t>(p.row_bytes), &sm.full[st]);
                     if (len > n1)
-                        bulk_load(dst + static_cast<size_t>(n1) * p.slab_bytes, p.data,
+                        bulk_load(dst + static_cast<size_t>(n1) * p.slab_bytes,
+                                  m.run_b[r] + static_cast<int64_t>(i0 + n1 - na) * p.row_bytes,
                                   static_cast<uint32_t>(len - n1) * static_cast<uint32_t>(p.row_bytes), &sm.full[st]);
                 }
             } else {
-                for (int f = lane; f < n_valid; f += 32) {
-                    const int64_t row = slot_row(m, f, p.pblock_shift, pmask, p.n_rows);
-                    bulk_load(stage + static_cast<size_t>(f) * p.slab_bytes, p.data + row * p.row_bytes + col,
-                              static_cast<uint32_t>(slen), &sm.full[st]);
-                }
+                for (int f = lane; f < n_valid; f += 32)
+                    bulk_load(stage + static_cast<size_t>(f) * p.slab_bytes,
+                              slot_ptr(m, f, p.pblock_shift, pmask, p.row_bytes) + col, static_cast<uint32_t>(slen),
+                              &sm.full[st]);
             }
         } else {
             switch (p.vec_bytes) {
@@ -710,6 +729,53 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
                 return;
             }
             last_issued = u;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Cross-GPU barrier between iterations of a sharded deck (one launch of one CTA per GPU).
+// Rank r writes `epoch` into slot r of every rank's flag array (system-scope release after a
+// system fence, so this GPU's earlier writes to peer shards are visible first), then waits until
+// every slot of its own array holds at least `epoch` (system-scope acquire).  The wait is bounded:
+// past PEER_WAIT_LIMIT_NS it records DEV_ERR_PEER_TIMEOUT and returns.
+// ---------------------------------------------------------------------------------------------
+
+struct PeerBarrierParams {
+    uint32_t* flags[MAX_SHARDS]; // flags[r]: rank r's array of n_ranks words, as mapped in this process
+    int32_t n_ranks;
+    int32_t rank;
+    uint32_t epoch;
+    int* status;
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v)
+{
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p)
+{
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__global__ void __launch_bounds__(32) povs_peer_barrier_kernel(const __grid_constant__ PeerBarrierParams q)
+{
+    const int t = threadIdx.x;
+    __threadfence_system();
+    __syncwarp();
+    if (t < q.n_ranks) st_release_sys(q.flags[t] + q.rank, q.epoch);
+    if (t < q.n_ranks) {
+        const uint32_t* mine = q.flags[q.rank] + t;
+        const unsigned long long t0 = global_timer_ns();
+        while (static_cast<int32_t>(ld_acquire_sys(mine) - q.epoch) < 0) {
+            __nanosleep(200);
+            if (global_timer_ns() - t0 > PEER_WAIT_LIMIT_NS) {
+                atomicOr(q.status, DEV_ERR_PEER_TIMEOUT);
+                return;
+            }
         }
     }
 }

@@ -2,8 +2,9 @@
 
 Public API kept from the reference: ``shuffle``, ``Options``, ``BuildParams``, ``get_build_params``,
 ``optim_options_for_dataset``.  Additions: ``apply_randomness`` (inject offsets, block assignments
-and per-vblock permutations, for bit-exact comparison with other implementations) and
-``check_device_status``.
+and per-vblock permutations, for bit-exact comparison with other implementations),
+``check_device_status``, and decks split into shards: ``shuffle_shards`` (one process) and
+``ShardedDeck`` (one process per GPU).
 """
 
 from __future__ import annotations
@@ -16,6 +17,7 @@ import torch as t
 from . import numpy as povs_numpy
 from . import torch as povs_torch
 from .common import get_build_params, get_int_seed
+from .distributed import ShardedDeck, shuffle_shards
 from .injection import apply_randomness
 from .types import BuildParams, Options
 
@@ -27,6 +29,8 @@ __all__ = [
     "optim_options_for_dataset",
     "apply_randomness",
     "check_device_status",
+    "shuffle_shards",
+    "ShardedDeck",
 ]
 
 

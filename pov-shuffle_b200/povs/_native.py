@@ -42,6 +42,18 @@ SIGNATURES: dict[str, tuple] = {
     "povs_version": (ctypes.c_int32, []),
     "povs_set_tuning_v1": (ctypes.c_int, [_c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32]),
     "povs_describe_plan_v1": (ctypes.c_int, [_c_vp, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _P_I64, _c_i32]),
+    "povs_shuffle_shards_v1": (
+        ctypes.c_int,
+        [_c_vp, _P_I64, _c_i32, _c_i64, _P_I64, _c_i32, _c_i32, _c_i32, _c_i32, _c_u64, _c_i32, _c_vp, _c_u32],
+    ),
+    "povs_shuffle_sharded_v1": (
+        ctypes.c_int,
+        [_c_vp, _P_I64, _c_i32, _c_i32, _c_i64, _P_I64, _c_i32, _c_i32, _c_i32, _c_i32, _c_u64, _c_vp, _c_u32, _c_i32,
+         _c_vp, _c_u32],
+    ),
+    "povs_ipc_export_v1": (ctypes.c_int, [_c_vp, _c_i32, _c_vp, _P_I64]),
+    "povs_ipc_import_v1": (ctypes.c_int, [_c_vp, _c_i64, _c_i32, ctypes.POINTER(_c_vp), ctypes.POINTER(_c_vp)]),
+    "povs_ipc_close_v1": (ctypes.c_int, [_c_vp, _c_i32]),
     "povs_apply_static_v1": (
         ctypes.c_int,
         [_c_vp, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _P_I64, _c_vp, _c_vp, _c_i32, _c_i32, _c_vp, _c_u32],
@@ -231,6 +243,79 @@ def apply_static(
         flags,
     )
     check(code, "povs_apply_static_v1")
+
+
+def _ptr_array(ptrs) -> ctypes.Array:
+    return (ctypes.c_void_p * len(ptrs))(*[ctypes.c_void_p(int(p)) for p in ptrs])
+
+
+def shuffle_shards(
+    shard_ptrs: list[int],
+    shard_rows: list[int],
+    row_bytes: int,
+    offsets: list[int],
+    iterations: int,
+    pblock: int,
+    vblock: int,
+    seed: int,
+    device: int,
+    flags: int = 0,
+) -> None:
+    """Shuffle a deck held in several shards addressable from ``device`` (one process)."""
+    lib = load()
+    rows = _i64_array(shard_rows)
+    code = lib.povs_shuffle_shards_v1(
+        _ptr_array(shard_ptrs), rows, len(shard_ptrs), row_bytes, _i64_array(offsets), len(offsets), iterations,
+        pblock, vblock, seed, device, ctypes.c_void_p(current_stream_handle(torch.device("cuda", device))), flags,
+    )
+    check(code, "povs_shuffle_shards_v1")
+
+
+def shuffle_sharded(
+    shard_ptrs: list[int],
+    shard_rows: list[int],
+    rank: int,
+    row_bytes: int,
+    offsets: list[int],
+    iterations: int,
+    pblock: int,
+    vblock: int,
+    seed: int,
+    flag_ptrs: list[int],
+    epoch_base: int,
+    device: int,
+    flags: int = 0,
+) -> None:
+    """This rank's part of a sharded shuffle (one process per GPU; see include/povs.h)."""
+    lib = load()
+    code = lib.povs_shuffle_sharded_v1(
+        _ptr_array(shard_ptrs), _i64_array(shard_rows), len(shard_ptrs), rank, row_bytes, _i64_array(offsets),
+        len(offsets), iterations, pblock, vblock, seed, _ptr_array(flag_ptrs), epoch_base & 0xFFFFFFFF, device,
+        ctypes.c_void_p(current_stream_handle(torch.device("cuda", device))), flags,
+    )
+    check(code, "povs_shuffle_sharded_v1")
+
+
+def ipc_export(ptr: int, device: int) -> tuple[bytes, int]:
+    """(64-byte IPC handle of the allocation holding ``ptr``, offset of ``ptr`` in it)."""
+    lib = load()
+    handle = (ctypes.c_uint8 * 64)()
+    offset = ctypes.c_int64(0)
+    check(lib.povs_ipc_export_v1(ctypes.c_void_p(ptr), device, handle, ctypes.byref(offset)), "povs_ipc_export_v1")
+    return bytes(handle), int(offset.value)
+
+
+def ipc_import(handle: bytes, offset: int, device: int) -> tuple[int, int]:
+    """Map a peer's exported allocation; returns (pointer at offset, mapping base to close)."""
+    lib = load()
+    h = (ctypes.c_uint8 * 64).from_buffer_copy(handle)
+    ptr, base = ctypes.c_void_p(), ctypes.c_void_p()
+    check(lib.povs_ipc_import_v1(h, offset, device, ctypes.byref(ptr), ctypes.byref(base)), "povs_ipc_import_v1")
+    return int(ptr.value), int(base.value)
+
+
+def ipc_close(base: int, device: int) -> None:
+    check(load().povs_ipc_close_v1(ctypes.c_void_p(base), device), "povs_ipc_close_v1")
 
 
 def device_status(device: int) -> int:

@@ -1,0 +1,192 @@
+"""Decks split along axis 0 into shards: several tensors in one process, or one shard per GPU
+process (torch.distributed, one process per GPU of a node).
+
+The result is the same permutation as ``povs.shuffle`` on the concatenated deck with the same
+seed: offsets, assignments and per-vblock permutations are functions of the seed and the global
+indices only.  Options are resolved and validated against the whole deck.
+
+One process per GPU (``ShardedDeck``): every rank maps the other ranks' shards with CUDA IPC at
+construction; a shuffle runs, on every rank, the vblocks ``rank, rank + world, ...``, reading
+member rows from local or peer memory over NVLink (bulk copies, no multicast) and writing them
+back with peer stores, with a device barrier between iterations.  The only collective on the data
+path is the broadcast of the seed from rank 0 (NCCL when the group's backend is NCCL).
+No reference counterpart: the reference has no multi-GPU code.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Any
+
+import torch
+import torch.distributed as dist
+
+from . import _native
+from .common import (
+    _validate_offsets,
+    _validate_pblock_size,
+    _validate_vblock_size,
+    choose_offsets,
+    get_int_seed,
+    randomness_flags,
+    seed_to_u64,
+)
+from .constants import MIN_VBLOCK_SIZE
+from .torch import _choose_pblock_size, _choose_thr_block_size, _validate_thr_block_size, options_is_complete
+from .types import Options
+
+MAX_SHARDS = 8
+
+
+def _row_layout(t: torch.Tensor) -> tuple[tuple[int, ...], torch.dtype]:
+    return tuple(t.shape[1:]), t.dtype
+
+
+def resolve_options(
+    n_rows: int, instance_size: int, dtype_bytes: int, device_id: int, options: Options | None
+) -> Options:
+    """Complete ``options`` for a deck of ``n_rows`` rows (same rules as ``optim_options_for_dataset``)."""
+    options = options or Options()
+    if options_is_complete(options):
+        return options
+    vblk = options.virtual_block_size or MIN_VBLOCK_SIZE
+    pblk = options.physical_block_size or _choose_pblock_size(instance_size, dtype_bytes, vblk, device_id)
+    return Options(
+        virtual_block_size=vblk,
+        physical_block_size=pblk,
+        offsets=choose_offsets(n_rows, instance_size, dtype_bytes, pblk),
+        gpu_thread_block_size=_choose_thr_block_size(instance_size, dtype_bytes, vblk, pblk, device_id),
+        randomness=options.randomness,
+    )
+
+
+def validate(n_rows: int, instance_size: int, dtype_bytes: int, iterations: int, options: Options,
+             shard_rows: list[int]) -> None:
+    """Preflight of a sharded deck (``AssertionError`` like the single-tensor path)."""
+    assert n_rows >= 2, f"dataset must have at least 2 instances, but has {n_rows}"
+    assert iterations >= 1, f"iterations ({iterations}) must be at least 1"
+    _validate_vblock_size(options.virtual_block_size)
+    pblock = _validate_pblock_size(options.physical_block_size)
+    _validate_offsets(options.offsets, n_rows, instance_size, dtype_bytes, pblock)
+    _validate_thr_block_size(options.gpu_thread_block_size, options.physical_block_size, options.virtual_block_size)
+    assert 1 <= len(shard_rows) <= MAX_SHARDS, f"between 1 and {MAX_SHARDS} shards are supported"
+    assert min(shard_rows) >= pblock, f"every shard needs at least physical_block_size ({pblock}) rows"
+
+
+def shuffle_shards(
+    shards: list[torch.Tensor],
+    iterations: int = 1,
+    options: Options | None = None,
+    seed: int | Any | None = None,
+) -> None:
+    """Shuffle, in place, the deck formed by concatenating ``shards`` along axis 0 (one process).
+
+    All shards must be contiguous, share the row layout and dtype, and be addressable from the
+    first shard's device (same device, or peers with peer access enabled).
+    """
+    assert shards, "at least one shard is required"
+    layout = _row_layout(shards[0])
+    for s in shards:
+        assert isinstance(s, torch.Tensor) and s.is_cuda and s.is_contiguous(), "shards must be contiguous CUDA tensors"
+        assert _row_layout(s) == layout, "shards must share the row shape and dtype"
+    dev = shards[0].device
+    instance_size = math.prod(layout[0]) if layout[0] else 1
+    dtype_bytes = shards[0].element_size()
+    rows = [int(s.shape[0]) for s in shards]
+    n_rows = sum(rows)
+    opts = resolve_options(n_rows, instance_size, dtype_bytes, dev.index, options)
+    validate(n_rows, instance_size, dtype_bytes, iterations, opts, rows)
+    row_bytes = instance_size * dtype_bytes
+    if row_bytes == 0:
+        return
+    _native.shuffle_shards(
+        [s.data_ptr() for s in shards], rows, row_bytes, list(opts.offsets), iterations, opts.physical_block_size,
+        opts.virtual_block_size, seed_to_u64(get_int_seed(seed)), dev.index, randomness_flags(opts),
+    )
+
+
+class ShardedDeck:
+    """This rank's shard of a deck split across the GPUs of one node (one process per GPU).
+
+    :param shard: this rank's rows, a contiguous CUDA tensor on this rank's GPU; every rank's shard
+                  has the same row shape and dtype, and at least ``physical_block_size`` rows.
+    :param group: process group (default: the world).  Construction is collective.
+    """
+
+    def __init__(self, shard: torch.Tensor, group: dist.ProcessGroup | None = None, native: Any = None):
+        self.native = native if native is not None else _native
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        assert self.world <= MAX_SHARDS, f"at most {MAX_SHARDS} ranks are supported"
+        assert shard.is_contiguous(), "Tensor must be contiguous"
+        self.shard = shard
+        self.device = shard.device
+        meta = [None] * self.world
+        dist.all_gather_object(meta, (int(shard.shape[0]), tuple(shard.shape[1:]), str(shard.dtype)), group=group)
+        assert all(m[1:] == meta[0][1:] for m in meta), f"shards differ in row shape or dtype: {meta}"
+        self.shard_rows = [m[0] for m in meta]
+        self.n_rows = sum(self.shard_rows)
+        self.instance_size = math.prod(shard.shape[1:]) if shard.ndim > 1 else 1
+        self.dtype_bytes = shard.element_size()
+        self.row_bytes = self.instance_size * self.dtype_bytes
+        # One uint32 barrier word per rank, zeroed; epochs only grow.
+        self.flags = torch.zeros(self.world, dtype=torch.int32, device=self.device)
+        self.epoch = 0
+        dev_index = self.device.index if self.device.type == "cuda" else -1
+        mine = (
+            self.native.ipc_export(shard.data_ptr(), dev_index),
+            self.native.ipc_export(self.flags.data_ptr(), dev_index),
+        )
+        handles = [None] * self.world
+        dist.all_gather_object(handles, mine, group=group)
+        self._mapped: list[int] = []
+        self.shard_ptrs: list[int] = []
+        self.flag_ptrs: list[int] = []
+        for r, ((sh, so), (fh, fo)) in enumerate(handles):
+            if r == self.rank:
+                self.shard_ptrs.append(shard.data_ptr())
+                self.flag_ptrs.append(self.flags.data_ptr())
+                continue
+            sp, sb = self.native.ipc_import(sh, so, dev_index)
+            fp, fb = self.native.ipc_import(fh, fo, dev_index)
+            self._mapped += [sb, fb]
+            self.shard_ptrs.append(sp)
+            self.flag_ptrs.append(fp)
+        dist.barrier(group=group)
+
+    def options(self, options: Options | None = None) -> Options:
+        """Options resolved against the whole deck."""
+        return resolve_options(self.n_rows, self.instance_size, self.dtype_bytes, self.device.index or 0, options)
+
+    def broadcast_seed(self, seed: int | Any | None) -> int:
+        """Rank 0's seed, on every rank (the one collective of a shuffle)."""
+        value = get_int_seed(seed) if self.rank == 0 else 0
+        t = torch.tensor([seed_to_u64(value) - (1 << 64) if seed_to_u64(value) >= (1 << 63) else seed_to_u64(value)],
+                         dtype=torch.int64, device=self.device)
+        dist.broadcast(t, src=dist.get_global_rank(self.group, 0) if self.group is not None else 0, group=self.group)
+        return int(t.item()) & 0xFFFF_FFFF_FFFF_FFFF
+
+    def shuffle(self, iterations: int = 1, options: Options | None = None, seed: int | Any | None = None,
+                flags: int = 0) -> None:
+        """Collective: every rank calls with the same iterations and options."""
+        opts = self.options(options)
+        validate(self.n_rows, self.instance_size, self.dtype_bytes, iterations, opts, self.shard_rows)
+        seed_u64 = self.broadcast_seed(seed)
+        if self.row_bytes == 0:
+            return
+        self.native.shuffle_sharded(
+            self.shard_ptrs, self.shard_rows, self.rank, self.row_bytes, list(opts.offsets), iterations,
+            opts.physical_block_size, opts.virtual_block_size, seed_u64, self.flag_ptrs, self.epoch,
+            self.device.index if self.device.type == "cuda" else -1, flags | randomness_flags(opts),
+        )
+        self.epoch += iterations + 1
+
+    def close(self) -> None:
+        """Unmap the peers' memory (collective: no rank may still be using this rank's mappings)."""
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for base in self._mapped:
+            self.native.ipc_close(base, self.device.index if self.device.type == "cuda" else -1)
+        self._mapped = []

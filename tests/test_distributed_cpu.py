@@ -1,0 +1,86 @@
+"""Host-side logic of the one-process-per-GPU sharded mode, with two gloo ranks on CPU.
+
+The native layer is replaced by a recorder, so no GPU is touched: the test checks the collective
+set-up (row table, handle exchange), that every rank uses rank 0's seed, the epoch bookkeeping of
+the device barrier, option resolution against the whole deck, and the preflight errors.
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+REPO = Path(__file__).resolve().parent.parent
+
+
+class RecordingNative:
+    def __init__(self):
+        self.calls = []
+
+    def ipc_export(self, ptr, device):
+        return (bytes([dist.get_rank()]) * 64, 0)
+
+    def ipc_import(self, handle, offset, device):
+        return (1000 + handle[0], 2000 + handle[0])
+
+    def ipc_close(self, base, device):
+        self.calls.append(("close", base))
+
+    def shuffle_sharded(self, *args):
+        self.calls.append(("shuffle", args))
+
+
+def _worker(rank: int, world: int, port: int, out_dir: str):
+    sys.path[:0] = [str(REPO), str(REPO / "pov-shuffle_b200")]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import povs
+    from povs.distributed import ShardedDeck
+
+    rows = [40, 56][rank]
+    shard = torch.zeros((rows, 4), dtype=torch.float32)
+    native = RecordingNative()
+    deck = ShardedDeck(shard, native=native)
+    opts = povs.Options(virtual_block_size=2, physical_block_size=16, offsets=[0, 4, 8], gpu_thread_block_size=32)
+    deck.shuffle(iterations=3, options=opts, seed=11 if rank == 0 else 999)
+    deck.shuffle(iterations=2, options=opts, seed=12 if rank == 0 else 5)
+    errors = []
+    try:
+        deck.shuffle(iterations=1, options=opts._replace(physical_block_size=64), seed=1)
+    except AssertionError as e:
+        errors.append(str(e))
+    deck.close()
+    calls = [c for c in native.calls if c[0] == "shuffle"]
+    result = {
+        "shard_rows": deck.shard_rows,
+        "n_rows": deck.n_rows,
+        "shard_ptrs": deck.shard_ptrs,
+        "seeds": [c[1][8] for c in calls],
+        "epochs": [c[1][10] for c in calls],
+        "ranks": [c[1][2] for c in calls],
+        "errors": errors,
+        "closed": len([c for c in native.calls if c[0] == "close"]),
+    }
+    torch.save(result, os.path.join(out_dir, f"rank{rank}.pt"))
+    dist.destroy_process_group()
+
+
+def test_two_rank_control_plane(tmp_path):
+    port = 29500 + (os.getpid() % 2000)
+    mp.start_processes(_worker, args=(2, port, str(tmp_path)), nprocs=2, start_method="spawn", join=True)
+    r0 = torch.load(tmp_path / "rank0.pt")
+    r1 = torch.load(tmp_path / "rank1.pt")
+    for r, res in enumerate((r0, r1)):
+        assert res["shard_rows"] == [40, 56] and res["n_rows"] == 96
+        assert res["ranks"] == [r, r]
+        assert res["epochs"] == [0, 4], "epoch base advances by iterations + 1 per shuffle"
+        assert res["seeds"] == [11, 12], "every rank uses rank 0's seed"
+        assert res["errors"] and "at least physical_block_size" in res["errors"][0]
+        assert res["closed"] == 2
+    assert r0["shard_ptrs"][1] == 1000 + 1 and r1["shard_ptrs"][0] == 1000 + 0

@@ -275,3 +275,41 @@ def test_full_size_cfg3_keeps_every_row():
     assert torch.equal(torch.sort(got_ids).values, ids)
     moved = (got_ids != ids).float().mean().item()
     assert moved > 0.99
+
+
+@pytest.mark.parametrize(
+    "rows,row_bytes,P,V,offsets,iterations",
+    [
+        ([1000, 1500, 2599], 256, 32, 4, [0, 1, 2, 5, 31], 3),
+        ([64, 64], 16, 16, 2, [0, 4, 12], 4),
+        ([3000, 37, 2000, 999], 24, 16, 8, [0, 1, 2], 2),
+        ([300, 500], 12288, 16, 2, [0, 1, 3], 2),
+        ([1 << 15] * 8, 128, 64, 4, list(range(16)), 2),
+    ],
+)
+@pytest.mark.parametrize("randomness", ["uniform", "reference_cuda"])
+def test_shards_match_the_concatenated_deck(oracle_api, rows, row_bytes, P, V, offsets, iterations, randomness):
+    """A deck split into shards (one process) shuffles exactly like the concatenated deck."""
+    n = sum(rows)
+    host = random_rows(n, row_bytes, seed=n)
+    shards, start = [], 0
+    for r in rows:
+        shards.append(torch.from_numpy(host[start:start + r].copy()).to(DEV))
+        start += r
+    opts = povs.Options(V, P, offsets, 32, randomness)
+    povs.shuffle_shards(shards, iterations=iterations, options=opts, seed=123)
+    torch.cuda.synchronize()
+    povs.check_device_status(0)
+    got = torch.cat(shards).cpu().numpy()
+    whole = torch.from_numpy(host.copy()).to(DEV)
+    povs.shuffle(whole, iterations=iterations, options=opts, seed=123)
+    assert np.array_equal(got, whole.cpu().numpy())
+    want = host.copy()
+    oracle_api.shuffle(want, iterations, P, V, offsets, 123, randomness)
+    assert np.array_equal(got, want)
+
+
+def test_shards_smaller_than_a_pblock_are_rejected():
+    shards = [torch.zeros((8, 4), device=DEV), torch.zeros((100, 4), device=DEV)]
+    with pytest.raises(AssertionError, match="at least physical_block_size"):
+        povs.shuffle_shards(shards, iterations=1, options=povs.Options(2, 16, [0, 4], 32), seed=1)
