@@ -187,7 +187,8 @@ def run_ours(args, w: dict, wname: str) -> None:
     N, P, V, iters = w["rows"], w["P"], w["V"], w["iterations"]
     elem = ELEM_BYTES[w["dtype"]]
     offsets = choose_offsets(N, R // elem, elem, P)
-    opts = povs.Options(virtual_block_size=V, physical_block_size=P, offsets=offsets, gpu_thread_block_size=64)
+    opts = povs.Options(virtual_block_size=V, physical_block_size=P, offsets=offsets,
+                        gpu_thread_block_size=min(64, V * P))
     stream = torch.cuda.current_stream(device)
     if world > 1:
         # One deck of N rows split into `world` shards; every rank times the same collective steps.
@@ -324,42 +325,49 @@ def run_e2e(args, w, deck, opts, offsets, iters, world, rank, local, stream, sha
 
     shard_bytes = deck.numel() * deck.element_size()
     total_bytes = w["rows"] * row_bytes_of(w)
+    n_host = 2 if world == 1 else 1  # one deck: two alternating host decks keep both PCIe directions busy
     # Decide once (rank 0, before anything is pinned) so that every rank takes the same steps.
-    ok = torch.tensor([1 if psutil.virtual_memory().available >= 1.5 * total_bytes else 0], device=deck.device)
+    ok = torch.tensor([1 if psutil.virtual_memory().available >= (n_host + 0.5) * total_bytes else 0],
+                      device=deck.device)
     if world > 1:
         dist.broadcast(ok, src=0)
     if not int(ok.item()):
-        return {"value": None, "unit": "GB/s", "skipped": "not enough host memory for a pinned copy of the deck"}
-    host = torch.empty(shard_bytes, dtype=torch.uint8, pin_memory=True)
+        return {"value": None, "unit": "GB/s", "skipped": "not enough host memory for pinned copies of the deck"}
     flat = deck.view(torch.uint8).reshape(-1)
-    host.copy_(flat)
+    hosts = []
+    for _ in range(n_host):
+        h = torch.empty(shard_bytes, dtype=torch.uint8, pin_memory=True)
+        h.copy_(flat)
+        hosts.append(h)
+    host = hosts[0]
     R = row_bytes_of(w)
     P, V = w["P"], w["V"]
-    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    e2e_steps = max(2, args.e2e_steps)
     if world == 1:
-        lib = _native.load()
-        offs = (ctypes.c_int64 * len(offsets))(*offsets)
+        # povs.shuffle_many's native call: deck k of the timed steps is host deck k % 2, staged through
+        # the resident deck buffer and a second device buffer; copies in and out overlap the work.
+        second = torch.empty_like(flat)
+        buffers = [flat, second]
 
-        def step(seed: int) -> None:
-            rc = lib.povs_shuffle_host_v1(ctypes.c_void_p(host.data_ptr()), ctypes.c_void_p(flat.data_ptr()),
-                                          deck.shape[0], R, offs, len(offsets), iters, P, V, seed, local,
-                                          ctypes.c_void_p(stream.cuda_stream), 0)
-            _native.check(rc, "povs_shuffle_host_v1")
-        path = "povs_shuffle_host_v1 (pinned host deck)"
+        def run_steps(n: int, seed: int) -> None:
+            _native.shuffle_host_batch([hosts[k % 2].data_ptr() for k in range(n)], buffers, deck.shape[0], R,
+                                       offsets, iters, P, V, [seed + k for k in range(n)])
+        path = "povs_shuffle_host_batch_v1 (povs.shuffle_many): 2 pinned host decks alternating, 2 device buffers"
     else:
-        def step(seed: int) -> None:
-            flat.copy_(host, non_blocking=True)
-            sharded.shuffle(iterations=iters, options=opts, seed=seed)
-            host.copy_(flat, non_blocking=True)
-            torch.cuda.current_stream().synchronize()
+        def run_steps(n: int, seed: int) -> None:
+            for k in range(n):
+                flat.copy_(host, non_blocking=True)
+                sharded.shuffle(iterations=iters, options=opts, seed=seed + k)
+                host.copy_(flat, non_blocking=True)
+                torch.cuda.current_stream().synchronize()
         path = "per rank: pinned host shard -> ShardedDeck.shuffle -> host"
-    step(7)
+
+    run_steps(2, 7)
     if world > 1:
         dist.barrier(device_ids=[local])
     e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record(stream)
-    for s in range(e2e_steps):
-        step(100 + s)
+    run_steps(e2e_steps, 100)
     e_stop.record(stream)
     torch.cuda.synchronize()
     e_ms = e_start.elapsed_time(e_stop)
@@ -458,7 +466,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="bf16_32GiB", choices=sorted(WORKLOADS))
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=8)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)

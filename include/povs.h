@@ -84,6 +84,21 @@ int povs_shuffle_host_v1(void* host_data, void* device_buffer, int64_t n_rows, i
                          int32_t vblock, uint64_t seed, int32_t device, void* stream, uint32_t flags);
 
 /*
+ * Shuffle n_decks host decks of the same shape through n_buffers device buffers (>= 2 for
+ * overlap; each at least n_rows * row_bytes bytes on `device`): deck d is copied into buffer
+ * d % n_buffers, shuffled with seeds[d], and copied back, on internal streams ordered by events so
+ * that deck d's copy back overlaps deck d+1's copy in and iterations (the PCIe directions and the
+ * SMs work at the same time).  Work queued on `stream` before the call is ordered first; the call
+ * returns when every deck is back in host memory.  A host deck may appear more than once in the
+ * list (it is then shuffled again, after its previous copy back).  Use pinned host memory for
+ * overlap.  Batched form of povs_shuffle_host_v1 (same reference route).
+ */
+int povs_shuffle_host_batch_v1(void* const* host_decks, int32_t n_decks, void* const* device_buffers, int32_t n_buffers,
+                               int64_t n_rows, int64_t row_bytes, const int64_t* offsets, int32_t n_offsets,
+                               int32_t iterations, int32_t pblock, int32_t vblock, const uint64_t* seeds,
+                               int32_t device, void* stream, uint32_t flags);
+
+/*
  * Apply externally supplied randomness (test hook for bit-exact parity with the
  * reference's CPU and CUDA paths).  For each iteration t:
  *   offsets_per_iter[t]        (host)   the iteration's row offset, in [0, n_rows)

@@ -517,6 +517,88 @@ extern "C" int povs_shuffle_host_v1(void* host_data, void* device_buffer, int64_
     return POVS_OK;
 }
 
+extern "C" int povs_shuffle_host_batch_v1(void* const* host_decks, int32_t n_decks, void* const* device_buffers,
+                                          int32_t n_buffers, int64_t n_rows, int64_t row_bytes,
+                                          const int64_t* offsets, int32_t n_offsets, int32_t iterations,
+                                          int32_t pblock, int32_t vblock, const uint64_t* seeds, int32_t device,
+                                          void* stream, uint32_t flags)
+{
+    g_err[0] = '\0';
+    if (host_decks == nullptr || device_buffers == nullptr || seeds == nullptr || n_decks < 0 || n_buffers < 1 ||
+        n_buffers > 8)
+        return fail(POVS_ERR_INVALID_ARGUMENT, "host_decks, seeds and 1..8 device_buffers are required");
+    for (int i = 0; i < n_decks; ++i)
+        if (host_decks[i] == nullptr) return fail(POVS_ERR_INVALID_ARGUMENT, "host deck %d is NULL", i);
+    for (int b = 0; b < n_buffers; ++b) {
+        int r = check_common(device_buffers[b], n_rows, row_bytes, pblock, vblock, iterations);
+        if (r != POVS_OK) return r;
+    }
+    int r = check_offsets(offsets, n_offsets, n_rows);
+    if (r != POVS_OK) return r;
+    DeviceGuard dg;
+    r = dg.enter(device);
+    if (r != POVS_OK) return r;
+    DeviceCtx* c = nullptr;
+    r = get_ctx(device, &c);
+    if (r != POVS_OK) return r;
+    if (n_decks == 0) return POVS_OK;
+
+    // Deck d uses buffer d % n_buffers.  Copies in, the iterations and copies out run on three
+    // streams ordered by events, so deck d's copy out overlaps deck d+1's copy in and iterations.
+    cudaStream_t user = static_cast<cudaStream_t>(stream);
+    cudaStream_t s_in = nullptr, s_out = nullptr, s_cmp = nullptr;
+    std::vector<cudaEvent_t> ev;
+    const size_t bytes = static_cast<size_t>(n_rows) * static_cast<size_t>(row_bytes);
+    auto cleanup = [&]() {
+        for (cudaEvent_t e : ev)
+            if (e) cudaEventDestroy(e);
+        if (s_in) cudaStreamDestroy(s_in);
+        if (s_out) cudaStreamDestroy(s_out);
+        if (s_cmp) cudaStreamDestroy(s_cmp);
+    };
+    auto run = [&]() -> int {
+        POVS_CUDA_TRY(cudaStreamCreateWithFlags(&s_in, cudaStreamNonBlocking));
+        POVS_CUDA_TRY(cudaStreamCreateWithFlags(&s_out, cudaStreamNonBlocking));
+        POVS_CUDA_TRY(cudaStreamCreateWithFlags(&s_cmp, cudaStreamNonBlocking));
+        ev.assign(static_cast<size_t>(3 * n_buffers + 1), nullptr);
+        for (auto& e : ev) POVS_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        cudaEvent_t start = ev[3 * n_buffers];
+        // Work already queued on the caller's stream (e.g. writes to the buffers) comes first.
+        POVS_CUDA_TRY(cudaEventRecord(start, user));
+        POVS_CUDA_TRY(cudaStreamWaitEvent(s_in, start, 0));
+        POVS_CUDA_TRY(cudaStreamWaitEvent(s_cmp, start, 0));
+        POVS_CUDA_TRY(cudaStreamWaitEvent(s_out, start, 0));
+        for (int d = 0; d < n_decks; ++d) {
+            const int b = d % n_buffers;
+            cudaEvent_t in_done = ev[3 * b], cmp_done = ev[3 * b + 1], out_done = ev[3 * b + 2];
+            if (d >= n_buffers) POVS_CUDA_TRY(cudaStreamWaitEvent(s_in, out_done, 0));
+            POVS_CUDA_TRY(cudaMemcpyAsync(device_buffers[b], host_decks[d], bytes, cudaMemcpyHostToDevice, s_in));
+            POVS_CUDA_TRY(cudaEventRecord(in_done, s_in));
+            POVS_CUDA_TRY(cudaStreamWaitEvent(s_cmp, in_done, 0));
+            int rc = shuffle_on_device(device_buffers[b], n_rows, row_bytes, offsets, n_offsets, iterations, pblock,
+                                       vblock, seeds[d], *c, s_cmp, flags & ~POVS_FLAG_SYNC);
+            if (rc != POVS_OK) return rc;
+            POVS_CUDA_TRY(cudaEventRecord(cmp_done, s_cmp));
+            POVS_CUDA_TRY(cudaStreamWaitEvent(s_out, cmp_done, 0));
+            POVS_CUDA_TRY(cudaMemcpyAsync(host_decks[d], device_buffers[b], bytes, cudaMemcpyDeviceToHost, s_out));
+            POVS_CUDA_TRY(cudaEventRecord(out_done, s_out));
+        }
+        POVS_CUDA_TRY(cudaStreamSynchronize(s_in));
+        POVS_CUDA_TRY(cudaStreamSynchronize(s_cmp));
+        POVS_CUDA_TRY(cudaStreamSynchronize(s_out));
+        if (flags & POVS_FLAG_SYNC) {
+            int32_t st = 0;
+            int rs = read_status(*c, &st);
+            if (rs != POVS_OK) return rs;
+            if (st != 0) return fail(POVS_ERR_DEVICE_STATUS, "device status 0x%x after shuffle", st);
+        }
+        return POVS_OK;
+    };
+    r = run();
+    cleanup();
+    return r;
+}
+
 extern "C" int povs_apply_v1(void* data, int64_t n_rows, int64_t row_bytes, int32_t pblock, int32_t vblock,
                              int32_t iterations, const int64_t* offsets_per_iter, const int64_t* assign,
                              const int32_t* perms, int32_t sort_members, int32_t device, void* stream)

@@ -320,10 +320,13 @@ __device__ __forceinline__ void warp_make_perm_xorshift(const IterParams& p, uin
 // ---------------------------------------------------------------------------------------------
 
 struct StageMeta {
-    uint8_t* run_a[MAX_VBLOCK]; // address of the first row of the r-th ordered member
-    uint8_t* run_b[MAX_VBLOCK]; // address of its row n_a[r], where the run continues past a shard or deck end
-    int32_t n_a[MAX_VBLOCK];    // rows of the member stored contiguously from run_a
-    int32_t n_valid;            // valid rows (slots) of the unit
+    // Row i of the r-th ordered member is at (i < n_a[r] ? run_a[r] : run_b[r]) + i * row_bytes:
+    // run_a is the member's first row, run_b is where the run continues past a shard or deck end,
+    // pre-shifted back by n_a rows so that both cases index with i (a select, not a branch).
+    uintptr_t run_a[MAX_VBLOCK];
+    uintptr_t run_b[MAX_VBLOCK];
+    int32_t n_a[MAX_VBLOCK]; // rows of the member stored contiguously from run_a
+    int32_t n_valid;         // valid rows (slots) of the unit
     int32_t pad;
 };
 
@@ -394,8 +397,9 @@ struct VecOf<1> {
 __device__ __forceinline__ uint8_t* slot_ptr(const StageMeta& m, int f, int pshift, int pmask, int64_t row_bytes)
 {
     const int r = f >> pshift, i = f & pmask;
-    const int na = m.n_a[r];
-    return i < na ? m.run_a[r] + static_cast<int64_t>(i) * row_bytes : m.run_b[r] + static_cast<int64_t>(i - na) * row_bytes;
+    const uintptr_t a = m.run_a[r], b = m.run_b[r];
+    const uintptr_t base = i < m.n_a[r] ? a : b;
+    return reinterpret_cast<uint8_t*>(base + static_cast<uintptr_t>(static_cast<int64_t>(i) * row_bytes));
 }
 
 // Identity-order copy global -> stage of the unit's valid rows by one warp (plain loads).
@@ -582,9 +586,11 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
                 int sa = 0;
                 while (sa + 1 < p.n_shards && s0 >= p.shard_start[sa + 1]) ++sa;
                 const int64_t until_end = p.shard_start[sa + 1] - s0;
-                m.run_a[rank] = p.shard_base[sa] + (s0 - p.shard_start[sa]) * p.row_bytes;
-                m.run_b[rank] = p.shard_base[sa + 1 == p.n_shards ? 0 : sa + 1];
-                m.n_a[rank] = until_end < rows ? static_cast<int>(until_end) : rows;
+                const int na = until_end < rows ? static_cast<int>(until_end) : rows;
+                m.run_a[rank] = reinterpret_cast<uintptr_t>(p.shard_base[sa] + (s0 - p.shard_start[sa]) * p.row_bytes);
+                m.run_b[rank] = reinterpret_cast<uintptr_t>(p.shard_base[sa + 1 == p.n_shards ? 0 : sa + 1]) -
+                                static_cast<uintptr_t>(static_cast<int64_t>(na) * p.row_bytes);
+                m.n_a[rank] = na;
             }
             if (lane == 0) m.n_valid = n_valid;
             if constexpr (INJECTED) {
@@ -646,11 +652,11 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
                     const int n1 = i0 < na ? min(len, na - i0) : 0;
                     uint8_t* dst = stage + static_cast<size_t>(first + i0) * p.slab_bytes;
                     if (n1 > 0)
-                        bulk_load(dst, m.run_a[r] + static_cast<int64_t>(i0) * p.row_bytes,
+                        bulk_load(dst, reinterpret_cast<const uint8_t*>(m.run_a[r] + static_cast<uintptr_t>(i0) * p.row_bytes),
                                   static_cast<uint32_t>(n1) * static_cast<uint32_t>(p.row_bytes), &sm.full[st]);
                     if (len > n1)
                         bulk_load(dst + static_cast<size_t>(n1) * p.slab_bytes,
-                                  m.run_b[r] + static_cast<int64_t>(i0 + n1 - na) * p.row_bytes,
+                                  reinterpret_cast<const uint8_t*>(m.run_b[r] + static_cast<uintptr_t>(i0 + n1) * p.row_bytes),
                                   static_cast<uint32_t>(len - n1) * static_cast<uint32_t>(p.row_bytes), &sm.full[st]);
                 }
             } else {

@@ -31,6 +31,7 @@ __all__ = [
     "check_device_status",
     "shuffle_shards",
     "ShardedDeck",
+    "shuffle_many",
 ]
 
 
@@ -61,6 +62,27 @@ def shuffle(
         return
 
     raise TypeError(f"Unsupported data type: {type(data)}")
+
+
+def shuffle_many(
+    decks: list,
+    iterations: int = 1,
+    options: Options | None = None,
+    seed: int | np.random.Generator | Any | None = None,
+) -> None:
+    """Shuffle several host decks (NumPy arrays or CPU tensors) of one shape, each in place.
+
+    The decks stream through the GPU with their host/device copies overlapped; deck ``d`` is
+    shuffled with seed ``seed + d``.  Addition to the reference API.
+    """
+    base = get_int_seed(seed)
+    arrays = [d.numpy() if isinstance(d, t.Tensor) else d for d in decks]
+    for d in decks:
+        if isinstance(d, t.Tensor):
+            assert d.get_device() == -1, "shuffle_many takes host decks; use shuffle for CUDA tensors"
+        elif not isinstance(d, np.ndarray):
+            raise TypeError(f"Unsupported data type: {type(d)}")
+    povs_numpy.shuffle_many(arrays, iterations, options, [base + i for i in range(len(arrays))])
 
 
 def optim_options_for_dataset(data: np.ndarray | t.Tensor, options: Options | None = None) -> Options:

@@ -35,6 +35,11 @@ SIGNATURES: dict[str, tuple] = {
         ctypes.c_int,
         [_c_vp, _c_vp, _c_i64, _c_i64, _P_I64, _c_i32, _c_i32, _c_i32, _c_i32, _c_u64, _c_i32, _c_vp, _c_u32],
     ),
+    "povs_shuffle_host_batch_v1": (
+        ctypes.c_int,
+        [_c_vp, _c_i32, _c_vp, _c_i32, _c_i64, _c_i64, _P_I64, _c_i32, _c_i32, _c_i32, _c_i32,
+         ctypes.POINTER(ctypes.c_uint64), _c_i32, _c_vp, _c_u32],
+    ),
     "povs_apply_v1": (ctypes.c_int, [_c_vp, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _P_I64, _c_vp, _c_vp, _c_i32, _c_i32, _c_vp]),
     "povs_device_status_v1": (ctypes.c_int, [_c_i32, _P_I32]),
     "povs_release_v1": (ctypes.c_int, []),
@@ -169,6 +174,31 @@ def shuffle_host(
         flags,
     )
     check(code, "povs_shuffle_host_v1")
+
+
+def shuffle_host_batch(
+    host_ptrs: list[int],
+    device_buffers: list[torch.Tensor],
+    n_rows: int,
+    row_bytes: int,
+    offsets: list[int],
+    iterations: int,
+    pblock: int,
+    vblock: int,
+    seeds: list[int],
+    flags: int = 0,
+) -> None:
+    """Pipelined shuffle of several host decks of one shape (blocks until all are back)."""
+    lib = load()
+    dev = device_buffers[0].device
+    hp = (ctypes.c_void_p * len(host_ptrs))(*[ctypes.c_void_p(p) for p in host_ptrs])
+    bp = (ctypes.c_void_p * len(device_buffers))(*[ctypes.c_void_p(b.data_ptr()) for b in device_buffers])
+    sd = (ctypes.c_uint64 * max(1, len(seeds)))(*[int(x) & 0xFFFF_FFFF_FFFF_FFFF for x in seeds])
+    code = lib.povs_shuffle_host_batch_v1(
+        hp, len(host_ptrs), bp, len(device_buffers), n_rows, row_bytes, _i64_array(offsets), len(offsets),
+        iterations, pblock, vblock, sd, dev.index, ctypes.c_void_p(current_stream_handle(dev)), flags,
+    )
+    check(code, "povs_shuffle_host_batch_v1")
 
 
 def apply(

@@ -102,3 +102,38 @@ def optim_options_for_dataset(data: np.ndarray, options: Options | None) -> Opti
 
 def preflight(data: np.ndarray, iterations: int, options: Options) -> None:
     povs_preflight(data, iterations, options)
+
+
+def shuffle_many(decks: list, iterations: int, options: Options | None, seeds: list[int], flags: int = 0) -> None:
+    """Shuffle several host decks of one shape in place, overlapping their copies with the GPU work.
+
+    Two device staging buffers are used, so deck d's copy back overlaps deck d+1's copy in and
+    iterations.  Arrays that are not C-contiguous are staged through contiguous copies.
+    """
+    if not decks:
+        return
+    first = decks[0]
+    for d in decks:
+        assert d.shape == first.shape and d.dtype == first.dtype, "all decks must share shape and dtype"
+    options = typing.cast(
+        "_HostOptions",
+        options if options_is_complete(options) else optim_options_for_dataset(first, options),
+    )
+    preflight(first, iterations, options)
+    row_bytes = get_instance_size(first) * get_dtype_bytes(first)
+    if row_bytes == 0:
+        return
+    if not torch.cuda.is_available():
+        raise RuntimeError("povs requires a CUDA device (B200, sm_100a); none is available")
+    hosts = [d if d.flags.c_contiguous else np.ascontiguousarray(d) for d in decks]
+    n_rows = first.shape[0]
+    device = torch.device("cuda", torch.cuda.current_device())
+    buffers = [torch.empty(n_rows * row_bytes, dtype=torch.uint8, device=device) for _ in range(min(2, len(decks)))]
+    _native.shuffle_host_batch(
+        [h.ctypes.data for h in hosts], buffers, n_rows, row_bytes, list(options.offsets), iterations,
+        options.physical_block_size, options.virtual_block_size, [seed_to_u64(s) for s in seeds],
+        flags | randomness_flags(options),
+    )
+    for d, h in zip(decks, hosts):
+        if h is not d:
+            d[...] = h

@@ -313,3 +313,23 @@ def test_shards_smaller_than_a_pblock_are_rejected():
     shards = [torch.zeros((8, 4), device=DEV), torch.zeros((100, 4), device=DEV)]
     with pytest.raises(AssertionError, match="at least physical_block_size"):
         povs.shuffle_shards(shards, iterations=1, options=povs.Options(2, 16, [0, 4], 32), seed=1)
+
+
+def test_shuffle_many_matches_one_deck_at_a_time():
+    """Pipelined host decks: deck d gets seed + d, exactly like separate host-route calls."""
+    rng = np.random.default_rng(4)
+    decks = [rng.standard_normal((20_000, 24)).astype(np.float32) for _ in range(3)]
+    expected = [d.copy() for d in decks]
+    opts = povs.Options(virtual_block_size=4, physical_block_size=16, offsets=[0, 1, 2, 3])
+    for i, e in enumerate(expected):
+        povs.shuffle(e, iterations=3, options=opts, seed=50 + i)
+    povs.shuffle_many(decks, iterations=3, options=opts, seed=50)
+    for d, e in zip(decks, expected):
+        assert np.array_equal(d, e)
+    # The same deck twice: shuffled again after its first copy back.
+    again = rng.standard_normal((20_000, 24)).astype(np.float32)
+    twice = again.copy()
+    povs.shuffle(twice, iterations=2, options=opts, seed=7)
+    povs.shuffle(twice, iterations=2, options=opts, seed=8)
+    povs.shuffle_many([again, again], iterations=2, options=opts, seed=7)
+    assert np.array_equal(again, twice)
