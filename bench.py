@@ -195,8 +195,9 @@ def run_ours(args, w: dict, wname: str) -> None:
         rows = [N // world] * world
         rows[-1] += N - sum(rows)
         deck = make_deck(w, device, rows=rows[rank], seed_offset=rank)
-        sharded = povs.ShardedDeck(deck)
-        plan = {"shard_rows": rows}
+        push = args.sharded_order == "push"
+        sharded = povs.ShardedDeck(deck, double_buffer=push)
+        plan = {"shard_rows": rows, "order": "double-buffered push" if push else "in place"}
 
         def step(seed: int) -> None:
             sharded.shuffle(iterations=iters, options=opts, seed=seed)
@@ -245,9 +246,11 @@ def run_ours(args, w: dict, wname: str) -> None:
     if world == 1:
         bound, achieved, roof_peak, roof_kind = "hbm", 2 * deck_bytes / per_launch_s / 1e9, peak, peak_kind
     else:
-        # Per GPU and iteration, (world-1)/world of the rows it reads come from peers and as many of
-        # the rows written into its shard come from peers: 2 (world-1)/world x shard bytes each way.
-        link_bytes = 2 * (world - 1) / world * (deck_bytes / world)
+        # Per GPU and iteration, bytes crossing NVLink in each direction.  Push order: (world-1)/world
+        # of the rows of its shard go to peers and as many arrive from them, once each.  In place:
+        # every remote member row is read and written back, twice that.
+        crossings = 1 if args.sharded_order == "push" else 2
+        link_bytes = crossings * (world - 1) / world * (deck_bytes / world)
         bound, achieved, roof_peak, roof_kind = "nvlink", link_bytes / per_launch_s / 1e9, NVLINK_PEER_GBS, (
             "measured peer copy per direction on this pool")
 
@@ -470,6 +473,8 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--sharded-order", default="push", choices=["push", "inplace"],
+                    help="with --gpus N > 1: double-buffered push order (default) or in place")
     ap.add_argument("--rows", type=int, default=None, help="override the workload's row count (profiling captures)")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -122,18 +122,26 @@ int povs_apply_v1(void* data, int64_t n_rows, int64_t row_bytes, int32_t pblock,
  * [sum(shard_rows[0..i-1]), +shard_rows[i]) live at shard_ptrs[i].  The result equals
  * povs_shuffle_v1 on the concatenated deck with the same seed.  Every shard must be addressable
  * from `device` (allocations on it, or peer memory with peer access enabled) and hold at least
- * `pblock` rows; the caller orders any writes to the shards before the call.
+ * `pblock` rows; the caller orders any writes to the shards before the call.  scratch_ptrs is NULL
+ * (in place: each vblock is read into shared memory and written back) or one buffer per shard of
+ * the same size (double-buffered "push" order: each pblock's rows are read once from the buffer
+ * holding them and stored straight into their destination slots in the other buffer; an odd
+ * number of iterations ends with a copy back).  Both orders give the same result.
  * No reference counterpart: the reference shuffles one contiguous tensor (src/povs/torch.py:20-50).
  */
-int povs_shuffle_shards_v1(void* const* shard_ptrs, const int64_t* shard_rows, int32_t n_shards, int64_t row_bytes,
-                           const int64_t* offsets, int32_t n_offsets, int32_t iterations, int32_t pblock,
-                           int32_t vblock, uint64_t seed, int32_t device, void* stream, uint32_t flags);
+int povs_shuffle_shards_v1(void* const* shard_ptrs, void* const* scratch_ptrs, const int64_t* shard_rows,
+                           int32_t n_shards, int64_t row_bytes, const int64_t* offsets, int32_t n_offsets,
+                           int32_t iterations, int32_t pblock, int32_t vblock, uint64_t seed, int32_t device,
+                           void* stream, uint32_t flags);
 
 /*
- * Sharded mode, one process per GPU: rank `rank` of n_shards shuffles the vblocks rank,
- * rank + n_shards, ... of the deck whose shards are shard_ptrs (this rank's own shard and the
- * peers' shards as mapped into this process with povs_ipc_import_v1).  Member rows are read with
- * bulk copies from local or peer memory (NVLink, no multicast) and written back with peer stores.
+ * Sharded mode, one process per GPU, over the deck whose shards are shard_ptrs (this rank's own
+ * shard and the peers' shards as mapped into this process with povs_ipc_import_v1).  With
+ * scratch_ptrs NULL, rank `rank` reads the vblocks rank, rank + n_shards, ... from local or peer
+ * memory (bulk copies over NVLink, no multicast) and writes them back with peer stores.  With one
+ * scratch buffer per shard (same sizes, mapped the same way), rank `rank` moves the pblocks stored
+ * in its own shard, reading them locally and storing every row straight into its destination slot
+ * in the other buffer, so a row crosses NVLink at most once per iteration (half the traffic).
  * A device barrier over the ranks' flag arrays (peer_flags[r]: n_shards uint32 words of rank r,
  * zero-initialised, mapped here) runs before the first iteration and after each one, with epochs
  * epoch_base + 1 .. epoch_base + iterations + 1; every rank must call with the same arguments
@@ -143,10 +151,11 @@ int povs_shuffle_shards_v1(void* const* shard_ptrs, const int64_t* shard_rows, i
  */
 #define POVS_MAX_SHARDS 8
 #define POVS_DEV_PEER_TIMEOUT 4 /* device status bit: a peer GPU did not reach the barrier in time */
-int povs_shuffle_sharded_v1(void* const* shard_ptrs, const int64_t* shard_rows, int32_t n_shards, int32_t rank,
-                            int64_t row_bytes, const int64_t* offsets, int32_t n_offsets, int32_t iterations,
-                            int32_t pblock, int32_t vblock, uint64_t seed, void* const* peer_flags,
-                            uint32_t epoch_base, int32_t device, void* stream, uint32_t flags);
+int povs_shuffle_sharded_v1(void* const* shard_ptrs, void* const* scratch_ptrs, const int64_t* shard_rows,
+                            int32_t n_shards, int32_t rank, int64_t row_bytes, const int64_t* offsets,
+                            int32_t n_offsets, int32_t iterations, int32_t pblock, int32_t vblock, uint64_t seed,
+                            void* const* peer_flags, uint32_t epoch_base, int32_t device, void* stream,
+                            uint32_t flags);
 
 /* CUDA IPC of device memory between the processes of a sharded deck (64-byte handles). */
 int povs_ipc_export_v1(const void* ptr, int32_t device, void* handle_out, int64_t* offset_out);

@@ -56,24 +56,26 @@ int ilog2(int64_t x)
 
 using KernelFn = void (*)(IterParams);
 
-template <bool INJ, bool BULK>
+template <bool INJ, bool BULK, bool PUSH>
 KernelFn kernel_for_epl(int epl)
 {
     switch (epl) {
-    case 1: return povs::povs_iteration_kernel<1, INJ, BULK>;
-    case 2: return povs::povs_iteration_kernel<2, INJ, BULK>;
-    case 4: return povs::povs_iteration_kernel<4, INJ, BULK>;
-    case 8: return povs::povs_iteration_kernel<8, INJ, BULK>;
-    case 16: return povs::povs_iteration_kernel<16, INJ, BULK>;
-    case 32: return povs::povs_iteration_kernel<32, INJ, BULK>;
+    case 1: return povs::povs_iteration_kernel<1, INJ, BULK, PUSH>;
+    case 2: return povs::povs_iteration_kernel<2, INJ, BULK, PUSH>;
+    case 4: return povs::povs_iteration_kernel<4, INJ, BULK, PUSH>;
+    case 8: return povs::povs_iteration_kernel<8, INJ, BULK, PUSH>;
+    case 16: return povs::povs_iteration_kernel<16, INJ, BULK, PUSH>;
+    case 32: return povs::povs_iteration_kernel<32, INJ, BULK, PUSH>;
     default: return nullptr;
     }
 }
 
-KernelFn select_kernel(int epl, bool injected, bool bulk)
+// Push mode exists for device randomness only.
+KernelFn select_kernel(int epl, bool injected, bool bulk, bool push = false)
 {
-    if (injected) return bulk ? kernel_for_epl<true, true>(epl) : kernel_for_epl<true, false>(epl);
-    return bulk ? kernel_for_epl<false, true>(epl) : kernel_for_epl<false, false>(epl);
+    if (push) return bulk ? kernel_for_epl<false, true, true>(epl) : kernel_for_epl<false, false, true>(epl);
+    if (injected) return bulk ? kernel_for_epl<true, true, false>(epl) : kernel_for_epl<true, false, false>(epl);
+    return bulk ? kernel_for_epl<false, true, false>(epl) : kernel_for_epl<false, false, false>(epl);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -157,10 +159,10 @@ struct DeviceGuard {
 
 int set_smem_attr_all(int smem)
 {
-    for (int inj = 0; inj < 2; ++inj)
+    for (int mode = 0; mode < 3; ++mode)
         for (int bulk = 0; bulk < 2; ++bulk)
             for (int epl = 1; epl <= 32; epl <<= 1) {
-                KernelFn fn = select_kernel(epl, inj != 0, bulk != 0);
+                KernelFn fn = select_kernel(epl, mode == 1, bulk != 0, mode == 2);
                 cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
                                                      cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
                 if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
@@ -204,7 +206,7 @@ struct Plan {
     bool bulk = false;
 };
 
-int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out)
+int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out, bool push = false)
 {
     Tuning t;
     {
@@ -220,14 +222,18 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out)
 
     uintptr_t addr = 0;
     for (int i = 0; i < p.n_shards; ++i) addr |= reinterpret_cast<uintptr_t>(p.shard_base[i]);
+    if (push)
+        for (int i = 0; i < p.n_shards; ++i) addr |= reinterpret_cast<uintptr_t>(p.dst_base[i]);
     int vec = 16;
     while (vec > 1 && ((p.row_bytes % vec) != 0 || (addr % vec) != 0)) vec >>= 1;
     const bool bulk = (vec == 16) && !t.force_plain;
 
     // Slab width: whole rows when a vblock fits a stage, else the widest 128-byte (or vec) multiple that does.
+    // A stage holds a unit's rows: the vblock's V*P rows in place, one member's P rows in push mode.
+    const int64_t stage_rows = push ? p.pblock : vp;
     int64_t slab = p.row_bytes;
-    if (vp * p.row_bytes > t.stage_cap) {
-        const int64_t fit = t.stage_cap / vp;
+    if (stage_rows * p.row_bytes > t.stage_cap) {
+        const int64_t fit = t.stage_cap / stage_rows;
         const int64_t gran = fit >= 128 ? 128 : vec;
         slab = std::max<int64_t>(vec, (fit / gran) * gran);
     }
@@ -237,9 +243,9 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out)
     // Permutation slots: the stages' worth plus room for every permuter to work ahead.
     auto slots_for = [&](int stages) { return std::min(povs::MAX_SLOTS, stages + 2 * permuters); };
     auto stages_for = [&](int64_t sl, int64_t& stage_bytes) {
-        stage_bytes = ((vp * sl + 127) / 128) * 128;
+        stage_bytes = ((stage_rows * sl + 127) / 128) * 128;
         const int kp = slots_for(max_stages);
-        const int64_t fixed = povs::cta_smem_bytes(0, 0, kp, static_cast<int>(vp));
+        const int64_t fixed = povs::cta_smem_bytes(0, 0, kp, static_cast<int>(vp), p.pblock);
         const int64_t per_stage = stage_bytes + 16;
         return static_cast<int>(std::min<int64_t>(max_stages, (c.smem_optin - fixed) / per_stage));
     };
@@ -255,11 +261,12 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out)
     const int kp = slots_for(nst);
 
     const int warps = movers + permuters;
-    const int cta_smem = povs::cta_smem_bytes(nst, static_cast<int>(stage_bytes), kp, static_cast<int>(vp));
+    const int cta_smem = povs::cta_smem_bytes(nst, static_cast<int>(stage_bytes), kp, static_cast<int>(vp), p.pblock);
     const int per_sm_by_smem = std::max(1, c.smem_per_sm / (cta_smem + 1024));
     const int per_sm_by_threads = std::max(1, c.max_threads_per_sm / (warps * 32));
     const int ctas_per_sm = std::min(per_sm_by_smem, per_sm_by_threads);
-    const int64_t n_mine = p.vb_begin < p.n_vblocks ? (p.n_vblocks - p.vb_begin + p.vb_step - 1) / p.vb_step : 0;
+    const int64_t n_mine = push ? (p.push_rank < 0 ? p.n_pblocks : p.n_pblocks / std::max(1, p.n_shards) + 1)
+                                : (p.vb_begin < p.n_vblocks ? (p.n_vblocks - p.vb_begin + p.vb_step - 1) / p.vb_step : 0);
     const int grid = static_cast<int>(std::min<int64_t>(std::max<int64_t>(1, n_mine), static_cast<int64_t>(c.sm_count) * ctas_per_sm));
 
     p.slab_bytes = static_cast<int32_t>(slab);
@@ -272,7 +279,7 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out)
     p.n_movers = movers;
     p.n_permuters = permuters;
 
-    out.fn = select_kernel(epl, injected, bulk);
+    out.fn = select_kernel(epl, injected, bulk, push);
     out.grid = std::max(1, grid);
     out.block = warps * 32;
     out.smem = cta_smem;
@@ -323,6 +330,7 @@ void fill_geometry(IterParams& p, void* data, int64_t n_rows, int64_t row_bytes,
     p.shard_start[1] = n_rows;
     p.vb_begin = 0;
     p.vb_step = 1;
+    p.push_rank = -1;
 }
 
 int launch_direct(const Plan& pl, const IterParams& p, cudaStream_t s)
@@ -855,8 +863,31 @@ extern "C" int povs_apply_static_v1(void* data, int64_t n_rows, int64_t row_byte
 // Decks split into shards.
 // ------------------------------------------------------------------------------------------
 
-extern "C" int povs_shuffle_shards_v1(void* const* shard_ptrs, const int64_t* shard_rows, int32_t n_shards,
-                                      int64_t row_bytes, const int64_t* offsets, int32_t n_offsets,
+namespace {
+
+// Points the launch at source and destination shard tables (push mode) for iteration `it`:
+// even iterations read the decks and write the scratch buffers, odd ones the other way round.
+void set_push_direction(IterParams& p, void* const* shard_ptrs, void* const* scratch_ptrs, int32_t n_shards, int it)
+{
+    for (int i = 0; i < n_shards; ++i) {
+        uint8_t* deck = static_cast<uint8_t*>(shard_ptrs[i]);
+        uint8_t* scratch = static_cast<uint8_t*>(scratch_ptrs[i]);
+        p.shard_base[i] = (it % 2 == 0) ? deck : scratch;
+        p.dst_base[i] = (it % 2 == 0) ? scratch : deck;
+    }
+}
+
+int check_scratch(void* const* scratch_ptrs, int32_t n_shards)
+{
+    for (int i = 0; i < n_shards; ++i)
+        if (scratch_ptrs[i] == nullptr) return fail(POVS_ERR_INVALID_ARGUMENT, "scratch buffer %d is NULL", i);
+    return POVS_OK;
+}
+
+} // namespace
+
+extern "C" int povs_shuffle_shards_v1(void* const* shard_ptrs, void* const* scratch_ptrs, const int64_t* shard_rows,
+                                      int32_t n_shards, int64_t row_bytes, const int64_t* offsets, int32_t n_offsets,
                                       int32_t iterations, int32_t pblock, int32_t vblock, uint64_t seed,
                                       int32_t device, void* stream, uint32_t flags)
 {
@@ -868,21 +899,59 @@ extern "C" int povs_shuffle_shards_v1(void* const* shard_ptrs, const int64_t* sh
     if (r != POVS_OK) return r;
     r = check_offsets(offsets, n_offsets, n_rows);
     if (r != POVS_OK) return r;
+    if (scratch_ptrs != nullptr && (r = check_scratch(scratch_ptrs, n_shards)) != POVS_OK) return r;
     DeviceGuard dg;
     r = dg.enter(device);
     if (r != POVS_OK) return r;
     DeviceCtx* c = nullptr;
     r = get_ctx(device, &c);
     if (r != POVS_OK) return r;
-    return shuffle_on_device(shard_ptrs[0], n_rows, row_bytes, offsets, n_offsets, iterations, pblock, vblock, seed,
-                             *c, static_cast<cudaStream_t>(stream), flags, shard_ptrs, shard_rows, n_shards);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (scratch_ptrs == nullptr)
+        return shuffle_on_device(shard_ptrs[0], n_rows, row_bytes, offsets, n_offsets, iterations, pblock, vblock, seed,
+                                 *c, s, flags, shard_ptrs, shard_rows, n_shards);
+
+    // Double-buffered (push) mode in one launch per iteration over every pblock.
+    IterParams base;
+    fill_geometry(base, shard_ptrs[0], n_rows, row_bytes, pblock, vblock, c->status);
+    r = set_shards(base, shard_ptrs, shard_rows, n_shards);
+    if (r != POVS_OK) return r;
+    base.seed = seed;
+    base.rng_mode = (flags & POVS_FLAG_REFERENCE_RNG) ? povs::RNG_REFERENCE_CUDA : povs::RNG_UNIFORM;
+    base.n_offsets = n_offsets;
+    for (int i = 0; i < n_offsets; ++i) base.offsets[i] = offsets[i];
+    base.push_rank = -1;
+    set_push_direction(base, shard_ptrs, scratch_ptrs, n_shards, 0);
+    Plan pl;
+    r = plan_launch(base, *c, false, pl, true);
+    if (r != POVS_OK) return r;
+    for (int i = 0; i < iterations; ++i) {
+        IterParams p = base;
+        p.iteration = static_cast<uint32_t>(i);
+        set_push_direction(p, shard_ptrs, scratch_ptrs, n_shards, i);
+        r = launch_direct(pl, p, s);
+        if (r != POVS_OK) return r;
+    }
+    if (iterations % 2 == 1)
+        for (int i = 0; i < n_shards; ++i)
+            POVS_CUDA_TRY(cudaMemcpyAsync(shard_ptrs[i], scratch_ptrs[i],
+                                          static_cast<size_t>(shard_rows[i]) * static_cast<size_t>(row_bytes),
+                                          cudaMemcpyDeviceToDevice, s));
+    if (flags & POVS_FLAG_SYNC) {
+        POVS_CUDA_TRY(cudaStreamSynchronize(s));
+        int32_t st = 0;
+        r = read_status(*c, &st);
+        if (r != POVS_OK) return r;
+        if (st != 0) return fail(POVS_ERR_DEVICE_STATUS, "device status 0x%x after shuffle", st);
+    }
+    return POVS_OK;
 }
 
-extern "C" int povs_shuffle_sharded_v1(void* const* shard_ptrs, const int64_t* shard_rows, int32_t n_shards,
-                                       int32_t rank, int64_t row_bytes, const int64_t* offsets, int32_t n_offsets,
-                                       int32_t iterations, int32_t pblock, int32_t vblock, uint64_t seed,
-                                       void* const* peer_flags, uint32_t epoch_base, int32_t device, void* stream,
-                                       uint32_t flags)
+extern "C" int povs_shuffle_sharded_v1(void* const* shard_ptrs, void* const* scratch_ptrs, const int64_t* shard_rows,
+                                       int32_t n_shards, int32_t rank, int64_t row_bytes, const int64_t* offsets,
+                                       int32_t n_offsets, int32_t iterations, int32_t pblock, int32_t vblock,
+                                       uint64_t seed, void* const* peer_flags, uint32_t epoch_base, int32_t device,
+                                       void* stream, uint32_t flags)
 {
     g_err[0] = '\0';
     if (shard_ptrs == nullptr || shard_rows == nullptr || n_shards < 1 || n_shards > povs::MAX_SHARDS)
@@ -896,6 +965,8 @@ extern "C" int povs_shuffle_sharded_v1(void* const* shard_ptrs, const int64_t* s
     if (r != POVS_OK) return r;
     r = check_offsets(offsets, n_offsets, n_rows);
     if (r != POVS_OK) return r;
+    const bool push = scratch_ptrs != nullptr;
+    if (push && (r = check_scratch(scratch_ptrs, n_shards)) != POVS_OK) return r;
     DeviceGuard dg;
     r = dg.enter(device);
     if (r != POVS_OK) return r;
@@ -911,10 +982,18 @@ extern "C" int povs_shuffle_sharded_v1(void* const* shard_ptrs, const int64_t* s
     base.rng_mode = (flags & POVS_FLAG_REFERENCE_RNG) ? povs::RNG_REFERENCE_CUDA : povs::RNG_UNIFORM;
     base.n_offsets = n_offsets;
     for (int i = 0; i < n_offsets; ++i) base.offsets[i] = offsets[i];
-    base.vb_begin = rank;
-    base.vb_step = n_shards;
+    if (push) {
+        // Every rank moves the rows of the pblocks stored in its own shard, each straight to its
+        // destination slot in the other buffer: a row crosses NVLink at most once.
+        base.push_rank = rank;
+        set_push_direction(base, shard_ptrs, scratch_ptrs, n_shards, 0);
+    } else {
+        // Every rank reads and writes back whole vblocks rank, rank + n_shards, ...
+        base.vb_begin = rank;
+        base.vb_step = n_shards;
+    }
     Plan pl;
-    r = plan_launch(base, *c, false, pl);
+    r = plan_launch(base, *c, false, pl, push);
     if (r != POVS_OK) return r;
 
     povs::PeerBarrierParams q{};
@@ -937,11 +1016,18 @@ extern "C" int povs_shuffle_sharded_v1(void* const* shard_ptrs, const int64_t* s
     for (int i = 0; i < iterations; ++i) {
         IterParams p = base;
         p.iteration = static_cast<uint32_t>(i);
+        if (push) set_push_direction(p, shard_ptrs, scratch_ptrs, n_shards, i);
         r = launch_direct(pl, p, s);
         if (r != POVS_OK) return r;
         r = barrier(epoch_base + 2 + static_cast<uint32_t>(i));
         if (r != POVS_OK) return r;
     }
+    // After an odd number of push iterations the rows are in the scratch buffers; every peer has
+    // finished writing this rank's scratch (last barrier), so copy it back locally.
+    if (push && iterations % 2 == 1)
+        POVS_CUDA_TRY(cudaMemcpyAsync(shard_ptrs[rank], scratch_ptrs[rank],
+                                      static_cast<size_t>(shard_rows[rank]) * static_cast<size_t>(row_bytes),
+                                      cudaMemcpyDeviceToDevice, s));
     if (flags & POVS_FLAG_SYNC) {
         POVS_CUDA_TRY(cudaStreamSynchronize(s));
         int32_t st = 0;

@@ -96,6 +96,10 @@ struct IterParams {
     // vblocks handled by this launch: vb_begin, vb_begin + vb_step, ...
     int64_t vb_begin;
     int64_t vb_step;
+    // Push mode (double-buffered decks): rows are read from shard_base and written to dst_base.
+    // A launch moves the pblocks whose first storage row lies in shard push_rank (all pblocks if -1).
+    uint8_t* dst_base[MAX_SHARDS];
+    int32_t push_rank;
     int64_t offsets[MAX_INLINE_OFFSETS];
 };
 
@@ -327,26 +331,34 @@ struct StageMeta {
     uintptr_t run_b[MAX_VBLOCK];
     int32_t n_a[MAX_VBLOCK]; // rows of the member stored contiguously from run_a
     int32_t n_valid;         // valid rows (slots) of the unit
+    int32_t rows_mine;       // push mode: rows of the unit's own member
+    // push mode: the unit's own member in the source buffer, same (a, b, n_a) convention
+    uintptr_t src_a;
+    uintptr_t src_b;
+    int32_t src_na;
     int32_t pad;
 };
 
 __host__ __device__ inline int perm_bytes_per_slot(int vp) { return ((vp * 2 + 15) / 16) * 16; }
 
-__host__ __device__ inline int cta_smem_bytes(int n_stages, int stage_bytes, int n_slots, int vp)
+__host__ __device__ inline int cta_smem_bytes(int n_stages, int stage_bytes, int n_slots, int vp, int pblock)
 {
-    return n_stages * stage_bytes + n_slots * (perm_bytes_per_slot(vp) + static_cast<int>(sizeof(StageMeta))) +
+    return n_stages * stage_bytes +
+           n_slots * (perm_bytes_per_slot(vp) + perm_bytes_per_slot(pblock) + static_cast<int>(sizeof(StageMeta))) +
            (2 * n_stages + 2 * n_slots) * 8;
 }
 
 struct CtaSmem {
     uint8_t* data;
-    uint16_t* perm;
+    uint16_t* perm;   // per slot: source slot of every destination slot (in-place mode, and scratch)
+    uint16_t* pos;    // per slot, push mode: destination slot of every row of the unit's own member
     StageMeta* meta;
     uint64_t* full;   // data stage loaded (TMA bytes + issuer arrivals)
     uint64_t* empty;  // data stage read by every mover thread
     uint64_t* pfull;  // permutation slot written by its permuter warp
     uint64_t* pempty; // permutation slot read by every mover thread
     int perm_stride;  // uint16 entries per slot
+    int pos_stride;
 };
 
 __device__ __forceinline__ CtaSmem carve_smem(uint8_t* base, const IterParams& p)
@@ -357,6 +369,9 @@ __device__ __forceinline__ CtaSmem carve_smem(uint8_t* base, const IterParams& p
     s.perm = reinterpret_cast<uint16_t*>(q);
     s.perm_stride = perm_bytes_per_slot(p.vp) / 2;
     q += static_cast<size_t>(p.n_slots) * perm_bytes_per_slot(p.vp);
+    s.pos = reinterpret_cast<uint16_t*>(q);
+    s.pos_stride = perm_bytes_per_slot(p.pblock) / 2;
+    q += static_cast<size_t>(p.n_slots) * perm_bytes_per_slot(p.pblock);
     s.meta = reinterpret_cast<StageMeta*>(q);
     q += static_cast<size_t>(p.n_slots) * sizeof(StageMeta);
     s.full = reinterpret_cast<uint64_t*>(q);
@@ -402,18 +417,30 @@ __device__ __forceinline__ uint8_t* slot_ptr(const StageMeta& m, int f, int pshi
     return reinterpret_cast<uint8_t*>(base + static_cast<uintptr_t>(static_cast<int64_t>(i) * row_bytes));
 }
 
-// Identity-order copy global -> stage of the unit's valid rows by one warp (plain loads).
-template <int W>
+// Push mode: row i of the unit's own member in the source buffer.
+__device__ __forceinline__ const uint8_t* src_row_ptr(const StageMeta& m, int i, int64_t row_bytes)
+{
+    const uintptr_t base = i < m.src_na ? m.src_a : m.src_b;
+    return reinterpret_cast<const uint8_t*>(base + static_cast<uintptr_t>(static_cast<int64_t>(i) * row_bytes));
+}
+
+// Identity-order copy global -> stage by one warp (plain loads): the unit's valid rows (in place),
+// or the rows of the unit's own member (push).
+template <int W, bool PUSH>
 __device__ __forceinline__ void lsu_load_unit(const IterParams& p, const StageMeta& m, uint8_t* stage, int64_t col,
                                               int slen, int lane)
 {
     using T = typename VecOf<W>::T;
     const int cpr = slen / W;
     const int pmask = p.pblock - 1;
-    const int n_valid = m.n_valid;
+    const int n = PUSH ? m.rows_mine : m.n_valid;
+    auto src_of = [&](int f) -> const uint8_t* {
+        if constexpr (PUSH) return src_row_ptr(m, f, p.row_bytes) + col;
+        else return slot_ptr(m, f, p.pblock_shift, pmask, p.row_bytes) + col;
+    };
     if (cpr >= 32) {
-        for (int f = 0; f < n_valid; ++f) {
-            const T* src = reinterpret_cast<const T*>(slot_ptr(m, f, p.pblock_shift, pmask, p.row_bytes) + col);
+        for (int f = 0; f < n; ++f) {
+            const T* src = reinterpret_cast<const T*>(src_of(f));
             T* dst = reinterpret_cast<T*>(stage + static_cast<size_t>(f) * p.slab_bytes);
             for (int q = lane; q < cpr; q += 32) dst[q] = src[q];
         }
@@ -422,8 +449,8 @@ __device__ __forceinline__ void lsu_load_unit(const IterParams& p, const StageMe
         const int lrow = lane / cpr, lq = lane - lrow * cpr;
         if (lrow < g) {
 #pragma unroll 4
-            for (int f = lrow; f < n_valid; f += g) {
-                const T* src = reinterpret_cast<const T*>(slot_ptr(m, f, p.pblock_shift, pmask, p.row_bytes) + col);
+            for (int f = lrow; f < n; f += g) {
+                const T* src = reinterpret_cast<const T*>(src_of(f));
                 T* dst = reinterpret_cast<T*>(stage + static_cast<size_t>(f) * p.slab_bytes);
                 dst[lq] = src[lq];
             }
@@ -431,21 +458,30 @@ __device__ __forceinline__ void lsu_load_unit(const IterParams& p, const StageMe
     }
 }
 
-// This warp's share of the permuted copy stage -> global: destination slot f receives source
-// slot perm[f].  Work items are interleaved over the W warps of the CTA.
-template <int W>
+// This warp's share of the copy stage -> global.  In place: destination slot f receives stage row
+// idx[f] (idx = the permutation).  Push: stage row f (the unit's own member) goes to destination
+// slot idx[f] (idx = the member's destination slots).  Work items are interleaved over the warps.
+template <int W, bool PUSH>
 __device__ __forceinline__ void store_share(const IterParams& p, const StageMeta& m, const uint8_t* stage,
-                                            const uint16_t* perm, int64_t col, int slen, int lane, int warp,
+                                            const uint16_t* idx, int64_t col, int slen, int lane, int warp,
                                             int n_warps)
 {
     using T = typename VecOf<W>::T;
     const int cpr = slen / W;
     const int pmask = p.pblock - 1;
-    const int n_valid = m.n_valid;
+    const int n = PUSH ? m.rows_mine : m.n_valid;
+    auto src_row = [&](int f) -> int {
+        if constexpr (PUSH) return f;
+        else return idx[f];
+    };
+    auto dst_slot = [&](int f) -> int {
+        if constexpr (PUSH) return idx[f];
+        else return f;
+    };
     if (cpr >= 32) {
-        for (int f = warp; f < n_valid; f += n_warps) {
-            const T* src = reinterpret_cast<const T*>(stage + static_cast<size_t>(perm[f]) * p.slab_bytes);
-            T* dst = reinterpret_cast<T*>(slot_ptr(m, f, p.pblock_shift, pmask, p.row_bytes) + col);
+        for (int f = warp; f < n; f += n_warps) {
+            const T* src = reinterpret_cast<const T*>(stage + static_cast<size_t>(src_row(f)) * p.slab_bytes);
+            T* dst = reinterpret_cast<T*>(slot_ptr(m, dst_slot(f), p.pblock_shift, pmask, p.row_bytes) + col);
 #pragma unroll 4
             for (int q = lane; q < cpr; q += 32) dst[q] = src[q];
         }
@@ -453,7 +489,7 @@ __device__ __forceinline__ void store_share(const IterParams& p, const StageMeta
         const int g = 32 / cpr;
         const int lrow = lane / cpr, lq = lane - lrow * cpr;
         if (lrow >= g) return;
-        const int n_pass = (n_valid + g - 1) / g;
+        const int n_pass = (n + g - 1) / g;
         constexpr int U = 4;
         int t = warp;
         for (; t + (U - 1) * n_warps < n_pass; t += U * n_warps) {
@@ -463,10 +499,10 @@ __device__ __forceinline__ void store_share(const IterParams& p, const StageMeta
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const int f = (t + u * n_warps) * g + lrow;
-                ok[u] = f < n_valid;
+                ok[u] = f < n;
                 const int fs = ok[u] ? f : 0;
-                dst[u] = reinterpret_cast<T*>(slot_ptr(m, fs, p.pblock_shift, pmask, p.row_bytes) + col) + lq;
-                v[u] = reinterpret_cast<const T*>(stage + static_cast<size_t>(perm[fs]) * p.slab_bytes)[lq];
+                dst[u] = reinterpret_cast<T*>(slot_ptr(m, dst_slot(fs), p.pblock_shift, pmask, p.row_bytes) + col) + lq;
+                v[u] = reinterpret_cast<const T*>(stage + static_cast<size_t>(src_row(fs)) * p.slab_bytes)[lq];
             }
 #pragma unroll
             for (int u = 0; u < U; ++u)
@@ -474,11 +510,51 @@ __device__ __forceinline__ void store_share(const IterParams& p, const StageMeta
         }
         for (; t < n_pass; t += n_warps) {
             const int f = t * g + lrow;
-            if (f < n_valid) {
-                const T v = reinterpret_cast<const T*>(stage + static_cast<size_t>(perm[f]) * p.slab_bytes)[lq];
-                reinterpret_cast<T*>(slot_ptr(m, f, p.pblock_shift, pmask, p.row_bytes) + col)[lq] = v;
+            if (f < n) {
+                const T v = reinterpret_cast<const T*>(stage + static_cast<size_t>(src_row(f)) * p.slab_bytes)[lq];
+                reinterpret_cast<T*>(slot_ptr(m, dst_slot(f), p.pblock_shift, pmask, p.row_bytes) + col)[lq] = v;
             }
         }
+    }
+}
+
+// Push mode: the destination slot of every element of the unit's own member (elements
+// first .. first+count-1 of the vblock) under the uniform permutation; same sort as warp_make_perm.
+template <int EPL>
+__device__ __forceinline__ void warp_make_pos(const IterParams& p, uint64_t vblock, int n_valid, int first, int count,
+                                              uint16_t* pos, int lane)
+{
+    uint64_t x[EPL];
+    if constexpr (EPL >= 4) {
+#pragma unroll
+        for (int q = 0; q < EPL / 4; ++q) {
+            const uint32_t quad = static_cast<uint32_t>((lane * EPL) / 4 + q);
+            const U32x4 k = perm_key4(p.seed, p.iteration, vblock, quad);
+            const uint32_t w[4] = {k.x, k.y, k.z, k.w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const uint32_t e = quad * 4u + t;
+                x[4 * q + t] =
+                    (static_cast<int>(e) < n_valid) ? ((static_cast<uint64_t>(w[t]) << 32) | e) : ~uint64_t{0};
+            }
+        }
+    } else {
+        const uint32_t e0 = static_cast<uint32_t>(lane * EPL);
+        const U32x4 k = perm_key4(p.seed, p.iteration, vblock, e0 >> 2);
+#pragma unroll
+        for (int r = 0; r < EPL; ++r) {
+            const uint32_t e = e0 + r;
+            x[r] = (static_cast<int>(e) < n_valid)
+                       ? ((static_cast<uint64_t>(pick_word(k, static_cast<int>(e & 3u))) << 32) | e)
+                       : ~uint64_t{0};
+        }
+    }
+    warp_bitonic_sort<EPL>(x, lane);
+#pragma unroll
+    for (int r = 0; r < EPL; ++r) {
+        const int f = lane * EPL + r;
+        const int e = static_cast<int>(x[r] & 0xffffu) - first;
+        if (f < n_valid && e >= 0 && e < count) pos[e] = static_cast<uint16_t>(f);
     }
 }
 
@@ -493,9 +569,55 @@ __device__ __forceinline__ void store_share(const IterParams& p, const StageMeta
 // into slot u % KP, running up to KP units ahead of the movers.
 // ---------------------------------------------------------------------------------------------
 
-template <int EPL, bool INJECTED, bool BULK>
+// Push-mode work list: the pblocks whose first storage row lies in shard `push_rank` (all pblocks
+// when push_rank < 0).  Logical row L is stored at (L + offset) mod N, so these are the pblocks
+// whose first logical row falls in the shard's rows shifted back by the offset: at most two ranges.
+struct PushList {
+    int64_t first, cnt1, cnt2; // [first, first + cnt1) then [0, cnt2)
+    __device__ __forceinline__ int64_t size() const { return cnt1 + cnt2; }
+    __device__ __forceinline__ int64_t at(int64_t k) const { return k < cnt1 ? first + k : k - cnt1; }
+};
+
+__device__ __forceinline__ PushList push_list(const IterParams& p, int64_t offset)
+{
+    PushList l{0, p.n_pblocks, 0};
+    if (p.push_rank < 0) return l;
+    const int64_t s0 = p.shard_start[p.push_rank];
+    const int64_t len = p.shard_start[p.push_rank + 1] - s0;
+    int64_t ls = s0 - offset;
+    if (ls < 0) ls += p.n_rows;
+    const int64_t P = p.pblock;
+    l.first = (ls + P - 1) / P;
+    const int64_t hi = ls + len;
+    if (hi <= p.n_rows) {
+        const int64_t end = min(p.n_pblocks, (hi + P - 1) / P);
+        l.cnt1 = end > l.first ? end - l.first : 0;
+        l.cnt2 = 0;
+    } else {
+        l.cnt1 = p.n_pblocks > l.first ? p.n_pblocks - l.first : 0;
+        l.cnt2 = min(p.n_pblocks, (hi - p.n_rows + P - 1) / P);
+    }
+    return l;
+}
+
+// Storage run (a, pre-shifted b, n_a) of `rows` rows starting at storage row s0 in a table of shards.
+__device__ __forceinline__ void locate_run(const IterParams& p, uint8_t* const* base, int64_t s0, int rows,
+                                           uintptr_t& run_a, uintptr_t& run_b, int32_t& n_a)
+{
+    int sa = 0;
+    while (sa + 1 < p.n_shards && s0 >= p.shard_start[sa + 1]) ++sa;
+    const int64_t until_end = p.shard_start[sa + 1] - s0;
+    const int na = until_end < rows ? static_cast<int>(until_end) : rows;
+    run_a = reinterpret_cast<uintptr_t>(base[sa] + (s0 - p.shard_start[sa]) * p.row_bytes);
+    run_b = reinterpret_cast<uintptr_t>(base[sa + 1 == p.n_shards ? 0 : sa + 1]) -
+            static_cast<uintptr_t>(static_cast<int64_t>(na) * p.row_bytes);
+    n_a = na;
+}
+
+template <int EPL, bool INJECTED, bool BULK, bool PUSH>
 __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_constant__ IterParams p)
 {
+    static_assert(!(PUSH && INJECTED), "push mode draws its randomness on the device");
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -516,21 +638,31 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
     mbar_fence_init();
     __syncthreads();
 
-    // This launch handles vblocks vb_begin + vb_step * k, k = 0 .. n_mine-1; CTA b takes k = b, b + grid, ...
-    const int64_t n_mine = p.vb_begin < p.n_vblocks ? (p.n_vblocks - p.vb_begin + p.vb_step - 1) / p.vb_step : 0;
-    if (blockIdx.x >= n_mine) return;
-    const int64_t my_vblocks = (n_mine - blockIdx.x + gridDim.x - 1) / gridDim.x;
-    const int64_t n_units = my_vblocks * p.n_slabs;
+    // Iteration-wide randomness (identical in every thread).
+    int64_t offset;
+    if constexpr (INJECTED) {
+        offset = p.offset;
+    } else {
+        offset = p.offsets[reduce_range(offset_draw(p.seed, p.iteration), static_cast<uint32_t>(p.n_offsets))];
+    }
+
+    // Work list.  In place: vblocks vb_begin + vb_step * k, k < n_list.  Push: the pblocks of
+    // push_list.  CTA b takes list entries b, b + grid, ...; a unit is (entry, slab).
+    int64_t n_list;
+    PushList plist{};
+    if constexpr (PUSH) {
+        plist = push_list(p, offset);
+        n_list = plist.size();
+    } else {
+        n_list = p.vb_begin < p.n_vblocks ? (p.n_vblocks - p.vb_begin + p.vb_step - 1) / p.vb_step : 0;
+    }
+    if (blockIdx.x >= n_list) return;
+    const int64_t my_entries = (n_list - blockIdx.x + gridDim.x - 1) / gridDim.x;
+    const int64_t n_units = my_entries * p.n_slabs;
     const int pmask = p.pblock - 1;
 
     if (warp >= n_movers) {
         // ------------------------------------------------------------------ permuter warps
-        int64_t offset;
-        if constexpr (INJECTED) {
-            offset = p.offset;
-        } else {
-            offset = p.offsets[reduce_range(offset_draw(p.seed, p.iteration), static_cast<uint32_t>(p.n_offsets))];
-        }
         Feistel pi;
         // Uniform mode maps all n_v*V slots (padding ids anywhere); the reference-CUDA mode maps
         // slots [0, n_p) and leaves the padding in the last slots, as the reference does.
@@ -541,7 +673,18 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
         for (int64_t u = q; u < n_units; u += p.n_permuters) {
             const int k = static_cast<int>(u % kp);
             if (u >= kp && !warp_wait(&sm.pempty[k], static_cast<uint32_t>(((u / kp) - 1) & 1), p.status)) return;
-            const int64_t v = p.vb_begin + p.vb_step * (blockIdx.x + (u / p.n_slabs) * static_cast<int64_t>(gridDim.x));
+            const int64_t entry = blockIdx.x + (u / p.n_slabs) * static_cast<int64_t>(gridDim.x);
+            int64_t v;
+            int64_t own = -1;  // push: the unit's own pblock
+            int own_lane = 0;  // push: its slot within the vblock
+            if constexpr (PUSH) {
+                own = plist.at(entry);
+                const int64_t slot_of_own = static_cast<int64_t>(pi.inverse(static_cast<uint64_t>(own)));
+                v = slot_of_own / p.vblock;
+                own_lane = static_cast<int>(slot_of_own - v * p.vblock);
+            } else {
+                v = p.vb_begin + p.vb_step * entry;
+            }
             StageMeta& m = sm.meta[k];
             uint16_t* perm = sm.perm + static_cast<size_t>(k) * sm.perm_stride;
 
@@ -579,18 +722,15 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
             }
             const int n_valid = __reduce_add_sync(FULL_MASK, rows);
             if (lane < p.vblock && valid) {
-                // Storage run of the member: from row s0, split at most once where its shard (or the
-                // deck) ends; the continuation starts at row 0 of the next shard (shard 0 after the end).
+                // Storage run of the member (in the destination buffer in push mode): from row s0, split
+                // at most once where its shard (or the deck) ends.
                 int64_t s0 = mem * p.pblock + offset;
                 if (s0 >= p.n_rows) s0 -= p.n_rows;
-                int sa = 0;
-                while (sa + 1 < p.n_shards && s0 >= p.shard_start[sa + 1]) ++sa;
-                const int64_t until_end = p.shard_start[sa + 1] - s0;
-                const int na = until_end < rows ? static_cast<int>(until_end) : rows;
-                m.run_a[rank] = reinterpret_cast<uintptr_t>(p.shard_base[sa] + (s0 - p.shard_start[sa]) * p.row_bytes);
-                m.run_b[rank] = reinterpret_cast<uintptr_t>(p.shard_base[sa + 1 == p.n_shards ? 0 : sa + 1]) -
-                                static_cast<uintptr_t>(static_cast<int64_t>(na) * p.row_bytes);
-                m.n_a[rank] = na;
+                locate_run(p, PUSH ? p.dst_base : p.shard_base, s0, rows, m.run_a[rank], m.run_b[rank], m.n_a[rank]);
+                if (PUSH && lane == own_lane) {
+                    locate_run(p, p.shard_base, s0, rows, m.src_a, m.src_b, m.src_na);
+                    m.rows_mine = rows;
+                }
             }
             if (lane == 0) m.n_valid = n_valid;
             if constexpr (INJECTED) {
@@ -602,6 +742,20 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
                         sf = f;
                     }
                     perm[f] = static_cast<uint16_t>(sf);
+                }
+            } else if constexpr (PUSH) {
+                const int own_rank = __shfl_sync(FULL_MASK, rank, own_lane);
+                const int own_rows = __shfl_sync(FULL_MASK, rows, own_lane);
+                const int first = own_rank << p.pblock_shift;
+                uint16_t* pos = sm.pos + static_cast<size_t>(k) * sm.pos_stride;
+                if (ref_rng) {
+                    warp_make_perm_xorshift(p, static_cast<uint64_t>(v), n_valid, perm, lane);
+                    for (int f = lane; f < n_valid; f += 32) {
+                        const int e = static_cast<int>(perm[f]) - first;
+                        if (e >= 0 && e < own_rows) pos[e] = static_cast<uint16_t>(f);
+                    }
+                } else {
+                    warp_make_pos<EPL>(p, static_cast<uint64_t>(v), n_valid, first, own_rows, pos, lane);
                 }
             } else {
                 if (ref_rng)
@@ -627,51 +781,55 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
             return false;
         fence_proxy_async_smem();
         const StageMeta& m = sm.meta[k];
-        const int n_valid = m.n_valid;
+        const int n_load = PUSH ? m.rows_mine : m.n_valid;
         const int slab = static_cast<int>(u % p.n_slabs);
         const int64_t col = static_cast<int64_t>(slab) * p.slab_bytes;
         const int slen = static_cast<int>(min(static_cast<int64_t>(p.slab_bytes), p.row_bytes - col));
         uint8_t* stage = sm.data + static_cast<size_t>(st) * p.stage_bytes;
         if constexpr (BULK) {
-            if (lane == 0) mbar_expect_tx(&sm.full[st], static_cast<uint32_t>(n_valid) * static_cast<uint32_t>(slen));
+            if (lane == 0) mbar_expect_tx(&sm.full[st], static_cast<uint32_t>(n_load) * static_cast<uint32_t>(slen));
             __syncwarp();
             if (p.n_slabs == 1) {
-                // Whole rows: each member is <= 2 contiguous runs (split where the offset wraps),
-                // copied in pieces of at most copy_rows rows; pieces are spread over the lanes.
+                // Whole rows: each member is <= 2 contiguous runs (split where its shard or the deck
+                // ends), copied in pieces of at most copy_rows rows; pieces are spread over the lanes.
                 const int pieces_per_member = (p.pblock + p.copy_rows - 1) / p.copy_rows;
-                const int n_mem = (n_valid + pmask) >> p.pblock_shift;
+                const int n_mem = PUSH ? 1 : (n_load + pmask) >> p.pblock_shift;
                 for (int q = lane; q < n_mem * pieces_per_member; q += 32) {
                     const int r = q / pieces_per_member;
                     const int i0 = (q - r * pieces_per_member) * p.copy_rows;
                     const int first = r << p.pblock_shift;
-                    const int rows_r = min(p.pblock, n_valid - first);
+                    const int rows_r = min(p.pblock, n_load - first);
                     if (i0 >= rows_r) continue;
                     const int len = min(p.copy_rows, rows_r - i0);
-                    const int na = m.n_a[r];
-                    // Rows [i0, i0+len) of the member: the part before n_a from run_a, the rest from run_b.
+                    const int na = PUSH ? m.src_na : m.n_a[r];
+                    const uintptr_t ra = PUSH ? m.src_a : m.run_a[r];
+                    const uintptr_t rb = PUSH ? m.src_b : m.run_b[r];
+                    // Rows [i0, i0+len) of the member: the part before n_a from run a, the rest from run b.
                     const int n1 = i0 < na ? min(len, na - i0) : 0;
                     uint8_t* dst = stage + static_cast<size_t>(first + i0) * p.slab_bytes;
                     if (n1 > 0)
-                        bulk_load(dst, reinterpret_cast<const uint8_t*>(m.run_a[r] + static_cast<uintptr_t>(i0) * p.row_bytes),
+                        bulk_load(dst, reinterpret_cast<const uint8_t*>(ra + static_cast<uintptr_t>(i0) * p.row_bytes),
                                   static_cast<uint32_t>(n1) * static_cast<uint32_t>(p.row_bytes), &sm.full[st]);
                     if (len > n1)
                         bulk_load(dst + static_cast<size_t>(n1) * p.slab_bytes,
-                                  reinterpret_cast<const uint8_t*>(m.run_b[r] + static_cast<uintptr_t>(i0 + n1) * p.row_bytes),
+                                  reinterpret_cast<const uint8_t*>(rb + static_cast<uintptr_t>(i0 + n1) * p.row_bytes),
                                   static_cast<uint32_t>(len - n1) * static_cast<uint32_t>(p.row_bytes), &sm.full[st]);
                 }
             } else {
-                for (int f = lane; f < n_valid; f += 32)
-                    bulk_load(stage + static_cast<size_t>(f) * p.slab_bytes,
-                              slot_ptr(m, f, p.pblock_shift, pmask, p.row_bytes) + col, static_cast<uint32_t>(slen),
+                for (int f = lane; f < n_load; f += 32) {
+                    const uint8_t* src = PUSH ? src_row_ptr(m, f, p.row_bytes) + col
+                                              : slot_ptr(m, f, p.pblock_shift, pmask, p.row_bytes) + col;
+                    bulk_load(stage + static_cast<size_t>(f) * p.slab_bytes, src, static_cast<uint32_t>(slen),
                               &sm.full[st]);
+                }
             }
         } else {
             switch (p.vec_bytes) {
-            case 16: lsu_load_unit<16>(p, m, stage, col, slen, lane); break;
-            case 8: lsu_load_unit<8>(p, m, stage, col, slen, lane); break;
-            case 4: lsu_load_unit<4>(p, m, stage, col, slen, lane); break;
-            case 2: lsu_load_unit<2>(p, m, stage, col, slen, lane); break;
-            default: lsu_load_unit<1>(p, m, stage, col, slen, lane); break;
+            case 16: lsu_load_unit<16, PUSH>(p, m, stage, col, slen, lane); break;
+            case 8: lsu_load_unit<8, PUSH>(p, m, stage, col, slen, lane); break;
+            case 4: lsu_load_unit<4, PUSH>(p, m, stage, col, slen, lane); break;
+            case 2: lsu_load_unit<2, PUSH>(p, m, stage, col, slen, lane); break;
+            default: lsu_load_unit<1, PUSH>(p, m, stage, col, slen, lane); break;
             }
             __syncwarp();
         }
@@ -684,20 +842,21 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
         const int k = static_cast<int>(j % kp);
         if (!warp_wait(&sm.full[st], static_cast<uint32_t>((j / nst) & 1), p.status)) return false;
         const StageMeta& m = sm.meta[k];
-        const uint16_t* perm = sm.perm + static_cast<size_t>(k) * sm.perm_stride;
+        const uint16_t* idx = PUSH ? sm.pos + static_cast<size_t>(k) * sm.pos_stride
+                                   : sm.perm + static_cast<size_t>(k) * sm.perm_stride;
         const uint8_t* stage = sm.data + static_cast<size_t>(st) * p.stage_bytes;
         const int slab = static_cast<int>(j % p.n_slabs);
         const int64_t col = static_cast<int64_t>(slab) * p.slab_bytes;
         const int slen = static_cast<int>(min(static_cast<int64_t>(p.slab_bytes), p.row_bytes - col));
         if constexpr (BULK) {
-            store_share<16>(p, m, stage, perm, col, slen, lane, mw, n_movers);
+            store_share<16, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers);
         } else {
             switch (p.vec_bytes) {
-            case 16: store_share<16>(p, m, stage, perm, col, slen, lane, mw, n_movers); break;
-            case 8: store_share<8>(p, m, stage, perm, col, slen, lane, mw, n_movers); break;
-            case 4: store_share<4>(p, m, stage, perm, col, slen, lane, mw, n_movers); break;
-            case 2: store_share<2>(p, m, stage, perm, col, slen, lane, mw, n_movers); break;
-            default: store_share<1>(p, m, stage, perm, col, slen, lane, mw, n_movers); break;
+            case 16: store_share<16, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
+            case 8: store_share<8, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
+            case 4: store_share<4, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
+            case 2: store_share<2, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
+            default: store_share<1, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
             }
         }
         mbar_arrive(&sm.empty[st]);  // this thread's reads of the data stage are done

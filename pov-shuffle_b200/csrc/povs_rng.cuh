@@ -201,6 +201,54 @@ struct Feistel {
         return (L << wr) | R;
     }
 
+    // Inverse of round_trip32: undo rounds 11..0.  Round i starts with widths (lbits, rbits) when
+    // i is even and (rbits, lbits) when odd, and maps (L, R) to (R, (L ^ F_i(R)) & mask).
+    POVS_HD uint32_t round_trip32_inverse(uint32_t y) const
+    {
+        uint32_t L = y >> rbits;
+        uint32_t R = y & ((1u << rbits) - 1u);
+#pragma unroll
+        for (int i = FEISTEL_ROUNDS - 1; i >= 0; --i) {
+            const int wl_i = (i & 1) ? rbits : lbits;
+            const uint32_t prev_r = L;
+            const uint32_t prev_l = (R ^ lowbias32(prev_r ^ keys[i])) & ((1u << wl_i) - 1u);
+            L = prev_l;
+            R = prev_r;
+        }
+        return (L << rbits) | R;
+    }
+
+    POVS_HD uint64_t round_trip_inverse(uint64_t y) const
+    {
+        uint64_t L = y >> rbits;
+        uint64_t R = y & ((uint64_t{1} << rbits) - 1);
+#pragma unroll
+        for (int i = FEISTEL_ROUNDS - 1; i >= 0; --i) {
+            const int wl_i = (i & 1) ? rbits : lbits;
+            const uint64_t prev_r = L;
+            const uint32_t h0 = lowbias32(static_cast<uint32_t>(prev_r) ^ keys[i]);
+            const uint32_t h1 = lowbias32(static_cast<uint32_t>(prev_r >> 32) ^ h0 ^ keys[(i + 1) % FEISTEL_ROUNDS]);
+            const uint64_t f = (static_cast<uint64_t>(h1) << 32) | h0;
+            const uint64_t prev_l = (R ^ f) & ((uint64_t{1} << wl_i) - 1);
+            L = prev_l;
+            R = prev_r;
+        }
+        return (L << rbits) | R;
+    }
+
+    // pi^-1(y) for y in [0, domain): the inverse cycle walk.
+    POVS_HD uint64_t inverse(uint64_t y) const
+    {
+        if (lbits + rbits <= 32) {
+            uint32_t x = round_trip32_inverse(static_cast<uint32_t>(y));
+            while (x >= domain) x = round_trip32_inverse(x);
+            return x;
+        }
+        uint64_t x = round_trip_inverse(y);
+        while (x >= domain) x = round_trip_inverse(x);
+        return x;
+    }
+
     // pi(x) for x in [0, domain): cycle-walk until the image falls inside the domain.
     // Terminates because round_trip is a permutation of [0, 2^bits) and x is inside the domain.
     POVS_HD uint64_t operator()(uint64_t x) const

@@ -49,12 +49,12 @@ SIGNATURES: dict[str, tuple] = {
     "povs_describe_plan_v1": (ctypes.c_int, [_c_vp, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _P_I64, _c_i32]),
     "povs_shuffle_shards_v1": (
         ctypes.c_int,
-        [_c_vp, _P_I64, _c_i32, _c_i64, _P_I64, _c_i32, _c_i32, _c_i32, _c_i32, _c_u64, _c_i32, _c_vp, _c_u32],
+        [_c_vp, _c_vp, _P_I64, _c_i32, _c_i64, _P_I64, _c_i32, _c_i32, _c_i32, _c_i32, _c_u64, _c_i32, _c_vp, _c_u32],
     ),
     "povs_shuffle_sharded_v1": (
         ctypes.c_int,
-        [_c_vp, _P_I64, _c_i32, _c_i32, _c_i64, _P_I64, _c_i32, _c_i32, _c_i32, _c_i32, _c_u64, _c_vp, _c_u32, _c_i32,
-         _c_vp, _c_u32],
+        [_c_vp, _c_vp, _P_I64, _c_i32, _c_i32, _c_i64, _P_I64, _c_i32, _c_i32, _c_i32, _c_i32, _c_u64, _c_vp, _c_u32,
+         _c_i32, _c_vp, _c_u32],
     ),
     "povs_ipc_export_v1": (ctypes.c_int, [_c_vp, _c_i32, _c_vp, _P_I64]),
     "povs_ipc_import_v1": (ctypes.c_int, [_c_vp, _c_i64, _c_i32, ctypes.POINTER(_c_vp), ctypes.POINTER(_c_vp)]),
@@ -290,12 +290,16 @@ def shuffle_shards(
     seed: int,
     device: int,
     flags: int = 0,
+    scratch_ptrs: list[int] | None = None,
 ) -> None:
-    """Shuffle a deck held in several shards addressable from ``device`` (one process)."""
+    """Shuffle a deck held in several shards addressable from ``device`` (one process).
+
+    ``scratch_ptrs``: None (in place) or one buffer per shard of the same size (double-buffered).
+    """
     lib = load()
     rows = _i64_array(shard_rows)
     code = lib.povs_shuffle_shards_v1(
-        _ptr_array(shard_ptrs), rows, len(shard_ptrs), row_bytes, _i64_array(offsets), len(offsets), iterations,
+        _ptr_array(shard_ptrs), _ptr_array(scratch_ptrs) if scratch_ptrs else None, rows, len(shard_ptrs), row_bytes, _i64_array(offsets), len(offsets), iterations,
         pblock, vblock, seed, device, ctypes.c_void_p(current_stream_handle(torch.device("cuda", device))), flags,
     )
     check(code, "povs_shuffle_shards_v1")
@@ -315,11 +319,15 @@ def shuffle_sharded(
     epoch_base: int,
     device: int,
     flags: int = 0,
+    scratch_ptrs: list[int] | None = None,
 ) -> None:
-    """This rank's part of a sharded shuffle (one process per GPU; see include/povs.h)."""
+    """This rank's part of a sharded shuffle (one process per GPU; see include/povs.h).
+
+    ``scratch_ptrs``: None (in place) or one buffer per shard, mapped like the shards (double-buffered).
+    """
     lib = load()
     code = lib.povs_shuffle_sharded_v1(
-        _ptr_array(shard_ptrs), _i64_array(shard_rows), len(shard_ptrs), rank, row_bytes, _i64_array(offsets),
+        _ptr_array(shard_ptrs), _ptr_array(scratch_ptrs) if scratch_ptrs else None, _i64_array(shard_rows), len(shard_ptrs), rank, row_bytes, _i64_array(offsets),
         len(offsets), iterations, pblock, vblock, seed, _ptr_array(flag_ptrs), epoch_base & 0xFFFFFFFF, device,
         ctypes.c_void_p(current_stream_handle(torch.device("cuda", device))), flags,
     )

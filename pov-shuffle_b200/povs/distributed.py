@@ -6,10 +6,17 @@ seed: offsets, assignments and per-vblock permutations are functions of the seed
 indices only.  Options are resolved and validated against the whole deck.
 
 One process per GPU (``ShardedDeck``): every rank maps the other ranks' shards with CUDA IPC at
-construction; a shuffle runs, on every rank, the vblocks ``rank, rank + world, ...``, reading
-member rows from local or peer memory over NVLink (bulk copies, no multicast) and writing them
-back with peer stores, with a device barrier between iterations.  The only collective on the data
-path is the broadcast of the seed from rank 0 (NCCL when the group's backend is NCCL).
+construction, with a device barrier between iterations.  Two orders give the same result:
+
+* double-buffered (default; one scratch buffer per shard): every rank moves the pblocks stored in
+  its own shard, reading them locally and storing each row straight into its destination slot in
+  the other buffer (local or a peer's), so a row crosses NVLink at most once per iteration;
+* in place (``double_buffer=False``, no extra memory): every rank runs the vblocks
+  ``rank, rank + world, ...``, reading member rows from local or peer memory (bulk copies, no
+  multicast) and writing them back with peer stores, so a remote row crosses twice.
+
+The only collective on the data path is the broadcast of the seed from rank 0 (NCCL when the
+group's backend is NCCL).
 No reference counterpart: the reference has no multi-GPU code.
 """
 
@@ -78,11 +85,13 @@ def shuffle_shards(
     iterations: int = 1,
     options: Options | None = None,
     seed: int | Any | None = None,
+    scratch: list[torch.Tensor] | None = None,
 ) -> None:
     """Shuffle, in place, the deck formed by concatenating ``shards`` along axis 0 (one process).
 
     All shards must be contiguous, share the row layout and dtype, and be addressable from the
-    first shard's device (same device, or peers with peer access enabled).
+    first shard's device (same device, or peers with peer access enabled).  ``scratch``: optional
+    buffers shaped like the shards, used for the double-buffered order (contents are overwritten).
     """
     assert shards, "at least one shard is required"
     layout = _row_layout(shards[0])
@@ -97,11 +106,17 @@ def shuffle_shards(
     opts = resolve_options(n_rows, instance_size, dtype_bytes, dev.index, options)
     validate(n_rows, instance_size, dtype_bytes, iterations, opts, rows)
     row_bytes = instance_size * dtype_bytes
+    if scratch is not None:
+        assert len(scratch) == len(shards), "one scratch buffer per shard"
+        for b, s in zip(scratch, shards):
+            assert b.is_cuda and b.is_contiguous() and b.shape == s.shape and b.dtype == s.dtype, \
+                "scratch buffers must be contiguous CUDA tensors shaped like their shards"
     if row_bytes == 0:
         return
     _native.shuffle_shards(
         [s.data_ptr() for s in shards], rows, row_bytes, list(opts.offsets), iterations, opts.physical_block_size,
         opts.virtual_block_size, seed_to_u64(get_int_seed(seed)), dev.index, randomness_flags(opts),
+        scratch_ptrs=[b.data_ptr() for b in scratch] if scratch is not None else None,
     )
 
 
@@ -111,9 +126,12 @@ class ShardedDeck:
     :param shard: this rank's rows, a contiguous CUDA tensor on this rank's GPU; every rank's shard
                   has the same row shape and dtype, and at least ``physical_block_size`` rows.
     :param group: process group (default: the world).  Construction is collective.
+    :param double_buffer: allocate a scratch buffer the size of the shard and shuffle in the
+                          double-buffered order (half the NVLink traffic of the in-place order).
     """
 
-    def __init__(self, shard: torch.Tensor, group: dist.ProcessGroup | None = None, native: Any = None):
+    def __init__(self, shard: torch.Tensor, group: dist.ProcessGroup | None = None, native: Any = None,
+                 double_buffer: bool = True):
         self.native = native if native is not None else _native
         self.group = group
         self.rank = dist.get_rank(group)
@@ -132,27 +150,33 @@ class ShardedDeck:
         self.row_bytes = self.instance_size * self.dtype_bytes
         # One uint32 barrier word per rank, zeroed; epochs only grow.
         self.flags = torch.zeros(self.world, dtype=torch.int32, device=self.device)
+        self.scratch = torch.empty_like(shard) if double_buffer else None
         self.epoch = 0
         dev_index = self.device.index if self.device.type == "cuda" else -1
-        mine = (
-            self.native.ipc_export(shard.data_ptr(), dev_index),
-            self.native.ipc_export(self.flags.data_ptr(), dev_index),
-        )
+        mine = [self.native.ipc_export(shard.data_ptr(), dev_index),
+                self.native.ipc_export(self.flags.data_ptr(), dev_index)]
+        if self.scratch is not None:
+            mine.append(self.native.ipc_export(self.scratch.data_ptr(), dev_index))
         handles = [None] * self.world
         dist.all_gather_object(handles, mine, group=group)
         self._mapped: list[int] = []
         self.shard_ptrs: list[int] = []
         self.flag_ptrs: list[int] = []
-        for r, ((sh, so), (fh, fo)) in enumerate(handles):
+        self.scratch_ptrs: list[int] | None = [] if self.scratch is not None else None
+        local = [shard.data_ptr(), self.flags.data_ptr()] + ([self.scratch.data_ptr()] if self.scratch is not None else [])
+        for r, exported in enumerate(handles):
             if r == self.rank:
-                self.shard_ptrs.append(shard.data_ptr())
-                self.flag_ptrs.append(self.flags.data_ptr())
-                continue
-            sp, sb = self.native.ipc_import(sh, so, dev_index)
-            fp, fb = self.native.ipc_import(fh, fo, dev_index)
-            self._mapped += [sb, fb]
-            self.shard_ptrs.append(sp)
-            self.flag_ptrs.append(fp)
+                ptrs = local
+            else:
+                ptrs = []
+                for handle, offset in exported:
+                    ptr, base = self.native.ipc_import(handle, offset, dev_index)
+                    self._mapped.append(base)
+                    ptrs.append(ptr)
+            self.shard_ptrs.append(ptrs[0])
+            self.flag_ptrs.append(ptrs[1])
+            if self.scratch_ptrs is not None:
+                self.scratch_ptrs.append(ptrs[2])
         dist.barrier(group=group)
 
     def options(self, options: Options | None = None) -> Options:
@@ -179,6 +203,7 @@ class ShardedDeck:
             self.shard_ptrs, self.shard_rows, self.rank, self.row_bytes, list(opts.offsets), iterations,
             opts.physical_block_size, opts.virtual_block_size, seed_u64, self.flag_ptrs, self.epoch,
             self.device.index if self.device.type == "cuda" else -1, flags | randomness_flags(opts),
+            scratch_ptrs=self.scratch_ptrs,
         )
         self.epoch += iterations + 1
 

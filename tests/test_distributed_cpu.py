@@ -32,8 +32,8 @@ class RecordingNative:
     def ipc_close(self, base, device):
         self.calls.append(("close", base))
 
-    def shuffle_sharded(self, *args):
-        self.calls.append(("shuffle", args))
+    def shuffle_sharded(self, *args, scratch_ptrs=None):
+        self.calls.append(("shuffle", args, scratch_ptrs))
 
 
 def _worker(rank: int, world: int, port: int, out_dir: str):
@@ -64,6 +64,7 @@ def _worker(rank: int, world: int, port: int, out_dir: str):
         "seeds": [c[1][8] for c in calls],
         "epochs": [c[1][10] for c in calls],
         "ranks": [c[1][2] for c in calls],
+        "scratch": [c[2] for c in calls],
         "errors": errors,
         "closed": len([c for c in native.calls if c[0] == "close"]),
     }
@@ -82,5 +83,6 @@ def test_two_rank_control_plane(tmp_path):
         assert res["epochs"] == [0, 4], "epoch base advances by iterations + 1 per shuffle"
         assert res["seeds"] == [11, 12], "every rank uses rank 0's seed"
         assert res["errors"] and "at least physical_block_size" in res["errors"][0]
-        assert res["closed"] == 2
+        assert res["closed"] == 3, "shard, barrier flags and scratch of the one peer are unmapped"
+        assert len(res["scratch"]) == 2 and all(len(p) == 2 for p in res["scratch"])
     assert r0["shard_ptrs"][1] == 1000 + 1 and r1["shard_ptrs"][0] == 1000 + 0

@@ -35,7 +35,7 @@ def _split(world: int) -> list[int]:
     return rows
 
 
-def _worker(rank: int, world: int, port: int, out_dir: str, randomness: str):
+def _worker(rank: int, world: int, port: int, out_dir: str, randomness: str, double_buffer: bool):
     sys.path[:0] = [str(REPO), str(REPO / "pov-shuffle_b200")]
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -46,10 +46,10 @@ def _worker(rank: int, world: int, port: int, out_dir: str, randomness: str):
     rows = _split(world)
     start = sum(rows[:rank])
     shard = torch.from_numpy(_deck()[start:start + rows[rank]].copy()).to(f"cuda:{rank}")
-    deck = povs.ShardedDeck(shard)
+    deck = povs.ShardedDeck(shard, double_buffer=double_buffer)
     opts = povs.Options(V, P, OFFSETS, 64, randomness)
     deck.shuffle(iterations=ITERATIONS, options=opts, seed=SEED if rank == 0 else 12345)
-    deck.shuffle(iterations=1, options=opts, seed=SEED + 1)
+    deck.shuffle(iterations=2, options=opts, seed=SEED + 1)
     torch.cuda.synchronize()
     povs.check_device_status(rank)
     np.save(os.path.join(out_dir, f"rank{rank}.npy"), shard.cpu().numpy())
@@ -58,15 +58,17 @@ def _worker(rank: int, world: int, port: int, out_dir: str, randomness: str):
 
 
 @pytest.mark.parametrize("randomness", ["uniform", "reference_cuda"])
-def test_sharded_deck_matches_oracle(oracle_api, tmp_path, randomness):
+@pytest.mark.parametrize("double_buffer", [False, True])
+def test_sharded_deck_matches_oracle(oracle_api, tmp_path, randomness, double_buffer):
+    """Odd (3) then even (2) iteration counts: the double-buffered order ends in the shard both ways."""
     world = min(torch.cuda.device_count(), 8)
     if world < 2:
         pytest.skip("needs at least two GPUs")
-    port = 31000 + (os.getpid() % 2000) + (7 if randomness == "uniform" else 0)
-    mp.start_processes(_worker, args=(world, port, str(tmp_path), randomness), nprocs=world, start_method="spawn",
-                       join=True)
+    port = 31000 + (os.getpid() % 2000) + (7 if randomness == "uniform" else 0) + (3 if double_buffer else 0)
+    mp.start_processes(_worker, args=(world, port, str(tmp_path), randomness, double_buffer), nprocs=world,
+                       start_method="spawn", join=True)
     got = np.concatenate([np.load(tmp_path / f"rank{r}.npy") for r in range(world)])
     want = _deck()
     oracle_api.shuffle(want, ITERATIONS, P, V, OFFSETS, SEED, randomness)
-    oracle_api.shuffle(want, 1, P, V, OFFSETS, SEED + 1, randomness)
+    oracle_api.shuffle(want, 2, P, V, OFFSETS, SEED + 1, randomness)
     assert np.array_equal(got, want)

@@ -288,8 +288,11 @@ def test_full_size_cfg3_keeps_every_row():
     ],
 )
 @pytest.mark.parametrize("randomness", ["uniform", "reference_cuda"])
-def test_shards_match_the_concatenated_deck(oracle_api, rows, row_bytes, P, V, offsets, iterations, randomness):
-    """A deck split into shards (one process) shuffles exactly like the concatenated deck."""
+@pytest.mark.parametrize("double_buffer", [False, True])
+def test_shards_match_the_concatenated_deck(oracle_api, rows, row_bytes, P, V, offsets, iterations, randomness,
+                                            double_buffer):
+    """A deck split into shards (one process) shuffles exactly like the concatenated deck, in
+    place and in the double-buffered order (pblocks pushed to their destination slots)."""
     n = sum(rows)
     host = random_rows(n, row_bytes, seed=n)
     shards, start = [], 0
@@ -297,7 +300,8 @@ def test_shards_match_the_concatenated_deck(oracle_api, rows, row_bytes, P, V, o
         shards.append(torch.from_numpy(host[start:start + r].copy()).to(DEV))
         start += r
     opts = povs.Options(V, P, offsets, 32, randomness)
-    povs.shuffle_shards(shards, iterations=iterations, options=opts, seed=123)
+    scratch = [torch.full_like(s, 0xA5) for s in shards] if double_buffer else None
+    povs.shuffle_shards(shards, iterations=iterations, options=opts, seed=123, scratch=scratch)
     torch.cuda.synchronize()
     povs.check_device_status(0)
     got = torch.cat(shards).cpu().numpy()
@@ -307,6 +311,22 @@ def test_shards_match_the_concatenated_deck(oracle_api, rows, row_bytes, P, V, o
     want = host.copy()
     oracle_api.shuffle(want, iterations, P, V, offsets, 123, randomness)
     assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("iterations", [1, 2, 5])
+def test_double_buffered_shards_one_shard(oracle_api, iterations):
+    """One shard in the double-buffered order: odd iteration counts end with the copy back."""
+    n, row_bytes, P, V, offsets = 100_003, 64, 32, 4, [0, 3, 7, 31]
+    host = random_rows(n, row_bytes, seed=9)
+    deck = torch.from_numpy(host.copy()).to(DEV)
+    scratch = torch.empty_like(deck)
+    povs.shuffle_shards([deck], iterations=iterations, options=povs.Options(V, P, offsets, 32), seed=77,
+                        scratch=[scratch])
+    torch.cuda.synchronize()
+    povs.check_device_status(0)
+    want = host.copy()
+    oracle_api.shuffle(want, iterations, P, V, offsets, 77)
+    assert np.array_equal(deck.cpu().numpy(), want)
 
 
 def test_shards_smaller_than_a_pblock_are_rejected():
