@@ -225,6 +225,43 @@ int povs_apply_static_v1(void* data, int64_t n_rows, int64_t row_bytes, int32_t 
                          const int32_t* perms_host, int32_t sort_members, int32_t device, void* stream,
                          uint32_t flags);
 
+/*
+ * Batched decks: n_decks independent decks of the same geometry, deck d at
+ * data + d * deck_stride (bytes; deck_stride >= n_rows * row_bytes), all shuffled by one launch
+ * per iteration.  Deck d ends exactly as povs_shuffle_v1 on it alone with seed seeds[d] would
+ * leave it.  `seeds` is a DEVICE array of n_decks seeds that must stay unchanged until the stream
+ * has run the work.  Flags as povs_shuffle_v1.
+ * Replaces the reference's loop of one povs.shuffle call per episode in its bias exercises
+ * (src/povs/eval/exercises.py:387-389, 268-270).
+ */
+int povs_shuffle_batch_v1(void* data, int64_t n_decks, int64_t deck_stride, int64_t n_rows, int64_t row_bytes,
+                          const int64_t* offsets, int32_t n_offsets, int32_t iterations, int32_t pblock,
+                          int32_t vblock, const uint64_t* seeds, int32_t device, void* stream, uint32_t flags);
+
+/*
+ * Travel-distance histogram over shuffled episodes (all pointers are device memory; asynchronous
+ * on `stream`).  ids: int32 (id_bytes 4) or int64 (id_bytes 8); element i of episode e at
+ * ids[e * episode_stride + i * element_stride], each episode a permutation of 0 .. deck-1.
+ * kind 0: counts[(i - v) mod deck] += 1 for every element (positional travel distance,
+ * get_tvd, src/povs/eval/metrics.py:38-87).  kind 1: counts[((v[(i + step) mod deck] - v[i]) - step)
+ * mod deck] += 1 for every position (2-gram relative travel distance with step = skip + 1,
+ * get_ngram_tvd with n = 2, metrics.py:147-172).  counts: deck uint64 bins, ADDED to.
+ */
+int povs_travel_histogram_v1(const void* ids, int32_t id_bytes, int64_t n_episodes, int64_t deck,
+                             int64_t episode_stride, int64_t element_stride, int32_t kind, int64_t step,
+                             uint64_t* counts, int32_t device, void* stream);
+
+/*
+ * n-gram keys (n >= 2) over shuffled episodes, for the sparse n-gram TVD (get_ngram_tvd with
+ * n > 2, metrics.py:173-248): for every episode e and anchor a (positions[j] for j < n_positions,
+ * or every position 0 .. deck-1 when positions is NULL), keys[e * count + j] =
+ * sum over k = 1 .. n-1 of (((v[(a + k*step) mod deck] - v[a]) - k*step) mod deck) * deck^(n-1-k),
+ * in wrapping 64-bit arithmetic.  Same id layout as povs_travel_histogram_v1.
+ */
+int povs_ngram_keys_v1(const void* ids, int32_t id_bytes, int64_t n_episodes, int64_t deck, int64_t episode_stride,
+                       int64_t element_stride, int32_t n, int64_t step, const int64_t* positions,
+                       int64_t n_positions, int64_t* keys, int32_t device, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -14,6 +14,7 @@
 
 #include "../../include/povs.h"
 #include "povs_kernel.cuh"
+#include "povs_metrics.cuh"
 
 using povs::IterParams;
 
@@ -134,6 +135,7 @@ struct DeviceCtx {
 };
 
 constexpr int MAX_DEVICES = 64;
+constexpr int64_t SLAB_FLOOR_BYTES = 2048; // preferred minimum width of a column slab
 DeviceCtx g_ctx[MAX_DEVICES];
 std::mutex g_ctx_mu;
 
@@ -188,6 +190,9 @@ int get_ctx(int dev, DeviceCtx** out)
         c.max_threads_per_sm = prop.maxThreadsPerMultiProcessor;
         int r = set_smem_attr_all(c.smem_optin);
         if (r != POVS_OK) return r;
+        POVS_CUDA_TRY(cudaFuncSetAttribute(reinterpret_cast<const void*>(povs::povs_travel_histogram_kernel),
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           povs::HIST_SMEM_MAX_BINS * static_cast<int>(sizeof(uint32_t))));
         POVS_CUDA_TRY(cudaMalloc(&c.status, sizeof(int)));
         POVS_CUDA_TRY(cudaMemset(c.status, 0, sizeof(int)));
         c.ready = true;
@@ -224,6 +229,7 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out, boo
     for (int i = 0; i < p.n_shards; ++i) addr |= reinterpret_cast<uintptr_t>(p.shard_base[i]);
     if (push)
         for (int i = 0; i < p.n_shards; ++i) addr |= reinterpret_cast<uintptr_t>(p.dst_base[i]);
+    if (p.n_decks > 1) addr |= static_cast<uintptr_t>(p.deck_stride);
     int vec = 16;
     while (vec > 1 && ((p.row_bytes % vec) != 0 || (addr % vec) != 0)) vec >>= 1;
     const bool bulk = (vec == 16) && !t.force_plain;
@@ -231,17 +237,25 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out, boo
     // Slab width: whole rows when a vblock fits a stage, else the widest 128-byte (or vec) multiple that does.
     // A stage holds a unit's rows: the vblock's V*P rows in place, one member's P rows in push mode.
     const int64_t stage_rows = push ? p.pblock : vp;
-    int64_t slab = p.row_bytes;
-    if (stage_rows * p.row_bytes > t.stage_cap) {
-        const int64_t fit = t.stage_cap / stage_rows;
-        const int64_t gran = fit >= 128 ? 128 : vec;
-        slab = std::max<int64_t>(vec, (fit / gran) * gran);
-    }
     const int max_stages = std::max(2, std::min(t.n_stages, povs::MAX_STAGES));
     const int movers = std::max(1, std::min(t.movers, 15));
     const int permuters = std::max(1, std::min(t.permuters, 16 - movers));
     // Permutation slots: the stages' worth plus room for every permuter to work ahead.
     auto slots_for = [&](int stages) { return std::min(povs::MAX_SLOTS, stages + 2 * permuters); };
+    int64_t slab = p.row_bytes;
+    if (stage_rows * p.row_bytes > t.stage_cap) {
+        const int64_t fit = t.stage_cap / stage_rows;
+        const int64_t gran = fit >= 128 ? 128 : vec;
+        slab = std::max<int64_t>(vec, (fit / gran) * gran);
+        // Wide rows: pieces of at least SLAB_FLOOR bytes per row and stage when three such stages
+        // fit (per-row copies of 1 KiB and less leave the DRAM well short of its copy bandwidth).
+        const int64_t wide = std::min<int64_t>(p.row_bytes, ((SLAB_FLOOR_BYTES / vec) * vec));
+        if (slab < wide) {
+            const int64_t wide_stage = ((stage_rows * wide + 127) / 128) * 128;
+            const int64_t fixed = povs::cta_smem_bytes(0, 0, slots_for(3), static_cast<int>(vp), p.pblock);
+            if (fixed + 3 * (wide_stage + 16) <= c.smem_optin) slab = wide;
+        }
+    }
     auto stages_for = [&](int64_t sl, int64_t& stage_bytes) {
         stage_bytes = ((stage_rows * sl + 127) / 128) * 128;
         const int kp = slots_for(max_stages);
@@ -266,7 +280,9 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out, boo
     const int per_sm_by_threads = std::max(1, c.max_threads_per_sm / (warps * 32));
     const int ctas_per_sm = std::min(per_sm_by_smem, per_sm_by_threads);
     const int64_t n_mine = push ? (p.push_rank < 0 ? p.n_pblocks : p.n_pblocks / std::max(1, p.n_shards) + 1)
-                                : (p.vb_begin < p.n_vblocks ? (p.n_vblocks - p.vb_begin + p.vb_step - 1) / p.vb_step : 0);
+                                : (p.vb_begin < p.n_vblocks * p.n_decks
+                                       ? (p.n_vblocks * p.n_decks - p.vb_begin + p.vb_step - 1) / p.vb_step
+                                       : 0);
     const int grid = static_cast<int>(std::min<int64_t>(std::max<int64_t>(1, n_mine), static_cast<int64_t>(c.sm_count) * ctas_per_sm));
 
     p.slab_bytes = static_cast<int32_t>(slab);
@@ -331,6 +347,9 @@ void fill_geometry(IterParams& p, void* data, int64_t n_rows, int64_t row_bytes,
     p.vb_begin = 0;
     p.vb_step = 1;
     p.push_rank = -1;
+    p.n_decks = 1;
+    p.deck_stride = 0;
+    p.deck_seeds = nullptr;
 }
 
 int launch_direct(const Plan& pl, const IterParams& p, cudaStream_t s)
@@ -418,7 +437,8 @@ int set_shards(IterParams& p, void* const* shard_ptrs, const int64_t* shard_rows
 int shuffle_on_device(void* data, int64_t n_rows, int64_t row_bytes, const int64_t* offsets, int32_t n_offsets,
                       int32_t iterations, int32_t pblock, int32_t vblock, uint64_t seed, DeviceCtx& c,
                       cudaStream_t s, uint32_t flags, void* const* shard_ptrs = nullptr,
-                      const int64_t* shard_rows = nullptr, int32_t n_shards = 1)
+                      const int64_t* shard_rows = nullptr, int32_t n_shards = 1, int64_t n_decks = 1,
+                      int64_t deck_stride = 0, const uint64_t* deck_seeds = nullptr)
 {
     IterParams base;
     fill_geometry(base, data, n_rows, row_bytes, pblock, vblock, c.status);
@@ -426,6 +446,9 @@ int shuffle_on_device(void* data, int64_t n_rows, int64_t row_bytes, const int64
         int rs = set_shards(base, shard_ptrs, shard_rows, n_shards);
         if (rs != POVS_OK) return rs;
     }
+    base.n_decks = n_decks;
+    base.deck_stride = deck_stride;
+    base.deck_seeds = deck_seeds;
     base.seed = seed;
     base.rng_mode = (flags & POVS_FLAG_REFERENCE_RNG) ? povs::RNG_REFERENCE_CUDA : povs::RNG_UNIFORM;
     base.n_offsets = n_offsets;
@@ -1109,5 +1132,134 @@ extern "C" int povs_ipc_close_v1(void* base, int32_t device)
     int r = dg.enter(device);
     if (r != POVS_OK) return r;
     POVS_CUDA_TRY(cudaIpcCloseMemHandle(base));
+    return POVS_OK;
+}
+
+// ------------------------------------------------------------------------------------------
+// Batched decks and shuffle-bias metrics.
+// ------------------------------------------------------------------------------------------
+
+extern "C" int povs_shuffle_batch_v1(void* data, int64_t n_decks, int64_t deck_stride, int64_t n_rows,
+                                     int64_t row_bytes, const int64_t* offsets, int32_t n_offsets, int32_t iterations,
+                                     int32_t pblock, int32_t vblock, const uint64_t* seeds, int32_t device,
+                                     void* stream, uint32_t flags)
+{
+    g_err[0] = '\0';
+    int r = check_common(data, n_rows, row_bytes, pblock, vblock, iterations);
+    if (r != POVS_OK) return r;
+    r = check_offsets(offsets, n_offsets, n_rows);
+    if (r != POVS_OK) return r;
+    if (n_decks < 1) return fail(POVS_ERR_INVALID_ARGUMENT, "n_decks (%lld) must be positive", static_cast<long long>(n_decks));
+    if (seeds == nullptr) return fail(POVS_ERR_INVALID_ARGUMENT, "seeds is NULL");
+    if (n_decks > 1 && deck_stride < n_rows * row_bytes)
+        return fail(POVS_ERR_INVALID_ARGUMENT, "deck_stride (%lld) is smaller than a deck (%lld bytes)",
+                    static_cast<long long>(deck_stride), static_cast<long long>(n_rows * row_bytes));
+    if ((flags & ~uint32_t{POVS_FLAG_NO_GRAPH | POVS_FLAG_SYNC | POVS_FLAG_REFERENCE_RNG}) != 0)
+        return fail(POVS_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
+    DeviceGuard dg;
+    r = dg.enter(device);
+    if (r != POVS_OK) return r;
+    DeviceCtx* c = nullptr;
+    r = get_ctx(device, &c);
+    if (r != POVS_OK) return r;
+    return shuffle_on_device(data, n_rows, row_bytes, offsets, n_offsets, iterations, pblock, vblock, 0, *c,
+                             static_cast<cudaStream_t>(stream), flags, nullptr, nullptr, 1, n_decks,
+                             n_decks > 1 ? deck_stride : 0, seeds);
+}
+
+namespace {
+
+int check_metric_args(const void* ids, int32_t id_bytes, int64_t n_episodes, int64_t deck)
+{
+    if (ids == nullptr) return fail(POVS_ERR_INVALID_ARGUMENT, "ids is NULL");
+    if (id_bytes != 4 && id_bytes != 8) return fail(POVS_ERR_INVALID_ARGUMENT, "id_bytes must be 4 or 8, is %d", id_bytes);
+    if (n_episodes < 1 || deck < 1)
+        return fail(POVS_ERR_INVALID_ARGUMENT, "episodes (%lld) and deck size (%lld) must be positive",
+                    static_cast<long long>(n_episodes), static_cast<long long>(deck));
+    return POVS_OK;
+}
+
+int metric_grid(const DeviceCtx& c, int64_t total, int64_t min_blocks)
+{
+    const int64_t want = std::max<int64_t>(1, (total + 255) / 256);
+    return static_cast<int>(std::max<int64_t>(min_blocks, std::min<int64_t>(want, int64_t{4} * c.sm_count)));
+}
+
+} // namespace
+
+extern "C" int povs_travel_histogram_v1(const void* ids, int32_t id_bytes, int64_t n_episodes, int64_t deck,
+                                        int64_t episode_stride, int64_t element_stride, int32_t kind, int64_t step,
+                                        uint64_t* counts, int32_t device, void* stream)
+{
+    g_err[0] = '\0';
+    int r = check_metric_args(ids, id_bytes, n_episodes, deck);
+    if (r != POVS_OK) return r;
+    if (counts == nullptr) return fail(POVS_ERR_INVALID_ARGUMENT, "counts is NULL");
+    if (kind != 0 && kind != 1) return fail(POVS_ERR_INVALID_ARGUMENT, "kind must be 0 (positional) or 1 (pairs)");
+    if (kind == 1 && step < 1) return fail(POVS_ERR_INVALID_ARGUMENT, "step (%lld) must be positive", static_cast<long long>(step));
+    DeviceGuard dg;
+    r = dg.enter(device);
+    if (r != POVS_OK) return r;
+    DeviceCtx* c = nullptr;
+    r = get_ctx(device, &c);
+    if (r != POVS_OK) return r;
+    povs::MetricParams q{};
+    q.ids = ids;
+    q.id_bytes = id_bytes;
+    q.kind = kind;
+    q.n_episodes = n_episodes;
+    q.deck = deck;
+    q.episode_stride = episode_stride;
+    q.element_stride = element_stride;
+    q.step = step;
+    q.counts = reinterpret_cast<unsigned long long*>(counts);
+    q.smem_bins = deck <= povs::HIST_SMEM_MAX_BINS ? static_cast<int32_t>(deck) : 0;
+    const int64_t total = n_episodes * deck;
+    // Shared-memory bins are uint32: keep every CTA below 2^32 observations.
+    const int grid = metric_grid(*c, total, total / (int64_t{1} << 31) + 1);
+    void* args[] = {&q};
+    cudaError_t e = cudaLaunchKernel(reinterpret_cast<const void*>(povs::povs_travel_histogram_kernel), dim3(grid),
+                                     dim3(256), args, static_cast<size_t>(q.smem_bins) * sizeof(uint32_t),
+                                     static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernel(histogram)");
+    return POVS_OK;
+}
+
+extern "C" int povs_ngram_keys_v1(const void* ids, int32_t id_bytes, int64_t n_episodes, int64_t deck,
+                                  int64_t episode_stride, int64_t element_stride, int32_t n, int64_t step,
+                                  const int64_t* positions, int64_t n_positions, int64_t* keys, int32_t device,
+                                  void* stream)
+{
+    g_err[0] = '\0';
+    int r = check_metric_args(ids, id_bytes, n_episodes, deck);
+    if (r != POVS_OK) return r;
+    if (keys == nullptr) return fail(POVS_ERR_INVALID_ARGUMENT, "keys is NULL");
+    if (n < 2) return fail(POVS_ERR_INVALID_ARGUMENT, "n-gram degree (%d) must be at least 2", n);
+    if (step < 1) return fail(POVS_ERR_INVALID_ARGUMENT, "step (%lld) must be positive", static_cast<long long>(step));
+    if (positions != nullptr && n_positions < 1) return fail(POVS_ERR_INVALID_ARGUMENT, "n_positions must be positive");
+    DeviceGuard dg;
+    r = dg.enter(device);
+    if (r != POVS_OK) return r;
+    DeviceCtx* c = nullptr;
+    r = get_ctx(device, &c);
+    if (r != POVS_OK) return r;
+    povs::MetricParams q{};
+    q.ids = ids;
+    q.id_bytes = id_bytes;
+    q.kind = n;
+    q.n_episodes = n_episodes;
+    q.deck = deck;
+    q.episode_stride = episode_stride;
+    q.element_stride = element_stride;
+    q.step = step;
+    q.positions = positions;
+    q.n_positions = positions != nullptr ? n_positions : 0;
+    q.keys = keys;
+    const int64_t total = n_episodes * (positions != nullptr ? n_positions : deck);
+    const int grid = metric_grid(*c, total, 1);
+    void* args[] = {&q};
+    cudaError_t e = cudaLaunchKernel(reinterpret_cast<const void*>(povs::povs_ngram_keys_kernel), dim3(grid), dim3(256),
+                                     args, 0, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernel(ngram keys)");
     return POVS_OK;
 }

@@ -100,6 +100,12 @@ struct IterParams {
     // A launch moves the pblocks whose first storage row lies in shard push_rank (all pblocks if -1).
     uint8_t* dst_base[MAX_SHARDS];
     int32_t push_rank;
+    // Batched decks (device randomness, in place, one shard): n_decks independent decks of the same
+    // geometry at data + d * deck_stride, deck d shuffled with seed deck_seeds[d] (device array).
+    // n_decks == 1: the single deck of `data` with `seed`.
+    int64_t n_decks;
+    int64_t deck_stride;
+    const uint64_t* deck_seeds;
     int64_t offsets[MAX_INLINE_OFFSETS];
 };
 
@@ -257,15 +263,15 @@ __device__ __forceinline__ void warp_bitonic_sort(uint64_t (&x)[EPL], int lane)
 
 // Generates the permutation of one vblock: perm[f] = source slot of destination slot f, f < n_valid.
 template <int EPL>
-__device__ __forceinline__ void warp_make_perm(const IterParams& p, uint64_t vblock, int n_valid, uint16_t* perm,
-                                               int lane)
+__device__ __forceinline__ void warp_make_perm(const IterParams& p, uint64_t seed, uint64_t vblock, int n_valid,
+                                               uint16_t* perm, int lane)
 {
     uint64_t x[EPL];
     if constexpr (EPL >= 4) {
 #pragma unroll
         for (int q = 0; q < EPL / 4; ++q) {
             const uint32_t quad = static_cast<uint32_t>((lane * EPL) / 4 + q);
-            const U32x4 k = perm_key4(p.seed, p.iteration, vblock, quad);
+            const U32x4 k = perm_key4(seed, p.iteration, vblock, quad);
             const uint32_t w[4] = {k.x, k.y, k.z, k.w};
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
@@ -276,7 +282,7 @@ __device__ __forceinline__ void warp_make_perm(const IterParams& p, uint64_t vbl
         }
     } else {
         const uint32_t e0 = static_cast<uint32_t>(lane * EPL);
-        const U32x4 k = perm_key4(p.seed, p.iteration, vblock, e0 >> 2);
+        const U32x4 k = perm_key4(seed, p.iteration, vblock, e0 >> 2);
 #pragma unroll
         for (int r = 0; r < EPL; ++r) {
             const uint32_t e = e0 + r;
@@ -296,13 +302,13 @@ __device__ __forceinline__ void warp_make_perm(const IterParams& p, uint64_t vbl
 // The reference kernel's permutation (src/povs/__cuda/lib/povs.cu:282-321): identity over the
 // gap-free slots 0..n_valid-1, then a forward Fisher-Yates on one thread with xorshift32
 // (13, 17, 5) seeded by the vblock seed and Lemire's multiply-shift range reduction.
-__device__ __forceinline__ void warp_make_perm_xorshift(const IterParams& p, uint64_t vblock, int n_valid,
-                                                        uint16_t* perm, int lane)
+__device__ __forceinline__ void warp_make_perm_xorshift(const IterParams& p, uint64_t seed, uint64_t vblock,
+                                                        int n_valid, uint16_t* perm, int lane)
 {
     for (int f = lane; f < n_valid; f += 32) perm[f] = static_cast<uint16_t>(f);
     __syncwarp();
     if (lane == 0) {
-        uint32_t r = vblock_seed(p.seed, p.iteration, vblock);
+        uint32_t r = vblock_seed(seed, p.iteration, vblock);
         const int last = n_valid - 1;
         for (int i = 0; i <= last; ++i) {
             r ^= r << 13;
@@ -521,15 +527,15 @@ __device__ __forceinline__ void store_share(const IterParams& p, const StageMeta
 // Push mode: the destination slot of every element of the unit's own member (elements
 // first .. first+count-1 of the vblock) under the uniform permutation; same sort as warp_make_perm.
 template <int EPL>
-__device__ __forceinline__ void warp_make_pos(const IterParams& p, uint64_t vblock, int n_valid, int first, int count,
-                                              uint16_t* pos, int lane)
+__device__ __forceinline__ void warp_make_pos(const IterParams& p, uint64_t seed, uint64_t vblock, int n_valid,
+                                              int first, int count, uint16_t* pos, int lane)
 {
     uint64_t x[EPL];
     if constexpr (EPL >= 4) {
 #pragma unroll
         for (int q = 0; q < EPL / 4; ++q) {
             const uint32_t quad = static_cast<uint32_t>((lane * EPL) / 4 + q);
-            const U32x4 k = perm_key4(p.seed, p.iteration, vblock, quad);
+            const U32x4 k = perm_key4(seed, p.iteration, vblock, quad);
             const uint32_t w[4] = {k.x, k.y, k.z, k.w};
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
@@ -540,7 +546,7 @@ __device__ __forceinline__ void warp_make_pos(const IterParams& p, uint64_t vblo
         }
     } else {
         const uint32_t e0 = static_cast<uint32_t>(lane * EPL);
-        const U32x4 k = perm_key4(p.seed, p.iteration, vblock, e0 >> 2);
+        const U32x4 k = perm_key4(seed, p.iteration, vblock, e0 >> 2);
 #pragma unroll
         for (int r = 0; r < EPL; ++r) {
             const uint32_t e = e0 + r;
@@ -654,7 +660,8 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
         plist = push_list(p, offset);
         n_list = plist.size();
     } else {
-        n_list = p.vb_begin < p.n_vblocks ? (p.n_vblocks - p.vb_begin + p.vb_step - 1) / p.vb_step : 0;
+        const int64_t total = p.n_vblocks * p.n_decks;
+        n_list = p.vb_begin < total ? (total - p.vb_begin + p.vb_step - 1) / p.vb_step : 0;
     }
     if (blockIdx.x >= n_list) return;
     const int64_t my_entries = (n_list - blockIdx.x + gridDim.x - 1) / gridDim.x;
@@ -667,8 +674,12 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
         // Uniform mode maps all n_v*V slots (padding ids anywhere); the reference-CUDA mode maps
         // slots [0, n_p) and leaves the padding in the last slots, as the reference does.
         const bool ref_rng = p.rng_mode == RNG_REFERENCE_CUDA;
-        if constexpr (!INJECTED)
-            pi.init(p.seed, p.iteration, ref_rng ? static_cast<uint64_t>(p.n_pblocks) : static_cast<uint64_t>(p.n_vblocks) * p.vblock);
+        const uint64_t domain = ref_rng ? static_cast<uint64_t>(p.n_pblocks) : static_cast<uint64_t>(p.n_vblocks) * p.vblock;
+        if constexpr (!INJECTED) pi.init(p.seed, p.iteration, domain);
+        // Batched decks: the randomness of the deck of the current unit.
+        uint64_t seed = p.seed;
+        int64_t deck = -1; // batched decks: none drawn yet
+        int64_t deck_offset = offset;
         const int q = warp - n_movers;
         for (int64_t u = q; u < n_units; u += p.n_permuters) {
             const int k = static_cast<int>(u % kp);
@@ -684,6 +695,21 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
                 own_lane = static_cast<int>(slot_of_own - v * p.vblock);
             } else {
                 v = p.vb_begin + p.vb_step * entry;
+            }
+            uintptr_t deck_shift = 0; // batched decks: byte offset of the unit's deck
+            if constexpr (!PUSH && !INJECTED) {
+                if (p.n_decks > 1) {
+                    const int64_t d = v / p.n_vblocks;
+                    v -= d * p.n_vblocks;
+                    if (d != deck) {
+                        deck = d;
+                        seed = p.deck_seeds[d];
+                        pi.init(seed, p.iteration, domain);
+                        deck_offset = p.offsets[reduce_range(offset_draw(seed, p.iteration),
+                                                             static_cast<uint32_t>(p.n_offsets))];
+                    }
+                    deck_shift = static_cast<uintptr_t>(d * p.deck_stride);
+                }
             }
             StageMeta& m = sm.meta[k];
             uint16_t* perm = sm.perm + static_cast<size_t>(k) * sm.perm_stride;
@@ -724,9 +750,11 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
             if (lane < p.vblock && valid) {
                 // Storage run of the member (in the destination buffer in push mode): from row s0, split
                 // at most once where its shard (or the deck) ends.
-                int64_t s0 = mem * p.pblock + offset;
+                int64_t s0 = mem * p.pblock + deck_offset;
                 if (s0 >= p.n_rows) s0 -= p.n_rows;
                 locate_run(p, PUSH ? p.dst_base : p.shard_base, s0, rows, m.run_a[rank], m.run_b[rank], m.n_a[rank]);
+                m.run_a[rank] += deck_shift;
+                m.run_b[rank] += deck_shift;
                 if (PUSH && lane == own_lane) {
                     locate_run(p, p.shard_base, s0, rows, m.src_a, m.src_b, m.src_na);
                     m.rows_mine = rows;
@@ -749,19 +777,19 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
                 const int first = own_rank << p.pblock_shift;
                 uint16_t* pos = sm.pos + static_cast<size_t>(k) * sm.pos_stride;
                 if (ref_rng) {
-                    warp_make_perm_xorshift(p, static_cast<uint64_t>(v), n_valid, perm, lane);
+                    warp_make_perm_xorshift(p, seed, static_cast<uint64_t>(v), n_valid, perm, lane);
                     for (int f = lane; f < n_valid; f += 32) {
                         const int e = static_cast<int>(perm[f]) - first;
                         if (e >= 0 && e < own_rows) pos[e] = static_cast<uint16_t>(f);
                     }
                 } else {
-                    warp_make_pos<EPL>(p, static_cast<uint64_t>(v), n_valid, first, own_rows, pos, lane);
+                    warp_make_pos<EPL>(p, seed, static_cast<uint64_t>(v), n_valid, first, own_rows, pos, lane);
                 }
             } else {
                 if (ref_rng)
-                    warp_make_perm_xorshift(p, static_cast<uint64_t>(v), n_valid, perm, lane);
+                    warp_make_perm_xorshift(p, seed, static_cast<uint64_t>(v), n_valid, perm, lane);
                 else
-                    warp_make_perm<EPL>(p, static_cast<uint64_t>(v), n_valid, perm, lane);
+                    warp_make_perm<EPL>(p, seed, static_cast<uint64_t>(v), n_valid, perm, lane);
             }
             __syncwarp();
             mbar_arrive(&sm.pfull[k]); // each lane publishes its writes to the slot

@@ -3,8 +3,10 @@
 Public API kept from the reference: ``shuffle``, ``Options``, ``BuildParams``, ``get_build_params``,
 ``optim_options_for_dataset``.  Additions: ``apply_randomness`` (inject offsets, block assignments
 and per-vblock permutations, for bit-exact comparison with other implementations),
-``check_device_status``, and decks split into shards: ``shuffle_shards`` (one process) and
-``ShardedDeck`` (one process per GPU).
+``check_device_status``, decks split into shards: ``shuffle_shards`` (one process) and
+``ShardedDeck`` (one process per GPU), many host decks streamed through the GPU (``shuffle_many``)
+and many independent CUDA decks shuffled together (``shuffle_batch``).  ``povs.eval`` holds the
+shuffle-bias metrics and exercises on the GPU.
 """
 
 from __future__ import annotations
@@ -32,6 +34,7 @@ __all__ = [
     "shuffle_shards",
     "ShardedDeck",
     "shuffle_many",
+    "shuffle_batch",
 ]
 
 
@@ -83,6 +86,31 @@ def shuffle_many(
         elif not isinstance(d, np.ndarray):
             raise TypeError(f"Unsupported data type: {type(d)}")
     povs_numpy.shuffle_many(arrays, iterations, options, [base + i for i in range(len(arrays))])
+
+
+def shuffle_batch(
+    decks: t.Tensor,
+    iterations: int = 1,
+    options: Options | None = None,
+    seeds: Any = None,
+) -> None:
+    """Shuffle each deck ``decks[d]`` of a contiguous CUDA tensor (n_decks, rows, ...) independently, in place.
+
+    One launch per iteration covers every deck.  ``seeds``: a sequence with one seed per deck, an int
+    (deck d gets ``seeds + d``), or a generator / None from which one seed per deck is drawn in deck
+    order; deck d ends exactly as ``shuffle(decks[d], iterations, options, seed=<its seed>)`` would
+    leave it.  Addition to the reference API (its bias exercises loop over decks one call at a time).
+    """
+    if not isinstance(decks, t.Tensor) or decks.get_device() == -1:
+        raise TypeError("shuffle_batch takes a CUDA tensor of decks; use shuffle_many for host decks")
+    n = decks.shape[0]
+    if isinstance(seeds, (int, np.integer)) and not isinstance(seeds, bool):
+        per_deck = [int(seeds) + d for d in range(n)]
+    elif seeds is None or isinstance(seeds, (np.random.Generator, t.Generator)):
+        per_deck = [get_int_seed(seeds) for _ in range(n)]
+    else:
+        per_deck = [get_int_seed(s) for s in seeds]
+    povs_torch.shuffle_batch(decks, iterations, options, per_deck)
 
 
 def optim_options_for_dataset(data: np.ndarray | t.Tensor, options: Options | None = None) -> Options:

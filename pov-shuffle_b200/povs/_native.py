@@ -59,6 +59,18 @@ SIGNATURES: dict[str, tuple] = {
     "povs_ipc_export_v1": (ctypes.c_int, [_c_vp, _c_i32, _c_vp, _P_I64]),
     "povs_ipc_import_v1": (ctypes.c_int, [_c_vp, _c_i64, _c_i32, ctypes.POINTER(_c_vp), ctypes.POINTER(_c_vp)]),
     "povs_ipc_close_v1": (ctypes.c_int, [_c_vp, _c_i32]),
+    "povs_shuffle_batch_v1": (
+        ctypes.c_int,
+        [_c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _P_I64, _c_i32, _c_i32, _c_i32, _c_i32, _c_vp, _c_i32, _c_vp, _c_u32],
+    ),
+    "povs_travel_histogram_v1": (
+        ctypes.c_int,
+        [_c_vp, _c_i32, _c_i64, _c_i64, _c_i64, _c_i64, _c_i32, _c_i64, _c_vp, _c_i32, _c_vp],
+    ),
+    "povs_ngram_keys_v1": (
+        ctypes.c_int,
+        [_c_vp, _c_i32, _c_i64, _c_i64, _c_i64, _c_i64, _c_i32, _c_i64, _c_vp, _c_i64, _c_vp, _c_i32, _c_vp],
+    ),
     "povs_apply_static_v1": (
         ctypes.c_int,
         [_c_vp, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _P_I64, _c_vp, _c_vp, _c_i32, _c_i32, _c_vp, _c_u32],
@@ -140,6 +152,67 @@ def shuffle_device(
         flags,
     )
     check(code, "povs_shuffle_v1")
+
+
+def shuffle_batch(
+    decks: torch.Tensor,
+    row_bytes: int,
+    offsets: list[int],
+    iterations: int,
+    pblock: int,
+    vblock: int,
+    seeds: torch.Tensor,
+    flags: int = 0,
+) -> None:
+    """Shuffle every deck ``decks[d]`` (a contiguous CUDA tensor of shape (n_decks, rows, ...)) with
+    seed ``seeds[d]`` (int64 CUDA tensor holding the 64-bit seeds), one launch per iteration."""
+    lib = load()
+    dev = decks.device
+    assert seeds.is_cuda and seeds.dtype == torch.int64 and seeds.is_contiguous() and seeds.numel() == decks.shape[0]
+    code = lib.povs_shuffle_batch_v1(
+        ctypes.c_void_p(decks.data_ptr()), decks.shape[0], decks.stride(0) * decks.element_size(), decks.shape[1],
+        row_bytes, _i64_array(offsets), len(offsets), iterations, pblock, vblock, ctypes.c_void_p(seeds.data_ptr()),
+        dev.index, ctypes.c_void_p(current_stream_handle(dev)), flags,
+    )
+    check(code, "povs_shuffle_batch_v1")
+
+
+def _episode_layout(ids: torch.Tensor) -> tuple[int, int, int, int]:
+    assert ids.is_cuda and ids.dim() == 2 and ids.dtype in (torch.int32, torch.int64), \
+        "episodes must be a 2-D int32/int64 CUDA tensor"
+    return ids.element_size(), ids.shape[0], ids.shape[1], ids.stride(0)
+
+
+def travel_histogram(ids: torch.Tensor, kind: int, step: int, counts: torch.Tensor) -> None:
+    """Add the travel-distance histogram of the episodes ``ids`` (n_episodes, deck) to ``counts``
+    (int64 CUDA tensor of ``deck`` bins): kind 0 positional, kind 1 2-gram with ``step``."""
+    lib = load()
+    id_bytes, n_ep, deck, ep_stride = _episode_layout(ids)
+    assert counts.is_cuda and counts.dtype == torch.int64 and counts.numel() == deck and counts.is_contiguous()
+    dev = ids.device
+    code = lib.povs_travel_histogram_v1(
+        ctypes.c_void_p(ids.data_ptr()), id_bytes, n_ep, deck, ep_stride, ids.stride(1), kind, step,
+        ctypes.c_void_p(counts.data_ptr()), dev.index, ctypes.c_void_p(current_stream_handle(dev)),
+    )
+    check(code, "povs_travel_histogram_v1")
+
+
+def ngram_keys(ids: torch.Tensor, n: int, step: int, positions: torch.Tensor | None = None) -> torch.Tensor:
+    """int64 keys of every n-gram (anchored at ``positions`` or at every position) of every episode."""
+    lib = load()
+    id_bytes, n_ep, deck, ep_stride = _episode_layout(ids)
+    dev = ids.device
+    count = deck if positions is None else positions.numel()
+    keys = torch.empty(n_ep * count, dtype=torch.int64, device=dev)
+    if positions is not None:
+        assert positions.is_cuda and positions.dtype == torch.int64 and positions.is_contiguous()
+    code = lib.povs_ngram_keys_v1(
+        ctypes.c_void_p(ids.data_ptr()), id_bytes, n_ep, deck, ep_stride, ids.stride(1), n, step,
+        ctypes.c_void_p(positions.data_ptr()) if positions is not None else None, count if positions is not None else 0,
+        ctypes.c_void_p(keys.data_ptr()), dev.index, ctypes.c_void_p(current_stream_handle(dev)),
+    )
+    check(code, "povs_ngram_keys_v1")
+    return keys
 
 
 def shuffle_host(

@@ -101,8 +101,9 @@ def _gpu_episodes(it: int, randomness: str):
     n_ep = BIAS["episodes"]
     decks = torch.arange(N_ROWS, dtype=torch.int32, device="cuda:0")[None, :, None].repeat(n_ep, 1, WIDTH)
     flags = _native.FLAG_REFERENCE_RNG if randomness == "reference_cuda" else 0
-    for s in range(n_ep):
-        _native.shuffle_device(decks[s], WIDTH * 4, OFFSETS, it, P, V, s, flags)
+    # All episodes in one batched launch per iteration; episode s uses seed s.
+    seeds = torch.arange(n_ep, dtype=torch.int64, device="cuda:0")
+    _native.shuffle_batch(decks, WIDTH * 4, OFFSETS, it, P, V, seeds, flags)
     torch.cuda.synchronize()
     povs.check_device_status(0)
     flat = decks.cpu().numpy()

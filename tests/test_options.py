@@ -173,3 +173,12 @@ def test_seed_normalisation():
     assert isinstance(get_int_seed(None), int)
     with pytest.raises(TypeError):
         get_int_seed("seed")
+
+
+def test_thread_block_hint_for_small_vblocks():
+    """V * P below 32 (P = 8) is accepted with the minimum hint; larger hints are still rejected."""
+    _validate_thr_block_size(32, 2, 8)
+    with pytest.raises(AssertionError, match="must not exceed total instances"):
+        _validate_thr_block_size(64, 2, 8)
+    with pytest.raises(AssertionError, match="must not exceed total instances"):
+        _validate_thr_block_size(128, 4, 16)
