@@ -40,6 +40,10 @@ extern "C" {
  * xorshift32 forward Fisher-Yates, padding in the last vblock; src/povs/__cuda/lib/povs.cu:396-430,
  * 294-316) instead of uniform per-vblock permutations.  For statistical comparisons with it. */
 #define POVS_FLAG_REFERENCE_RNG 4u
+/* Chain the iterations of one call with ordinary stream order instead of programmatic dependent
+ * launches (by default iteration i+1's CTAs start their set-up while iteration i drains, and wait
+ * for it to complete before touching the deck). */
+#define POVS_FLAG_NO_PDL 8u
 
 /* Limits of this build. */
 #define POVS_MAX_OFFSETS 256 /* offsets are passed to the device inline in the launch parameters */

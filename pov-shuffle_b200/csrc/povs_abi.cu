@@ -101,9 +101,11 @@ std::mutex g_tuning_mu;
 struct GraphKey {
     KernelFn fn;
     int grid, block, smem, iterations;
+    bool pdl;
     bool operator==(const GraphKey& o) const
     {
-        return fn == o.fn && grid == o.grid && block == o.block && smem == o.smem && iterations == o.iterations;
+        return fn == o.fn && grid == o.grid && block == o.block && smem == o.smem && iterations == o.iterations &&
+               pdl == o.pdl;
     }
 };
 struct GraphKeyHash {
@@ -114,6 +116,7 @@ struct GraphKeyHash {
         h = h * 1000003u ^ static_cast<size_t>(k.block);
         h = h * 1000003u ^ static_cast<size_t>(k.smem);
         h = h * 1000003u ^ static_cast<size_t>(k.iterations);
+        h = h * 1000003u ^ static_cast<size_t>(k.pdl);
         return h;
     }
 };
@@ -352,21 +355,32 @@ void fill_geometry(IterParams& p, void* data, int64_t n_rows, int64_t row_bytes,
     p.deck_seeds = nullptr;
 }
 
-int launch_direct(const Plan& pl, const IterParams& p, cudaStream_t s)
+// `chained`: the launch follows another iteration kernel of the same call on `s`, so it may be
+// a programmatic dependent launch (the kernel waits for the previous grid before any data access).
+int launch_direct(const Plan& pl, const IterParams& p, cudaStream_t s, bool chained = false)
 {
     void* args[] = {const_cast<IterParams*>(&p)};
-    cudaError_t e = cudaLaunchKernel(reinterpret_cast<const void*>(pl.fn), dim3(pl.grid), dim3(pl.block), args,
-                                     static_cast<size_t>(pl.smem), s);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernel");
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(pl.grid);
+    cfg.blockDim = dim3(pl.block);
+    cfg.dynamicSmemBytes = static_cast<size_t>(pl.smem);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = chained ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(pl.fn), args);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelExC");
     return POVS_OK;
 }
 
 // Replays `iters` chained iteration kernels as one CUDA graph (cached per launch shape).
-int launch_graph(DeviceCtx& c, const Plan& pl, std::vector<IterParams>& ps, cudaStream_t s)
+int launch_graph(DeviceCtx& c, const Plan& pl, std::vector<IterParams>& ps, cudaStream_t s, bool pdl)
 {
     const int iters = static_cast<int>(ps.size());
     std::lock_guard<std::mutex> lk(c.mu);
-    GraphKey key{pl.fn, pl.grid, pl.block, pl.smem, iters};
+    GraphKey key{pl.fn, pl.grid, pl.block, pl.smem, iters, pdl};
     auto it = c.graphs.find(key);
     if (it == c.graphs.end()) {
         CachedGraph g;
@@ -381,7 +395,20 @@ int launch_graph(DeviceCtx& c, const Plan& pl, std::vector<IterParams>& ps, cuda
             kp.sharedMemBytes = static_cast<unsigned>(pl.smem);
             kp.kernelParams = args;
             cudaGraphNode_t node;
-            POVS_CUDA_TRY(cudaGraphAddKernelNode(&node, g.graph, prev ? &prev : nullptr, prev ? 1 : 0, &kp));
+            if (pdl) {
+                // Programmatic edge: iteration i+1 may launch once every CTA of iteration i has
+                // signalled (its movers still wait for iteration i to complete).
+                POVS_CUDA_TRY(cudaGraphAddKernelNode(&node, g.graph, nullptr, 0, &kp));
+                if (prev) {
+                    cudaGraphEdgeData ed{};
+                    ed.from_port = cudaGraphKernelNodePortProgrammatic;
+                    ed.to_port = 0;
+                    ed.type = cudaGraphDependencyTypeProgrammatic;
+                    POVS_CUDA_TRY(cudaGraphAddDependencies_v2(g.graph, &prev, &node, &ed, 1));
+                }
+            } else {
+                POVS_CUDA_TRY(cudaGraphAddKernelNode(&node, g.graph, prev ? &prev : nullptr, prev ? 1 : 0, &kp));
+            }
             g.nodes.push_back(node);
             prev = node;
         }
@@ -459,13 +486,14 @@ int shuffle_on_device(void* data, int64_t n_rows, int64_t row_bytes, const int64
     if (iterations == 0) return POVS_OK;
     std::vector<IterParams> ps(static_cast<size_t>(iterations), base);
     for (int i = 0; i < iterations; ++i) ps[i].iteration = static_cast<uint32_t>(i);
+    const bool pdl = (flags & POVS_FLAG_NO_PDL) == 0;
     if (iterations == 1 || (flags & POVS_FLAG_NO_GRAPH)) {
         for (int i = 0; i < iterations; ++i) {
-            r = launch_direct(pl, ps[i], s);
+            r = launch_direct(pl, ps[i], s, pdl && i > 0);
             if (r != POVS_OK) return r;
         }
     } else {
-        r = launch_graph(c, pl, ps, s);
+        r = launch_graph(c, pl, ps, s, pdl);
         if (r != POVS_OK) return r;
     }
     if (flags & POVS_FLAG_SYNC) {
@@ -1154,7 +1182,7 @@ extern "C" int povs_shuffle_batch_v1(void* data, int64_t n_decks, int64_t deck_s
     if (n_decks > 1 && deck_stride < n_rows * row_bytes)
         return fail(POVS_ERR_INVALID_ARGUMENT, "deck_stride (%lld) is smaller than a deck (%lld bytes)",
                     static_cast<long long>(deck_stride), static_cast<long long>(n_rows * row_bytes));
-    if ((flags & ~uint32_t{POVS_FLAG_NO_GRAPH | POVS_FLAG_SYNC | POVS_FLAG_REFERENCE_RNG}) != 0)
+    if ((flags & ~uint32_t{POVS_FLAG_NO_GRAPH | POVS_FLAG_SYNC | POVS_FLAG_REFERENCE_RNG | POVS_FLAG_NO_PDL}) != 0)
         return fail(POVS_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
     DeviceGuard dg;
     r = dg.enter(device);

@@ -173,6 +173,12 @@ __device__ __forceinline__ void bulk_load(void* dst_smem, const void* src_gmem, 
                  : "memory");
 }
 
+// Programmatic dependent launch: the next kernel of a chain may start its CTAs (set-up and
+// permutations, which read no data) while this grid drains; its movers wait for this grid's
+// completion and memory flush before touching the deck.  Both are no-ops for ordinary launches.
+__device__ __forceinline__ void allow_dependent_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void wait_for_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void fence_proxy_async_smem()
 {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -643,6 +649,7 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
     }
     mbar_fence_init();
     __syncthreads();
+    allow_dependent_launch();
 
     // Iteration-wide randomness (identical in every thread).
     int64_t offset;
@@ -900,6 +907,8 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
         }
     };
 
+    // Nothing of the deck is read or written before the previous iteration's grid has finished.
+    wait_for_prior_grid();
     const int64_t ahead = nst - 1;
     int64_t last_issued = -1;
     for (int64_t u = mw; u < ahead && u < n_units; u += n_movers) {

@@ -24,6 +24,7 @@ ERRORS = {-1: "invalid argument", -2: "unsupported", -3: "CUDA error", -4: "devi
 FLAG_NO_GRAPH = 1
 FLAG_SYNC = 2
 FLAG_REFERENCE_RNG = 4
+FLAG_NO_PDL = 8
 
 # (name, restype, argtypes) of every exported symbol declared in include/povs.h.
 _c_i32, _c_i64, _c_u32, _c_u64, _c_vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_void_p

@@ -94,6 +94,12 @@ def test_graph_and_direct_launches_agree(oracle_api):
     a = gpu_shuffle_bytes(host, 16, 4, [0, 1, 2, 3], 5, seed=9)
     b = gpu_shuffle_bytes(host, 16, 4, [0, 1, 2, 3], 5, seed=9, flags=_native.FLAG_NO_GRAPH)
     assert np.array_equal(a, b)
+    # Chained iterations without programmatic dependent launches (graph and direct).
+    for flags in (_native.FLAG_NO_PDL, _native.FLAG_NO_PDL | _native.FLAG_NO_GRAPH):
+        assert np.array_equal(a, gpu_shuffle_bytes(host, 16, 4, [0, 1, 2, 3], 5, seed=9, flags=flags))
+    want = host.copy()
+    oracle_api.shuffle(want, 5, 16, 4, [0, 1, 2, 3], 9)
+    assert np.array_equal(a, want)
     c = gpu_shuffle_bytes(host, 16, 4, [0, 1, 2, 3], 5, seed=10)
     assert not np.array_equal(a, c)
 
