@@ -301,7 +301,7 @@ def run_ours(args, w: dict, wname: str) -> None:
                 "peak_kind": roof_kind,
                 "unit": "GB/s",
                 "frac": round(achieved / roof_peak, 4),
-                "traffic": traffic_per_launch("povs_iteration_kernel", wname) if world == 1 else None,
+                "traffic": traffic_per_launch("povs_iteration_kernel", wname) if world == 1 and args.rows is None else None,
                 "alg_bytes_per_launch": 2 * deck_bytes // world,
                 "hbm_frac_per_gpu": round(2 * deck_bytes / world / per_launch_s / 1e9 / peak, 4),
             },
