@@ -417,7 +417,7 @@ def cpu_baseline(w: dict, threads: int, target_s: float) -> dict:
     rows = min(rows, max(probe_rows, (8 << 30) // R))  # at most 8 GiB of host memory
     t = run(rows) if rows != probe_rows else t_probe
     gbs = 2 * rows * R * iters / t / 1e9
-    return {
+    out = {
         "value": round(gbs, 3),
         "unit": "GB/s",
         "cores": threads,
@@ -425,6 +425,16 @@ def cpu_baseline(w: dict, threads: int, target_s: float) -> dict:
         "kind": "port",
         "sample": f"{rows:,} of {w['rows']:,} rows x {R} B, {iters} iterations, {t:.2f} s",
     }
+    if threads == 1:
+        # The reference's uniform baseline: numpy.random.Generator.shuffle of the rows (one full
+        # shuffle moves every byte once: 2 x bytes / time, the same unit as one POV iteration).
+        base = np.random.default_rng(w["seed"]).integers(0, 256, size=(rows, R), dtype=np.uint8)
+        t0 = time.perf_counter()
+        np.random.default_rng(w["seed"]).shuffle(base)
+        tn = time.perf_counter() - t0
+        out["numpy_shuffle"] = {"value": round(2 * rows * R / tn / 1e9, 3), "unit": "GB/s", "cores": 1,
+                                "sample": f"numpy Generator.shuffle of {rows:,} rows x {R} B, {tn:.2f} s"}
+    return out
 
 
 def run_reference(args, w: dict, wname: str) -> None:
@@ -449,7 +459,7 @@ def run_reference(args, w: dict, wname: str) -> None:
         "steps": args.steps,
         "warmup": args.warmup,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "u8",
         "data": "synthetic",

@@ -161,6 +161,13 @@ int povs_shuffle_sharded_v1(void* const* shard_ptrs, void* const* scratch_ptrs, 
                             void* const* peer_flags, uint32_t epoch_base, int32_t device, void* stream,
                             uint32_t flags);
 
+/*
+ * Time limit of the cross-GPU barrier between iterations of povs_shuffle_sharded_v1 (process-wide;
+ * 0 restores the default of 20 s).  A barrier that gives up sets POVS_DEV_PEER_TIMEOUT in the
+ * device status word and returns, so the context stays usable.  No reference counterpart.
+ */
+int povs_set_peer_wait_limit_v1(uint64_t limit_ns);
+
 /* CUDA IPC of device memory between the processes of a sharded deck (64-byte handles). */
 int povs_ipc_export_v1(const void* ptr, int32_t device, void* handle_out, int64_t* offset_out);
 int povs_ipc_import_v1(const void* handle, int64_t offset, int32_t device, void** ptr_out, void** base_out);

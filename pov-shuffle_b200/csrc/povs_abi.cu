@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -93,6 +94,7 @@ struct Tuning {
 };
 Tuning g_tuning;
 std::mutex g_tuning_mu;
+std::atomic<unsigned long long> g_peer_wait_ns{povs::PEER_WAIT_LIMIT_NS};
 
 // ------------------------------------------------------------------------------------------
 // Per-device context.
@@ -1052,6 +1054,7 @@ extern "C" int povs_shuffle_sharded_v1(void* const* shard_ptrs, void* const* scr
     q.n_ranks = n_shards;
     q.rank = rank;
     q.status = c->status;
+    q.limit_ns = g_peer_wait_ns.load();
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     auto barrier = [&](uint32_t epoch) -> int {
         q.epoch = epoch;
@@ -1289,5 +1292,12 @@ extern "C" int povs_ngram_keys_v1(const void* ids, int32_t id_bytes, int64_t n_e
     cudaError_t e = cudaLaunchKernel(reinterpret_cast<const void*>(povs::povs_ngram_keys_kernel), dim3(grid), dim3(256),
                                      args, 0, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernel(ngram keys)");
+    return POVS_OK;
+}
+
+extern "C" int povs_set_peer_wait_limit_v1(uint64_t limit_ns)
+{
+    g_err[0] = '\0';
+    g_peer_wait_ns.store(limit_ns == 0 ? povs::PEER_WAIT_LIMIT_NS : static_cast<unsigned long long>(limit_ns));
     return POVS_OK;
 }

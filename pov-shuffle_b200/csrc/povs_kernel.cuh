@@ -56,7 +56,7 @@ enum : int {
     DEV_ERR_PEER_TIMEOUT = 4, // a cross-GPU barrier gave up waiting for a peer
 };
 
-constexpr unsigned long long PEER_WAIT_LIMIT_NS = 20000000000ull; // 20 s for a peer GPU to reach the barrier
+constexpr unsigned long long PEER_WAIT_LIMIT_NS = 20000000000ull; // default: 20 s for a peer GPU to reach the barrier
 
 constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull; // 2 s: far beyond any legitimate wait
 
@@ -940,7 +940,7 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
 // Rank r writes `epoch` into slot r of every rank's flag array (system-scope release after a
 // system fence, so this GPU's earlier writes to peer shards are visible first), then waits until
 // every slot of its own array holds at least `epoch` (system-scope acquire).  The wait is bounded:
-// past PEER_WAIT_LIMIT_NS it records DEV_ERR_PEER_TIMEOUT and returns.
+// past limit_ns (default PEER_WAIT_LIMIT_NS) it records DEV_ERR_PEER_TIMEOUT and returns.
 // ---------------------------------------------------------------------------------------------
 
 struct PeerBarrierParams {
@@ -949,6 +949,7 @@ struct PeerBarrierParams {
     int32_t rank;
     uint32_t epoch;
     int* status;
+    unsigned long long limit_ns;
 };
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v)
@@ -974,7 +975,7 @@ __global__ void __launch_bounds__(32) povs_peer_barrier_kernel(const __grid_cons
         const unsigned long long t0 = global_timer_ns();
         while (static_cast<int32_t>(ld_acquire_sys(mine) - q.epoch) < 0) {
             __nanosleep(200);
-            if (global_timer_ns() - t0 > PEER_WAIT_LIMIT_NS) {
+            if (global_timer_ns() - t0 > q.limit_ns) {
                 atomicOr(q.status, DEV_ERR_PEER_TIMEOUT);
                 return;
             }

@@ -72,6 +72,7 @@ SIGNATURES: dict[str, tuple] = {
         ctypes.c_int,
         [_c_vp, _c_i32, _c_i64, _c_i64, _c_i64, _c_i64, _c_i32, _c_i64, _c_vp, _c_i64, _c_vp, _c_i32, _c_vp],
     ),
+    "povs_set_peer_wait_limit_v1": (ctypes.c_int, [_c_u64]),
     "povs_apply_static_v1": (
         ctypes.c_int,
         [_c_vp, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _P_I64, _c_vp, _c_vp, _c_i32, _c_i32, _c_vp, _c_u32],
@@ -406,6 +407,12 @@ def shuffle_sharded(
         ctypes.c_void_p(current_stream_handle(torch.device("cuda", device))), flags,
     )
     check(code, "povs_shuffle_sharded_v1")
+
+
+def set_peer_wait_limit(seconds: float | None) -> None:
+    """Time limit of the cross-GPU barrier of sharded shuffles (None: the default, 20 s)."""
+    check(load().povs_set_peer_wait_limit_v1(0 if seconds is None else max(1, int(seconds * 1e9))),
+          "povs_set_peer_wait_limit_v1")
 
 
 def ipc_export(ptr: int, device: int) -> tuple[bytes, int]:
