@@ -9,7 +9,8 @@
  *       path's member order as an option (src/povs/numpy.py:120-136);
  *   (2) this build's device randomness (Philox4x32-10 of Salmon et al., SC'11; a 12-round
  *       Feistel bijection with cycle walking for the pblock -> vblock map; per-vblock orders
- *       from sorting (key, element)), so the default GPU mode can be checked bit-exactly.
+ *       from sorting packed 32-bit (key | element) words), so the default GPU mode can be
+ *       checked bit-exactly.
  * Written independently of the CUDA sources; Philox is pinned by the Random123 known-answer
  * vectors in the tests.
  */
@@ -257,6 +258,17 @@ typedef struct {
     int32_t e;
 } keyed_t;
 
+/* Sort key of element e of a vblock of up to VP slots (the device's packed 32-bit key): the
+ * element's Philox word with its low idx_bits bits replaced by e, idx_bits = log2 of the sort width
+ * max(32, next power of two >= VP) (povs_kernel.cuh: PermKey, perm_sort_keys). */
+static uint64_t perm_sort_key(uint32_t w, int e, int VP)
+{
+    int width = 32;
+    while (width < VP) width <<= 1;
+    const uint32_t mask = (uint32_t)width - 1u;
+    return (uint64_t)((w & ~mask) | (uint32_t)e);
+}
+
 static int cmp_keyed(const void* a, const void* b)
 {
     const keyed_t* x = (const keyed_t*)a;
@@ -309,7 +321,7 @@ int oracle_device_randomness(uint64_t seed, uint32_t iteration, int64_t N, int P
             uint32_t w[4];
             draw(seed, (uint32_t)e >> 2, (uint32_t)v, ((uint32_t)((uint64_t)v >> 32) & 0x00FFFFFFu) | ((uint32_t)DOM_PERM << 24),
                  iteration, w);
-            keys[e].key = ((uint64_t)w[e & 3] << 32) | (uint32_t)e;
+            keys[e].key = perm_sort_key(w[e & 3], e, VP);
             keys[e].e = e;
         }
         qsort(keys, (size_t)n_valid, sizeof(keyed_t), cmp_keyed);
@@ -391,7 +403,7 @@ static void* mt_worker(void* arg)
             uint32_t w[4];
             draw(t->seed, (uint32_t)e >> 2, (uint32_t)v,
                  ((uint32_t)((uint64_t)v >> 32) & 0x00FFFFFFu) | ((uint32_t)DOM_PERM << 24), t->iteration, w);
-            keys[e].key = ((uint64_t)w[e & 3] << 32) | (uint32_t)e;
+            keys[e].key = perm_sort_key(w[e & 3], e, t->V * t->P);
             keys[e].e = e;
         }
         qsort(keys, (size_t)n_valid, sizeof(keyed_t), cmp_keyed);

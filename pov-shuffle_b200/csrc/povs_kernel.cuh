@@ -209,23 +209,23 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* s
 }
 
 // ---------------------------------------------------------------------------------------------
-// Register bitonic sort over one warp: n = 32 * EPL 64-bit values, lane l owns elements
+// Register bitonic sort over one warp: n = 32 * EPL values (T = uint32_t), lane l owns elements
 // l*EPL .. l*EPL+EPL-1.  Ascending.  For distances j >= EPL the partner is in lane l ^ (j/EPL)
 // at the same register; the direction bits of the element index then depend on the lane only.
 // ---------------------------------------------------------------------------------------------
 
 // Compare-exchange of registers r and r|j inside one lane (ascending when `up`).
-template <int EPL>
-__device__ __forceinline__ void cx_regs(uint64_t (&x)[EPL], int r, int j, bool up)
+template <int EPL, typename T>
+__device__ __forceinline__ void cx_regs(T (&x)[EPL], int r, int j, bool up)
 {
-    const uint64_t a = x[r], b = x[r | j];
-    const bool swap = up ? (a > b) : (a < b);
-    x[r] = swap ? b : a;
-    x[r | j] = swap ? a : b;
+    const T a = x[r], b = x[r | j];
+    const T lo = min(a, b), hi = max(a, b);
+    x[r] = up ? lo : hi;
+    x[r | j] = up ? hi : lo;
 }
 
-template <int EPL>
-__device__ __forceinline__ void warp_bitonic_sort(uint64_t (&x)[EPL], int lane)
+template <int EPL, typename T>
+__device__ __forceinline__ void warp_bitonic_sort(T (&x)[EPL], int lane)
 {
     const int base = lane * EPL; // element index of register 0 (its low log2(EPL) bits are zero)
     // Phases k = 2 .. EPL sort within each lane's registers (compile-time network).
@@ -237,7 +237,7 @@ __device__ __forceinline__ void warp_bitonic_sort(uint64_t (&x)[EPL], int lane)
             for (int r = 0; r < EPL; ++r) {
                 if ((r & j) == 0) {
                     const bool up = (k == EPL) ? ((base & k) == 0) : ((r & k) == 0);
-                    cx_regs<EPL>(x, r, j, up);
+                    cx_regs<EPL, T>(x, r, j, up);
                 }
             }
         }
@@ -254,25 +254,36 @@ __device__ __forceinline__ void warp_bitonic_sort(uint64_t (&x)[EPL], int lane)
             const int lm = j / EPL;
 #pragma unroll
             for (int r = 0; r < EPL; ++r) {
-                const uint64_t y = __shfl_xor_sync(FULL_MASK, x[r], lm);
-                x[r] = ((x[r] < y) == keep_min) ? x[r] : y;
+                const T y = __shfl_xor_sync(FULL_MASK, x[r], lm);
+                x[r] = keep_min ? min(x[r], y) : max(x[r], y);
             }
         }
 #pragma unroll
         for (int j = EPL >> 1; j > 0; j >>= 1) {
 #pragma unroll
             for (int r = 0; r < EPL; ++r)
-                if ((r & j) == 0) cx_regs<EPL>(x, r, j, up);
+                if ((r & j) == 0) cx_regs<EPL, T>(x, r, j, up);
         }
     }
 }
 
-// Generates the permutation of one vblock: perm[f] = source slot of destination slot f, f < n_valid.
+// Sort keys of a vblock's elements e = 0 .. 32*EPL-1: the element's 32-bit Philox word with its
+// low IDX_BITS bits replaced by e (so keys are distinct and the sort is a permutation).  Elements
+// past n_valid get all high bits set: they sort after every valid element (same high bits: the
+// larger index).  The order of the valid keys is a uniformly random permutation except where two
+// elements' high bits tie (probability below n^2 / 2^(33 - IDX_BITS) per vblock), whose relative
+// order is then their index order.
 template <int EPL>
-__device__ __forceinline__ void warp_make_perm(const IterParams& p, uint64_t seed, uint64_t vblock, int n_valid,
-                                               uint16_t* perm, int lane)
+struct PermKey {
+    static constexpr int IDX_BITS = EPL >= 32 ? 10 : EPL >= 16 ? 9 : EPL >= 8 ? 8 : EPL >= 4 ? 7 : EPL >= 2 ? 6 : 5;
+    static constexpr uint32_t IDX_MASK = (1u << IDX_BITS) - 1u;
+};
+
+template <int EPL>
+__device__ __forceinline__ void perm_sort_keys(const IterParams& p, uint64_t seed, uint64_t vblock, int n_valid,
+                                               uint32_t (&x)[EPL], int lane)
 {
-    uint64_t x[EPL];
+    constexpr uint32_t M = PermKey<EPL>::IDX_MASK;
     if constexpr (EPL >= 4) {
 #pragma unroll
         for (int q = 0; q < EPL / 4; ++q) {
@@ -282,8 +293,7 @@ __device__ __forceinline__ void warp_make_perm(const IterParams& p, uint64_t see
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
                 const uint32_t e = quad * 4u + t;
-                x[4 * q + t] =
-                    (static_cast<int>(e) < n_valid) ? ((static_cast<uint64_t>(w[t]) << 32) | e) : ~uint64_t{0};
+                x[4 * q + t] = ((static_cast<int>(e) < n_valid) ? (w[t] & ~M) : ~M) | e;
             }
         }
     } else {
@@ -292,16 +302,23 @@ __device__ __forceinline__ void warp_make_perm(const IterParams& p, uint64_t see
 #pragma unroll
         for (int r = 0; r < EPL; ++r) {
             const uint32_t e = e0 + r;
-            x[r] = (static_cast<int>(e) < n_valid)
-                       ? ((static_cast<uint64_t>(pick_word(k, static_cast<int>(e & 3u))) << 32) | e)
-                       : ~uint64_t{0};
+            x[r] = ((static_cast<int>(e) < n_valid) ? (pick_word(k, static_cast<int>(e & 3u)) & ~M) : ~M) | e;
         }
     }
-    warp_bitonic_sort<EPL>(x, lane);
+}
+
+// Generates the permutation of one vblock: perm[f] = source slot of destination slot f, f < n_valid.
+template <int EPL>
+__device__ __forceinline__ void warp_make_perm(const IterParams& p, uint64_t seed, uint64_t vblock, int n_valid,
+                                               uint16_t* perm, int lane)
+{
+    uint32_t x[EPL];
+    perm_sort_keys<EPL>(p, seed, vblock, n_valid, x, lane);
+    warp_bitonic_sort<EPL, uint32_t>(x, lane);
 #pragma unroll
     for (int r = 0; r < EPL; ++r) {
         const int f = lane * EPL + r;
-        if (f < n_valid) perm[f] = static_cast<uint16_t>(x[r] & 0xffffu);
+        if (f < n_valid) perm[f] = static_cast<uint16_t>(x[r] & PermKey<EPL>::IDX_MASK);
     }
 }
 
@@ -536,36 +553,13 @@ template <int EPL>
 __device__ __forceinline__ void warp_make_pos(const IterParams& p, uint64_t seed, uint64_t vblock, int n_valid,
                                               int first, int count, uint16_t* pos, int lane)
 {
-    uint64_t x[EPL];
-    if constexpr (EPL >= 4) {
-#pragma unroll
-        for (int q = 0; q < EPL / 4; ++q) {
-            const uint32_t quad = static_cast<uint32_t>((lane * EPL) / 4 + q);
-            const U32x4 k = perm_key4(seed, p.iteration, vblock, quad);
-            const uint32_t w[4] = {k.x, k.y, k.z, k.w};
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                const uint32_t e = quad * 4u + t;
-                x[4 * q + t] =
-                    (static_cast<int>(e) < n_valid) ? ((static_cast<uint64_t>(w[t]) << 32) | e) : ~uint64_t{0};
-            }
-        }
-    } else {
-        const uint32_t e0 = static_cast<uint32_t>(lane * EPL);
-        const U32x4 k = perm_key4(seed, p.iteration, vblock, e0 >> 2);
-#pragma unroll
-        for (int r = 0; r < EPL; ++r) {
-            const uint32_t e = e0 + r;
-            x[r] = (static_cast<int>(e) < n_valid)
-                       ? ((static_cast<uint64_t>(pick_word(k, static_cast<int>(e & 3u))) << 32) | e)
-                       : ~uint64_t{0};
-        }
-    }
-    warp_bitonic_sort<EPL>(x, lane);
+    uint32_t x[EPL];
+    perm_sort_keys<EPL>(p, seed, vblock, n_valid, x, lane);
+    warp_bitonic_sort<EPL, uint32_t>(x, lane);
 #pragma unroll
     for (int r = 0; r < EPL; ++r) {
         const int f = lane * EPL + r;
-        const int e = static_cast<int>(x[r] & 0xffffu) - first;
+        const int e = static_cast<int>(x[r] & PermKey<EPL>::IDX_MASK) - first;
         if (f < n_valid && e >= 0 && e < count) pos[e] = static_cast<uint16_t>(f);
     }
 }
