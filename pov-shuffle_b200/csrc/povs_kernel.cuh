@@ -453,45 +453,83 @@ __device__ __forceinline__ const uint8_t* src_row_ptr(const StageMeta& m, int i,
     return reinterpret_cast<const uint8_t*>(base + static_cast<uintptr_t>(static_cast<int64_t>(i) * row_bytes));
 }
 
+// A slab of slen bytes per row as W-byte chunks over a warp: cpr chunks per row, g rows per warp
+// instruction, lane -> (row lrow, chunk lq).  Shifts instead of divisions when cpr is a power of two.
+struct LaneGeom {
+    int cpr, g, lrow, lq, g_shift; // g_shift = log2(g), or -1 when g is not a power of two
+    __device__ __forceinline__ int passes(int n) const { return g_shift >= 0 ? (n + g - 1) >> g_shift : (n + g - 1) / g; }
+};
+
+template <int W>
+__device__ __forceinline__ LaneGeom lane_geom(int slen, int lane)
+{
+    LaneGeom lg;
+    lg.cpr = slen / W;
+    if (lg.cpr >= 32) {
+        lg.g = 1;
+        lg.lrow = 0;
+        lg.lq = lane;
+        lg.g_shift = 0;
+    } else if ((lg.cpr & (lg.cpr - 1)) == 0) {
+        const int cs = __ffs(lg.cpr) - 1;
+        lg.g = 32 >> cs;
+        lg.lrow = lane >> cs;
+        lg.lq = lane & (lg.cpr - 1);
+        lg.g_shift = 5 - cs;
+    } else {
+        lg.g = 32 / lg.cpr;
+        lg.lrow = lane / lg.cpr;
+        lg.lq = lane - lg.lrow * lg.cpr;
+        lg.g_shift = -1;
+    }
+    return lg;
+}
+
 // Identity-order copy global -> stage by one warp (plain loads): the unit's valid rows (in place),
-// or the rows of the unit's own member (push).
+// or the rows of the unit's own member (push).  Several loads per lane are in flight.
 template <int W, bool PUSH>
 __device__ __forceinline__ void lsu_load_unit(const IterParams& p, const StageMeta& m, uint8_t* stage, int64_t col,
                                               int slen, int lane)
 {
     using T = typename VecOf<W>::T;
-    const int cpr = slen / W;
+    const LaneGeom lg = lane_geom<W>(slen, lane);
     const int pmask = p.pblock - 1;
     const int n = PUSH ? m.rows_mine : m.n_valid;
     auto src_of = [&](int f) -> const uint8_t* {
         if constexpr (PUSH) return src_row_ptr(m, f, p.row_bytes) + col;
         else return slot_ptr(m, f, p.pblock_shift, pmask, p.row_bytes) + col;
     };
-    if (cpr >= 32) {
+    if (lg.cpr >= 32) {
         for (int f = 0; f < n; ++f) {
             const T* src = reinterpret_cast<const T*>(src_of(f));
             T* dst = reinterpret_cast<T*>(stage + static_cast<size_t>(f) * p.slab_bytes);
-            for (int q = lane; q < cpr; q += 32) dst[q] = src[q];
+            for (int q = lane; q < lg.cpr; q += 32) dst[q] = src[q];
         }
-    } else {
-        const int g = 32 / cpr;
-        const int lrow = lane / cpr, lq = lane - lrow * cpr;
-        if (lrow < g) {
-#pragma unroll 4
-            for (int f = lrow; f < n; f += g) {
-                const T* src = reinterpret_cast<const T*>(src_of(f));
-                T* dst = reinterpret_cast<T*>(stage + static_cast<size_t>(f) * p.slab_bytes);
-                dst[lq] = src[lq];
+    } else if (lg.lrow < lg.g) {
+        constexpr int UL = W >= 8 ? 4 : 8; // loads in flight per lane (wide chunks cost registers)
+        for (int f0 = lg.lrow; f0 < n; f0 += UL * lg.g) {
+            T v[UL];
+#pragma unroll
+            for (int u = 0; u < UL; ++u) {
+                const int f = f0 + u * lg.g;
+                if (f < n) v[u] = reinterpret_cast<const T*>(src_of(f))[lg.lq];
+            }
+#pragma unroll
+            for (int u = 0; u < UL; ++u) {
+                const int f = f0 + u * lg.g;
+                if (f < n) reinterpret_cast<T*>(stage + static_cast<size_t>(f) * p.slab_bytes)[lg.lq] = v[u];
             }
         }
     }
 }
 
-// This warp's share of the copy stage -> global.  In place: destination slot f receives stage row
+// store_share with the lane geometry computed by divisions: the form the bulk (TMA) path uses,
+// where it measured faster than the shift form below (the per-unit share of this arithmetic is
+// small there).  This warp's share of the copy stage -> global.  In place: destination slot f receives stage row
 // idx[f] (idx = the permutation).  Push: stage row f (the unit's own member) goes to destination
 // slot idx[f] (idx = the member's destination slots).  Work items are interleaved over the warps.
 template <int W, bool PUSH>
-__device__ __forceinline__ void store_share(const IterParams& p, const StageMeta& m, const uint8_t* stage,
+__device__ __forceinline__ void store_share_div(const IterParams& p, const StageMeta& m, const uint8_t* stage,
                                             const uint16_t* idx, int64_t col, int slen, int lane, int warp,
                                             int n_warps)
 {
@@ -519,6 +557,66 @@ __device__ __forceinline__ void store_share(const IterParams& p, const StageMeta
         const int lrow = lane / cpr, lq = lane - lrow * cpr;
         if (lrow >= g) return;
         const int n_pass = (n + g - 1) / g;
+        constexpr int U = 4;
+        int t = warp;
+        for (; t + (U - 1) * n_warps < n_pass; t += U * n_warps) {
+            T v[U];
+            T* dst[U];
+            bool ok[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int f = (t + u * n_warps) * g + lrow;
+                ok[u] = f < n;
+                const int fs = ok[u] ? f : 0;
+                dst[u] = reinterpret_cast<T*>(slot_ptr(m, dst_slot(fs), p.pblock_shift, pmask, p.row_bytes) + col) + lq;
+                v[u] = reinterpret_cast<const T*>(stage + static_cast<size_t>(src_row(fs)) * p.slab_bytes)[lq];
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+                if (ok[u]) *dst[u] = v[u];
+        }
+        for (; t < n_pass; t += n_warps) {
+            const int f = t * g + lrow;
+            if (f < n) {
+                const T v = reinterpret_cast<const T*>(stage + static_cast<size_t>(src_row(f)) * p.slab_bytes)[lq];
+                reinterpret_cast<T*>(slot_ptr(m, dst_slot(f), p.pblock_shift, pmask, p.row_bytes) + col)[lq] = v;
+            }
+        }
+    }
+}
+
+// This warp's share of the copy stage -> global.  In place: destination slot f receives stage row
+// idx[f] (idx = the permutation).  Push: stage row f (the unit's own member) goes to destination
+// slot idx[f] (idx = the member's destination slots).  Work items are interleaved over the warps.
+template <int W, bool PUSH>
+__device__ __forceinline__ void store_share(const IterParams& p, const StageMeta& m, const uint8_t* stage,
+                                            const uint16_t* idx, int64_t col, int slen, int lane, int warp,
+                                            int n_warps)
+{
+    using T = typename VecOf<W>::T;
+    const LaneGeom lg = lane_geom<W>(slen, lane);
+    const int cpr = lg.cpr;
+    const int pmask = p.pblock - 1;
+    const int n = PUSH ? m.rows_mine : m.n_valid;
+    auto src_row = [&](int f) -> int {
+        if constexpr (PUSH) return f;
+        else return idx[f];
+    };
+    auto dst_slot = [&](int f) -> int {
+        if constexpr (PUSH) return idx[f];
+        else return f;
+    };
+    if (cpr >= 32) {
+        for (int f = warp; f < n; f += n_warps) {
+            const T* src = reinterpret_cast<const T*>(stage + static_cast<size_t>(src_row(f)) * p.slab_bytes);
+            T* dst = reinterpret_cast<T*>(slot_ptr(m, dst_slot(f), p.pblock_shift, pmask, p.row_bytes) + col);
+#pragma unroll 4
+            for (int q = lane; q < cpr; q += 32) dst[q] = src[q];
+        }
+    } else {
+        const int g = lg.g, lrow = lg.lrow, lq = lg.lq;
+        if (lrow >= g) return;
+        const int n_pass = lg.passes(n);
         constexpr int U = 4;
         int t = warp;
         for (; t + (U - 1) * n_warps < n_pass; t += U * n_warps) {
@@ -620,6 +718,24 @@ __device__ __forceinline__ void locate_run(const IterParams& p, uint8_t* const* 
     n_a = na;
 }
 
+// Position of unit u in a ring of n entries: i = u % n and the phase bit ph = (u / n) & 1,
+// advanced one unit at a time without divisions.
+struct RingPos {
+    uint32_t i, ph;
+    __device__ __forceinline__ void next(uint32_t n)
+    {
+        if (++i == n) {
+            i = 0;
+            ph ^= 1u;
+        }
+    }
+};
+
+__device__ __forceinline__ RingPos ring_at(uint64_t u, uint32_t n)
+{
+    return RingPos{static_cast<uint32_t>(u % n), static_cast<uint32_t>((u / n) & 1u)};
+}
+
 template <int EPL, bool INJECTED, bool BULK, bool PUSH>
 __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_constant__ IterParams p)
 {
@@ -682,10 +798,38 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
         int64_t deck = -1; // batched decks: none drawn yet
         int64_t deck_offset = offset;
         const int q = warp - n_movers;
+        // Unit u = q, q + n_permuters, ...: its slot (u % kp, phase) and its list entry / slab
+        // (u / n_slabs, u % n_slabs) advance without divisions (n_permuters < kp).
+        const uint32_t step_e = static_cast<uint32_t>(p.n_permuters / p.n_slabs);
+        const uint32_t step_s = static_cast<uint32_t>(p.n_permuters % p.n_slabs);
+        RingPos kr = ring_at(static_cast<uint64_t>(q), static_cast<uint32_t>(kp));
+        int64_t entry_local = q / p.n_slabs;
+        uint32_t slab_q = static_cast<uint32_t>(q % p.n_slabs);
         for (int64_t u = q; u < n_units; u += p.n_permuters) {
-            const int k = static_cast<int>(u % kp);
-            if (u >= kp && !warp_wait(&sm.pempty[k], static_cast<uint32_t>(((u / kp) - 1) & 1), p.status)) return;
-            const int64_t entry = blockIdx.x + (u / p.n_slabs) * static_cast<int64_t>(gridDim.x);
+            int k;
+            int64_t entry;
+            if constexpr (BULK) {
+                // Bulk path: positions recomputed per unit (measured faster there).
+                k = static_cast<int>(u % kp);
+                if (u >= kp && !warp_wait(&sm.pempty[k], static_cast<uint32_t>(((u / kp) - 1) & 1), p.status)) return;
+                entry = blockIdx.x + (u / p.n_slabs) * static_cast<int64_t>(gridDim.x);
+            } else {
+                k = static_cast<int>(kr.i);
+                if (u >= kp && !warp_wait(&sm.pempty[k], kr.ph ^ 1u, p.status)) return;
+                entry = blockIdx.x + entry_local * static_cast<int64_t>(gridDim.x);
+                // Advance to this warp's next unit.
+                kr.i += static_cast<uint32_t>(p.n_permuters);
+                if (kr.i >= static_cast<uint32_t>(kp)) {
+                    kr.i -= static_cast<uint32_t>(kp);
+                    kr.ph ^= 1u;
+                }
+                entry_local += step_e;
+                slab_q += step_s;
+                if (slab_q >= static_cast<uint32_t>(p.n_slabs)) {
+                    slab_q -= static_cast<uint32_t>(p.n_slabs);
+                    ++entry_local;
+                }
+            }
             int64_t v;
             int64_t own = -1;  // push: the unit's own pblock
             int own_lane = 0;  // push: its slot within the vblock
@@ -800,22 +944,27 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
 
     // ---------------------------------------------------------------------- mover warps
     const int mw = warp;
+    // Nothing of the deck is read or written before the previous iteration's grid has finished.
+    wait_for_prior_grid();
+    const int64_t ahead = nst - 1;
+    int64_t last_issued = -1;
 
-    // Issues unit u into stage u % nst (called by mover u % n_movers).  Returns false on a timeout.
-    auto issue = [&](int64_t u) -> bool {
-        const int st = static_cast<int>(u % nst);
-        const int k = static_cast<int>(u % kp);
-        if (!warp_wait(&sm.pfull[k], static_cast<uint32_t>((u / kp) & 1), p.status)) return false;
-        if (u >= nst && !warp_wait(&sm.empty[st], static_cast<uint32_t>(((u / nst) - 1) & 1), p.status))
-            return false;
-        fence_proxy_async_smem();
-        const StageMeta& m = sm.meta[k];
-        const int n_load = PUSH ? m.rows_mine : m.n_valid;
-        const int slab = static_cast<int>(u % p.n_slabs);
-        const int64_t col = static_cast<int64_t>(slab) * p.slab_bytes;
-        const int slen = static_cast<int>(min(static_cast<int64_t>(p.slab_bytes), p.row_bytes - col));
-        uint8_t* stage = sm.data + static_cast<size_t>(st) * p.stage_bytes;
-        if constexpr (BULK) {
+    if constexpr (BULK) {
+        // TMA bulk loads.  Unit u's stage (u % nst), permutation slot (u % kp) and phases are
+        // recomputed per unit (on large units this measured faster than carrying ring counters).
+        auto issue = [&](int64_t u) -> bool {
+            const int st = static_cast<int>(u % nst);
+            const int k = static_cast<int>(u % kp);
+            if (!warp_wait(&sm.pfull[k], static_cast<uint32_t>((u / kp) & 1), p.status)) return false;
+            if (u >= nst && !warp_wait(&sm.empty[st], static_cast<uint32_t>(((u / nst) - 1) & 1), p.status))
+                return false;
+            fence_proxy_async_smem();
+            const StageMeta& m = sm.meta[k];
+            const int n_load = PUSH ? m.rows_mine : m.n_valid;
+            const int slab = static_cast<int>(u % p.n_slabs);
+            const int64_t col = static_cast<int64_t>(slab) * p.slab_bytes;
+            const int slen = static_cast<int>(min(static_cast<int64_t>(p.slab_bytes), p.row_bytes - col));
+            uint8_t* stage = sm.data + static_cast<size_t>(st) * p.stage_bytes;
             if (lane == 0) mbar_expect_tx(&sm.full[st], static_cast<uint32_t>(n_load) * static_cast<uint32_t>(slen));
             __syncwarp();
             if (p.n_slabs == 1) {
@@ -852,7 +1001,65 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
                               &sm.full[st]);
                 }
             }
-        } else {
+            mbar_arrive(&sm.full[st]);
+            return true;
+        };
+        auto store = [&](int64_t j) -> bool {
+            const int st = static_cast<int>(j % nst);
+            const int k = static_cast<int>(j % kp);
+            if (!warp_wait(&sm.full[st], static_cast<uint32_t>((j / nst) & 1), p.status)) return false;
+            const StageMeta& m = sm.meta[k];
+            const uint16_t* idx = PUSH ? sm.pos + static_cast<size_t>(k) * sm.pos_stride
+                                       : sm.perm + static_cast<size_t>(k) * sm.perm_stride;
+            const uint8_t* stage = sm.data + static_cast<size_t>(st) * p.stage_bytes;
+            const int slab = static_cast<int>(j % p.n_slabs);
+            const int64_t col = static_cast<int64_t>(slab) * p.slab_bytes;
+            const int slen = static_cast<int>(min(static_cast<int64_t>(p.slab_bytes), p.row_bytes - col));
+            store_share_div<16, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers);
+            mbar_arrive(&sm.empty[st]);  // this thread's reads of the data stage are done
+            mbar_arrive(&sm.pempty[k]);  // ... and of the permutation slot
+            return true;
+        };
+        // On a timeout: wait (bounded) for the copies of the units this warp issued and stop.
+        auto drain_and_stop = [&](int64_t from) {
+            for (int64_t u = from; u <= last_issued; ++u)
+                if (u % n_movers == mw) warp_wait(&sm.full[u % nst], static_cast<uint32_t>((u / nst) & 1), p.status);
+        };
+        for (int64_t u = mw; u < ahead && u < n_units; u += n_movers) {
+            if (!issue(u)) {
+                drain_and_stop(0);
+                return;
+            }
+            last_issued = u;
+        }
+        // Store before issuing: the issue of unit j+NST-1 waits for every mover's share of unit j-1.
+        for (int64_t j = 0; j < n_units; ++j) {
+            if (!store(j)) {
+                drain_and_stop(j);
+                return;
+            }
+            const int64_t u = j + ahead;
+            if (u < n_units && u % n_movers == mw) {
+                if (!issue(u)) {
+                    drain_and_stop(j + 1);
+                    return;
+                }
+                last_issued = u;
+            }
+        }
+    } else {
+        // Plain vector loads (rows not a multiple of 16 bytes, or an unaligned deck).  The stage and
+        // slot ring positions are carried from unit to unit without divisions: with small rows the
+        // per-unit bookkeeping is a visible share of the work.
+        auto issue = [&](RingPos sr, RingPos kr, int slab, bool wait_empty) -> bool {
+            const int st = static_cast<int>(sr.i);
+            const int k = static_cast<int>(kr.i);
+            if (!warp_wait(&sm.pfull[k], kr.ph, p.status)) return false;
+            if (wait_empty && !warp_wait(&sm.empty[st], sr.ph ^ 1u, p.status)) return false;
+            const StageMeta& m = sm.meta[k];
+            const int64_t col = static_cast<int64_t>(slab) * p.slab_bytes;
+            const int slen = static_cast<int>(min(static_cast<int64_t>(p.slab_bytes), p.row_bytes - col));
+            uint8_t* stage = sm.data + static_cast<size_t>(st) * p.stage_bytes;
             switch (p.vec_bytes) {
             case 16: lsu_load_unit<16, PUSH>(p, m, stage, col, slen, lane); break;
             case 8: lsu_load_unit<8, PUSH>(p, m, stage, col, slen, lane); break;
@@ -861,25 +1068,19 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
             default: lsu_load_unit<1, PUSH>(p, m, stage, col, slen, lane); break;
             }
             __syncwarp();
-        }
-        mbar_arrive(&sm.full[st]);
-        return true;
-    };
-
-    auto store = [&](int64_t j) -> bool {
-        const int st = static_cast<int>(j % nst);
-        const int k = static_cast<int>(j % kp);
-        if (!warp_wait(&sm.full[st], static_cast<uint32_t>((j / nst) & 1), p.status)) return false;
-        const StageMeta& m = sm.meta[k];
-        const uint16_t* idx = PUSH ? sm.pos + static_cast<size_t>(k) * sm.pos_stride
-                                   : sm.perm + static_cast<size_t>(k) * sm.perm_stride;
-        const uint8_t* stage = sm.data + static_cast<size_t>(st) * p.stage_bytes;
-        const int slab = static_cast<int>(j % p.n_slabs);
-        const int64_t col = static_cast<int64_t>(slab) * p.slab_bytes;
-        const int slen = static_cast<int>(min(static_cast<int64_t>(p.slab_bytes), p.row_bytes - col));
-        if constexpr (BULK) {
-            store_share<16, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers);
-        } else {
+            mbar_arrive(&sm.full[st]);
+            return true;
+        };
+        auto store = [&](RingPos sr, RingPos kr, int slab) -> bool {
+            const int st = static_cast<int>(sr.i);
+            const int k = static_cast<int>(kr.i);
+            if (!warp_wait(&sm.full[st], sr.ph, p.status)) return false;
+            const StageMeta& m = sm.meta[k];
+            const uint16_t* idx = PUSH ? sm.pos + static_cast<size_t>(k) * sm.pos_stride
+                                       : sm.perm + static_cast<size_t>(k) * sm.perm_stride;
+            const uint8_t* stage = sm.data + static_cast<size_t>(st) * p.stage_bytes;
+            const int64_t col = static_cast<int64_t>(slab) * p.slab_bytes;
+            const int slen = static_cast<int>(min(static_cast<int64_t>(p.slab_bytes), p.row_bytes - col));
             switch (p.vec_bytes) {
             case 16: store_share<16, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
             case 8: store_share<8, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
@@ -887,44 +1088,40 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
             case 2: store_share<2, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
             default: store_share<1, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
             }
-        }
-        mbar_arrive(&sm.empty[st]);  // this thread's reads of the data stage are done
-        mbar_arrive(&sm.pempty[k]);  // ... and of the permutation slot
-        return true;
-    };
-
-    // On a timeout: wait (bounded) for the copies of the units this warp issued and stop.
-    auto drain_and_stop = [&](int64_t from, int64_t last_issued) {
-        if constexpr (BULK) {
-            for (int64_t u = from; u <= last_issued; ++u)
-                if (u % n_movers == mw) warp_wait(&sm.full[u % nst], static_cast<uint32_t>((u / nst) & 1), p.status);
-        }
-    };
-
-    // Nothing of the deck is read or written before the previous iteration's grid has finished.
-    wait_for_prior_grid();
-    const int64_t ahead = nst - 1;
-    int64_t last_issued = -1;
-    for (int64_t u = mw; u < ahead && u < n_units; u += n_movers) {
-        if (!issue(u)) {
-            drain_and_stop(0, last_issued);
-            return;
-        }
-        last_issued = u;
-    }
-    // Store before issuing: the issue of unit j+NST-1 waits for every mover's share of unit j-1.
-    for (int64_t j = 0; j < n_units; ++j) {
-        if (!store(j)) {
-            drain_and_stop(j, last_issued);
-            return;
-        }
-        const int64_t u = j + ahead;
-        if (u < n_units && u % n_movers == mw) {
-            if (!issue(u)) {
-                drain_and_stop(j + 1, last_issued);
+            mbar_arrive(&sm.empty[st]);  // this thread's reads of the data stage are done
+            mbar_arrive(&sm.pempty[k]);  // ... and of the permutation slot
+            return true;
+        };
+        // Plain loads complete before a unit's `full` arrival, so a timeout needs no draining.
+        (void)last_issued;
+        const uint32_t n_slabs = static_cast<uint32_t>(p.n_slabs);
+        for (int64_t u = mw; u < ahead && u < n_units; u += n_movers) {
+            if (!issue(ring_at(static_cast<uint64_t>(u), static_cast<uint32_t>(nst)),
+                       ring_at(static_cast<uint64_t>(u), static_cast<uint32_t>(kp)),
+                       static_cast<int>(static_cast<uint64_t>(u) % n_slabs), u >= nst))
                 return;
+        }
+        // Store before issuing: the issue of unit j+NST-1 waits for every mover's share of unit j-1.
+        // Ring positions of unit j (stores) and of unit j + ahead (issues) advance one unit per step.
+        RingPos sj{0u, 0u}, kj{0u, 0u};
+        uint32_t slab_j = 0;
+        RingPos su = ring_at(static_cast<uint64_t>(ahead), static_cast<uint32_t>(nst));
+        RingPos ku = ring_at(static_cast<uint64_t>(ahead), static_cast<uint32_t>(kp));
+        uint32_t slab_u = static_cast<uint32_t>(static_cast<uint64_t>(ahead) % n_slabs);
+        uint32_t mover_u = static_cast<uint32_t>(ahead % n_movers);
+        for (int64_t j = 0; j < n_units; ++j) {
+            if (!store(sj, kj, static_cast<int>(slab_j))) return;
+            const int64_t u = j + ahead;
+            if (u < n_units && mover_u == static_cast<uint32_t>(mw)) {
+                if (!issue(su, ku, static_cast<int>(slab_u), u >= nst)) return;
             }
-            last_issued = u;
+            sj.next(static_cast<uint32_t>(nst));
+            kj.next(static_cast<uint32_t>(kp));
+            su.next(static_cast<uint32_t>(nst));
+            ku.next(static_cast<uint32_t>(kp));
+            if (++slab_j == n_slabs) slab_j = 0;
+            if (++slab_u == n_slabs) slab_u = 0;
+            if (++mover_u == static_cast<uint32_t>(n_movers)) mover_u = 0;
         }
     }
 }
