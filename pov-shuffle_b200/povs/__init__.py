@@ -113,11 +113,17 @@ def shuffle_batch(
     povs_torch.shuffle_batch(decks, iterations, options, per_deck)
 
 
-def optim_options_for_dataset(data: np.ndarray | t.Tensor, options: Options | None = None) -> Options:
+def optim_options_for_dataset(
+    data: np.ndarray | t.Tensor, options: Options | None = None, tuning: str = "reference"
+) -> Options:
     """Resolve partial or missing options for a dataset.
 
     :param data: ``torch.Tensor`` or ``numpy.ndarray``.
     :param options: Starting point.
+    :param tuning: ``"reference"`` (default): the reference's choices, so the same dataset gets the
+        same options; ``"b200"``: ``physical_block_size`` chosen for this build's B200 kernel
+        (vblocks of up to 64 KiB / 512 rows; several times faster than the reference's choice for
+        small rows).  Addition to the reference API.
     :returns: Complete options for the dataset's route (CUDA options include ``gpu_thread_block_size``).
     """
     options = options or Options()
@@ -125,14 +131,14 @@ def optim_options_for_dataset(data: np.ndarray | t.Tensor, options: Options | No
     if isinstance(data, np.ndarray):
         if povs_numpy.options_is_complete(options):
             return options
-        return povs_numpy.optim_options_for_dataset(data, options)
+        return povs_numpy.optim_options_for_dataset(data, options, tuning)
 
     if isinstance(data, t.Tensor):
         if data.get_device() == -1:
-            return optim_options_for_dataset(data.numpy(), options)
+            return optim_options_for_dataset(data.numpy(), options, tuning)
         if povs_torch.options_is_complete(options):
             return options
-        return povs_torch.optim_options_for_dataset(data, options)
+        return povs_torch.optim_options_for_dataset(data, options, tuning)
 
     raise TypeError(f"Unsupported data type: {type(data)}")
 

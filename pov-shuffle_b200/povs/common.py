@@ -27,7 +27,7 @@ from .constants import (
     MIN_VBLOCK_SIZE,
 )
 from .types import BuildParams, Options
-from .utils import is_power_of_2, least_factor_to_make_multiple
+from .utils import is_power_of_2, least_factor_to_make_multiple, round_down_to_power_of_2
 
 
 def get_build_params() -> BuildParams:
@@ -194,3 +194,32 @@ def _choose_base_offset(
                 "of the physical block size"
             )
         alignment //= 2
+
+
+# B200 option tuning (``tuning="b200"``): the iteration kernel stages one vblock (V * P rows) per
+# unit in shared memory.  Measured on B200 (GB/s of 2 x deck bytes per iteration): vblocks of
+# 32-64 KiB stream at 5.4-6.3 TB/s; 8-16 KiB vblocks pay per-unit overhead (1.6-3.8 TB/s); more
+# than 512 rows per vblock makes the permutation slots crowd out the data stages; rows of 2 KiB
+# and more are staged as 2 KiB column slabs of 32 rows (6.3-6.4 TB/s).
+B200_VBLOCK_BYTES = 64 * 1024
+B200_MAX_VBLOCK_ROWS = 512
+B200_WIDE_ROW_BYTES = 2048
+B200_WIDE_VBLOCK_ROWS = 32
+
+
+def choose_pblock_size_b200(row_bytes: int, vblock_size: int, deck_size: int) -> int:
+    """Physical block size for the B200 kernel: the largest power of two that keeps a vblock within
+    64 KiB and 512 rows (32 rows for rows of 2 KiB and more), at least ``MIN_PBLOCK_SIZE``, and at
+    most what leaves the deck two vblocks."""
+    if row_bytes >= B200_WIDE_ROW_BYTES:
+        rows = B200_WIDE_VBLOCK_ROWS
+    else:
+        rows = min(B200_MAX_VBLOCK_ROWS, B200_VBLOCK_BYTES // max(1, row_bytes))
+    pblock = max(MIN_PBLOCK_SIZE, round_down_to_power_of_2(max(1, rows // vblock_size)))
+    room = deck_size // (2 * vblock_size)
+    if room >= MIN_PBLOCK_SIZE:
+        pblock = min(pblock, round_down_to_power_of_2(room))
+    return max(MIN_PBLOCK_SIZE, pblock)
+
+
+TUNINGS = ("reference", "b200")

@@ -18,6 +18,8 @@ import torch
 
 from . import _native
 from .common import (
+    TUNINGS,
+    choose_pblock_size_b200,
     choose_offsets,
     get_dtype_bytes,
     get_instance_size,
@@ -78,18 +80,26 @@ def options_is_complete(options: Options | None) -> bool:
     )
 
 
-def optim_options_for_dataset(data: np.ndarray, options: Options | None) -> Options:
-    """Complete the options for a host dataset."""
+def optim_options_for_dataset(data: np.ndarray, options: Options | None, tuning: str = "reference") -> Options:
+    """Complete the options for a host dataset (``tuning`` as in ``povs.torch``: the reference's
+    default pblock, or the B200 kernel's choice)."""
+    assert tuning in TUNINGS, f"tuning ({tuning!r}) must be one of {TUNINGS}"
     options = options or Options()
     if options_is_complete(options):
         warnings.warn("All parameters already specified, skipping optimization")
         return options
     if options.physical_block_size is None and options.offsets is not None:
         purge_dependent_param(options, "physical_block_size", "offsets")
-    pblk = options.physical_block_size or DEFAULT_CPU_PBLOCK_SIZE
+    vblk = options.virtual_block_size or MIN_VBLOCK_SIZE
+    if options.physical_block_size:
+        pblk = options.physical_block_size
+    elif tuning == "b200":
+        pblk = choose_pblock_size_b200(get_instance_size(data) * get_dtype_bytes(data), vblk, data.shape[0])
+    else:
+        pblk = DEFAULT_CPU_PBLOCK_SIZE
     return Options(
         randomness=options.randomness,
-        virtual_block_size=options.virtual_block_size or MIN_VBLOCK_SIZE,
+        virtual_block_size=vblk,
         physical_block_size=pblk,
         offsets=choose_offsets(
             deck_size=data.shape[0],

@@ -78,6 +78,25 @@ def test_reference_cuda_randomness_mode_matches_oracle(oracle_api, n_rows, row_b
     assert np.array_equal(got, want)
 
 
+@pytest.mark.parametrize("row_bytes", [4, 64, 256])
+def test_b200_tuned_options_shuffle_like_the_oracle(oracle_api, row_bytes):
+    """``tuning="b200"`` picks the pblock for this kernel; the shuffle is still the oracle's."""
+    from povs.common import choose_pblock_size_b200
+
+    n_rows = 50_003
+    host = random_rows(n_rows, row_bytes, seed=row_bytes)
+    deck = torch.from_numpy(host.copy()).to(DEV)
+    opts = povs.optim_options_for_dataset(deck, tuning="b200")
+    assert opts.physical_block_size == choose_pblock_size_b200(row_bytes, 2, n_rows)
+    assert opts.gpu_thread_block_size is not None
+    povs.shuffle(deck, iterations=3, options=opts, seed=21)
+    torch.cuda.synchronize()
+    povs.check_device_status(0)
+    want = host.copy()
+    oracle_api.shuffle(want, 3, opts.physical_block_size, opts.virtual_block_size, opts.offsets, 21)
+    assert np.array_equal(deck.cpu().numpy(), want)
+
+
 def test_randomness_option_selects_the_mode():
     deck = torch.arange(4096 * 4, dtype=torch.float32, device=DEV).view(4096, 4)
     a, b = deck.clone(), deck.clone()
