@@ -328,10 +328,12 @@ def run_e2e(args, w, deck, opts, offsets, iters, world, rank, local, stream, sha
 
     shard_bytes = deck.numel() * deck.element_size()
     total_bytes = w["rows"] * row_bytes_of(w)
-    n_host = 2 if world == 1 else 1  # one deck: two alternating host decks keep both PCIe directions busy
+    # One GPU: three host decks in rotation through three device buffers keep both PCIe directions
+    # busy (a deck's copy in never waits for its own previous copy out); two when host memory is short.
+    avail = psutil.virtual_memory().available
+    n_host = (3 if avail >= 3.5 * total_bytes else 2) if world == 1 else 1
     # Decide once (rank 0, before anything is pinned) so that every rank takes the same steps.
-    ok = torch.tensor([1 if psutil.virtual_memory().available >= (n_host + 0.5) * total_bytes else 0],
-                      device=deck.device)
+    ok = torch.tensor([1 if avail >= (n_host + 0.5) * total_bytes else 0], device=deck.device)
     if world > 1:
         dist.broadcast(ok, src=0)
     if not int(ok.item()):
@@ -349,13 +351,13 @@ def run_e2e(args, w, deck, opts, offsets, iters, world, rank, local, stream, sha
     if world == 1:
         # povs.shuffle_many's native call: deck k of the timed steps is host deck k % 2, staged through
         # the resident deck buffer and a second device buffer; copies in and out overlap the work.
-        second = torch.empty_like(flat)
-        buffers = [flat, second]
+        buffers = [flat] + [torch.empty_like(flat) for _ in range(n_host - 1)]
 
         def run_steps(n: int, seed: int) -> None:
-            _native.shuffle_host_batch([hosts[k % 2].data_ptr() for k in range(n)], buffers, deck.shape[0], R,
+            _native.shuffle_host_batch([hosts[k % n_host].data_ptr() for k in range(n)], buffers, deck.shape[0], R,
                                        offsets, iters, P, V, [seed + k for k in range(n)])
-        path = "povs_shuffle_host_batch_v1 (povs.shuffle_many): 2 pinned host decks alternating, 2 device buffers"
+        path = (f"povs_shuffle_host_batch_v1 (povs.shuffle_many): {n_host} pinned host decks in rotation, "
+                f"{n_host} device buffers")
     else:
         def run_steps(n: int, seed: int) -> None:
             for k in range(n):
@@ -479,7 +481,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="bf16_32GiB", choices=sorted(WORKLOADS))
-    ap.add_argument("--e2e-steps", type=int, default=8)
+    ap.add_argument("--e2e-steps", type=int, default=16)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)

@@ -88,6 +88,21 @@ int povs_shuffle_host_v1(void* host_data, void* device_buffer, int64_t n_rows, i
                          int32_t vblock, uint64_t seed, int32_t device, void* stream, uint32_t flags);
 
 /*
+ * Same as povs_shuffle_v1 for a deck that STAYS in host memory, for decks larger than the
+ * device's memory: the kernels read and write the rows in place over PCIe / C2C through mapped
+ * page-locked memory (plain vector loads and stores, no TMA).  Memory from cudaHostAlloc /
+ * cudaMallocHost or already registered is used as is; any other host range is page-locked and
+ * mapped for the duration of the call (cudaHostRegister of the enclosing pages) and released
+ * before returning.  The call returns after the stream has synchronized.  Throughput is bound by
+ * the interconnect (each iteration moves the deck across it twice).
+ * Serves the reference's roadmap item of decks larger than memory (CONTRIBUTING.md:16) on the
+ * reference's CPU route (src/povs/numpy.py:18-61).
+ */
+int povs_shuffle_mapped_v1(void* host_data, int64_t n_rows, int64_t row_bytes, const int64_t* offsets,
+                           int32_t n_offsets, int32_t iterations, int32_t pblock, int32_t vblock, uint64_t seed,
+                           int32_t device, void* stream, uint32_t flags);
+
+/*
  * Shuffle n_decks host decks of the same shape through n_buffers device buffers (>= 2 for
  * overlap; each at least n_rows * row_bytes bytes on `device`): deck d is copied into buffer
  * d % n_buffers, shuffled with seeds[d], and copied back, on internal streams ordered by events so

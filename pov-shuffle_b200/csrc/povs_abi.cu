@@ -216,7 +216,8 @@ struct Plan {
     bool bulk = false;
 };
 
-int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out, bool push = false)
+int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out, bool push = false,
+                bool plain_loads = false)
 {
     Tuning t;
     {
@@ -237,7 +238,7 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out, boo
     if (p.n_decks > 1) addr |= static_cast<uintptr_t>(p.deck_stride);
     int vec = 16;
     while (vec > 1 && ((p.row_bytes % vec) != 0 || (addr % vec) != 0)) vec >>= 1;
-    const bool bulk = (vec == 16) && !t.force_plain;
+    const bool bulk = (vec == 16) && !t.force_plain && !plain_loads;
 
     // Slab width: whole rows when a vblock fits a stage, else the widest 128-byte (or vec) multiple that does.
     // A stage holds a unit's rows: the vblock's V*P rows in place, one member's P rows in push mode.
@@ -467,7 +468,7 @@ int shuffle_on_device(void* data, int64_t n_rows, int64_t row_bytes, const int64
                       int32_t iterations, int32_t pblock, int32_t vblock, uint64_t seed, DeviceCtx& c,
                       cudaStream_t s, uint32_t flags, void* const* shard_ptrs = nullptr,
                       const int64_t* shard_rows = nullptr, int32_t n_shards = 1, int64_t n_decks = 1,
-                      int64_t deck_stride = 0, const uint64_t* deck_seeds = nullptr)
+                      int64_t deck_stride = 0, const uint64_t* deck_seeds = nullptr, bool plain_loads = false)
 {
     IterParams base;
     fill_geometry(base, data, n_rows, row_bytes, pblock, vblock, c.status);
@@ -483,7 +484,7 @@ int shuffle_on_device(void* data, int64_t n_rows, int64_t row_bytes, const int64
     base.n_offsets = n_offsets;
     for (int i = 0; i < n_offsets; ++i) base.offsets[i] = offsets[i];
     Plan pl;
-    int r = plan_launch(base, c, false, pl);
+    int r = plan_launch(base, c, false, pl, false, plain_loads);
     if (r != POVS_OK) return r;
     if (iterations == 0) return POVS_OK;
     std::vector<IterParams> ps(static_cast<size_t>(iterations), base);
@@ -606,6 +607,8 @@ extern "C" int povs_shuffle_host_batch_v1(void* const* host_decks, int32_t n_dec
 
     // Deck d uses buffer d % n_buffers.  Copies in, the iterations and copies out run on three
     // streams ordered by events, so deck d's copy out overlaps deck d+1's copy in and iterations.
+    // Deck d's copy in waits for the copy out of the deck that last used its buffer and of the
+    // previous deck with the same host pointer (a deck listed twice is shuffled twice in order).
     cudaStream_t user = static_cast<cudaStream_t>(stream);
     cudaStream_t s_in = nullptr, s_out = nullptr, s_cmp = nullptr;
     std::vector<cudaEvent_t> ev;
@@ -621,9 +624,11 @@ extern "C" int povs_shuffle_host_batch_v1(void* const* host_decks, int32_t n_dec
         POVS_CUDA_TRY(cudaStreamCreateWithFlags(&s_in, cudaStreamNonBlocking));
         POVS_CUDA_TRY(cudaStreamCreateWithFlags(&s_out, cudaStreamNonBlocking));
         POVS_CUDA_TRY(cudaStreamCreateWithFlags(&s_cmp, cudaStreamNonBlocking));
-        ev.assign(static_cast<size_t>(3 * n_buffers + 1), nullptr);
+        ev.assign(static_cast<size_t>(2 * n_buffers + n_decks + 1), nullptr);
         for (auto& e : ev) POVS_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-        cudaEvent_t start = ev[3 * n_buffers];
+        cudaEvent_t start = ev[2 * n_buffers];
+        auto out_done = [&](int d) { return ev[static_cast<size_t>(2 * n_buffers + 1 + d)]; };
+        std::unordered_map<void*, int> last_use;
         // Work already queued on the caller's stream (e.g. writes to the buffers) comes first.
         POVS_CUDA_TRY(cudaEventRecord(start, user));
         POVS_CUDA_TRY(cudaStreamWaitEvent(s_in, start, 0));
@@ -631,8 +636,11 @@ extern "C" int povs_shuffle_host_batch_v1(void* const* host_decks, int32_t n_dec
         POVS_CUDA_TRY(cudaStreamWaitEvent(s_out, start, 0));
         for (int d = 0; d < n_decks; ++d) {
             const int b = d % n_buffers;
-            cudaEvent_t in_done = ev[3 * b], cmp_done = ev[3 * b + 1], out_done = ev[3 * b + 2];
-            if (d >= n_buffers) POVS_CUDA_TRY(cudaStreamWaitEvent(s_in, out_done, 0));
+            cudaEvent_t in_done = ev[2 * b], cmp_done = ev[2 * b + 1];
+            if (d >= n_buffers) POVS_CUDA_TRY(cudaStreamWaitEvent(s_in, out_done(d - n_buffers), 0));
+            auto prev = last_use.find(host_decks[d]);
+            if (prev != last_use.end()) POVS_CUDA_TRY(cudaStreamWaitEvent(s_in, out_done(prev->second), 0));
+            last_use[host_decks[d]] = d;
             POVS_CUDA_TRY(cudaMemcpyAsync(device_buffers[b], host_decks[d], bytes, cudaMemcpyHostToDevice, s_in));
             POVS_CUDA_TRY(cudaEventRecord(in_done, s_in));
             POVS_CUDA_TRY(cudaStreamWaitEvent(s_cmp, in_done, 0));
@@ -642,7 +650,7 @@ extern "C" int povs_shuffle_host_batch_v1(void* const* host_decks, int32_t n_dec
             POVS_CUDA_TRY(cudaEventRecord(cmp_done, s_cmp));
             POVS_CUDA_TRY(cudaStreamWaitEvent(s_out, cmp_done, 0));
             POVS_CUDA_TRY(cudaMemcpyAsync(host_decks[d], device_buffers[b], bytes, cudaMemcpyDeviceToHost, s_out));
-            POVS_CUDA_TRY(cudaEventRecord(out_done, s_out));
+            POVS_CUDA_TRY(cudaEventRecord(out_done(d), s_out));
         }
         POVS_CUDA_TRY(cudaStreamSynchronize(s_in));
         POVS_CUDA_TRY(cudaStreamSynchronize(s_cmp));
@@ -1299,5 +1307,68 @@ extern "C" int povs_set_peer_wait_limit_v1(uint64_t limit_ns)
 {
     g_err[0] = '\0';
     g_peer_wait_ns.store(limit_ns == 0 ? povs::PEER_WAIT_LIMIT_NS : static_cast<unsigned long long>(limit_ns));
+    return POVS_OK;
+}
+
+// ------------------------------------------------------------------------------------------
+// Decks that stay in host memory (mapped, page-locked).
+// ------------------------------------------------------------------------------------------
+
+extern "C" int povs_shuffle_mapped_v1(void* host_data, int64_t n_rows, int64_t row_bytes, const int64_t* offsets,
+                                      int32_t n_offsets, int32_t iterations, int32_t pblock, int32_t vblock,
+                                      uint64_t seed, int32_t device, void* stream, uint32_t flags)
+{
+    g_err[0] = '\0';
+    int r = check_common(host_data, n_rows, row_bytes, pblock, vblock, iterations);
+    if (r != POVS_OK) return r;
+    r = check_offsets(offsets, n_offsets, n_rows);
+    if (r != POVS_OK) return r;
+    DeviceGuard dg;
+    r = dg.enter(device);
+    if (r != POVS_OK) return r;
+    DeviceCtx* c = nullptr;
+    r = get_ctx(device, &c);
+    if (r != POVS_OK) return r;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+    // Page-lock and map the deck for the call unless the caller already did (pinned memory).
+    cudaPointerAttributes attr{};
+    POVS_CUDA_TRY(cudaPointerGetAttributes(&attr, host_data));
+    void* registered = nullptr;
+    if (attr.type == cudaMemoryTypeUnregistered) {
+        const uintptr_t page = 4096;
+        const uintptr_t begin = reinterpret_cast<uintptr_t>(host_data) & ~(page - 1);
+        const uintptr_t end = (reinterpret_cast<uintptr_t>(host_data) + static_cast<uintptr_t>(n_rows * row_bytes) +
+                               page - 1) & ~(page - 1);
+        registered = reinterpret_cast<void*>(begin);
+        POVS_CUDA_TRY(cudaHostRegister(registered, end - begin, cudaHostRegisterMapped | cudaHostRegisterPortable));
+    } else if (attr.type != cudaMemoryTypeHost) {
+        return fail(POVS_ERR_INVALID_ARGUMENT, "host_data is not host memory (use povs_shuffle_v1 for device decks)");
+    }
+    void* mapped = nullptr;
+    cudaError_t e = cudaHostGetDevicePointer(&mapped, host_data, 0);
+    if (e == cudaSuccess) {
+        // Plain vector loads and stores over the interconnect; TMA copies are not used on host memory.
+        r = shuffle_on_device(mapped, n_rows, row_bytes, offsets, n_offsets, iterations, pblock, vblock, seed, *c, s,
+                              flags & ~uint32_t{POVS_FLAG_SYNC}, nullptr, nullptr, 1, 1, 0, nullptr, true);
+        if (r == POVS_OK) {
+            e = cudaStreamSynchronize(s);
+            if (e != cudaSuccess) r = cuda_fail(e, "cudaStreamSynchronize");
+        }
+    } else {
+        r = cuda_fail(e, "cudaHostGetDevicePointer");
+    }
+    if (registered != nullptr) {
+        if (r != POVS_OK) cudaStreamSynchronize(s);  // the deck must not be unmapped under a running kernel
+        cudaError_t u = cudaHostUnregister(registered);
+        if (r == POVS_OK && u != cudaSuccess) r = cuda_fail(u, "cudaHostUnregister");
+    }
+    if (r != POVS_OK) return r;
+    if (flags & POVS_FLAG_SYNC) {
+        int32_t st = 0;
+        r = read_status(*c, &st);
+        if (r != POVS_OK) return r;
+        if (st != 0) return fail(POVS_ERR_DEVICE_STATUS, "device status 0x%x after shuffle", st);
+    }
     return POVS_OK;
 }

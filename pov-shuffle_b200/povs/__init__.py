@@ -35,6 +35,7 @@ __all__ = [
     "ShardedDeck",
     "shuffle_many",
     "shuffle_batch",
+    "shuffle_mapped",
 ]
 
 
@@ -65,6 +66,27 @@ def shuffle(
         return
 
     raise TypeError(f"Unsupported data type: {type(data)}")
+
+
+def shuffle_mapped(
+    data: np.ndarray | t.Tensor,
+    iterations: int = 1,
+    options: Options | None = None,
+    seed: int | np.random.Generator | Any | None = None,
+) -> None:
+    """Shuffle a host deck (NumPy array or CPU tensor) in place WITHOUT copying it to the GPU: the
+    kernels read and write it in host memory over the interconnect.  For decks larger than the
+    GPU's memory (``povs.shuffle`` switches to this by itself when a host deck does not fit).
+    Same result as ``povs.shuffle`` with the same arguments.  Addition to the reference API.
+    """
+    seed = get_int_seed(seed)
+    if isinstance(data, t.Tensor):
+        if data.get_device() != -1:
+            raise TypeError("shuffle_mapped takes host decks; use shuffle for CUDA tensors")
+        data = data.numpy()
+    if not isinstance(data, np.ndarray):
+        raise TypeError(f"Unsupported data type: {type(data)}")
+    povs_numpy.shuffle(data, iterations, options, seed, mapped=True)
 
 
 def shuffle_many(

@@ -60,6 +60,10 @@ SIGNATURES: dict[str, tuple] = {
     "povs_ipc_export_v1": (ctypes.c_int, [_c_vp, _c_i32, _c_vp, _P_I64]),
     "povs_ipc_import_v1": (ctypes.c_int, [_c_vp, _c_i64, _c_i32, ctypes.POINTER(_c_vp), ctypes.POINTER(_c_vp)]),
     "povs_ipc_close_v1": (ctypes.c_int, [_c_vp, _c_i32]),
+    "povs_shuffle_mapped_v1": (
+        ctypes.c_int,
+        [_c_vp, _c_i64, _c_i64, _P_I64, _c_i32, _c_i32, _c_i32, _c_i32, _c_u64, _c_i32, _c_vp, _c_u32],
+    ),
     "povs_shuffle_batch_v1": (
         ctypes.c_int,
         [_c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _P_I64, _c_i32, _c_i32, _c_i32, _c_i32, _c_vp, _c_i32, _c_vp, _c_u32],
@@ -249,6 +253,28 @@ def shuffle_host(
         flags,
     )
     check(code, "povs_shuffle_host_v1")
+
+
+def shuffle_mapped(
+    host_ptr: int,
+    n_rows: int,
+    row_bytes: int,
+    offsets: list[int],
+    iterations: int,
+    pblock: int,
+    vblock: int,
+    seed: int,
+    device: int,
+    flags: int = 0,
+) -> None:
+    """Shuffle rows that stay in host memory, through mapped page-locked memory (blocks until done)."""
+    lib = load()
+    dev = torch.device("cuda", device)
+    code = lib.povs_shuffle_mapped_v1(
+        ctypes.c_void_p(host_ptr), n_rows, row_bytes, _i64_array(offsets), len(offsets), iterations, pblock, vblock,
+        seed, device, ctypes.c_void_p(current_stream_handle(dev)), flags,
+    )
+    check(code, "povs_shuffle_mapped_v1")
 
 
 def shuffle_host_batch(

@@ -32,8 +32,19 @@ from .constants import DEFAULT_CPU_PBLOCK_SIZE, MIN_VBLOCK_SIZE
 from .types import Options
 
 
-def shuffle(data: np.ndarray, iterations: int, options: Options | None, seed: int, flags: int = 0) -> None:
-    """Shuffle a host array in place along axis 0 on the current CUDA device."""
+# Decks whose staging copy would leave less than this much device memory free are shuffled in
+# place in host memory (mapped) instead of through a device copy.
+DEVICE_HEADROOM_BYTES = 2 << 30
+
+
+def shuffle(data: np.ndarray, iterations: int, options: Options | None, seed: int, flags: int = 0,
+            mapped: bool | None = None) -> None:
+    """Shuffle a host array in place along axis 0 on the current CUDA device.
+
+    ``mapped``: None chooses: the deck is copied to the device and back when it fits the device's
+    free memory, else the kernels work on it in host memory (``povs_shuffle_mapped_v1``, bound by
+    the interconnect); True / False force one or the other.
+    """
     options = typing.cast(
         "_HostOptions",
         options if options_is_complete(options) else optim_options_for_dataset(data, options),
@@ -49,6 +60,17 @@ def shuffle(data: np.ndarray, iterations: int, options: Options | None, seed: in
     host = data if contiguous else np.ascontiguousarray(data)
     n_rows = host.shape[0]
     device = torch.device("cuda", torch.cuda.current_device())
+    if mapped is None:
+        free, _ = torch.cuda.mem_get_info(device)
+        mapped = n_rows * row_bytes + DEVICE_HEADROOM_BYTES > free
+    if mapped:
+        _native.shuffle_mapped(
+            host.ctypes.data, n_rows, row_bytes, list(options.offsets), iterations, options.physical_block_size,
+            options.virtual_block_size, seed_to_u64(seed), device.index, flags | randomness_flags(options),
+        )
+        if not contiguous:
+            data[...] = host
+        return
     staging = torch.empty(n_rows * row_bytes, dtype=torch.uint8, device=device)
     _native.shuffle_host(
         host.ctypes.data,

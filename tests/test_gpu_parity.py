@@ -97,6 +97,45 @@ def test_b200_tuned_options_shuffle_like_the_oracle(oracle_api, row_bytes):
     assert np.array_equal(deck.cpu().numpy(), want)
 
 
+@pytest.mark.parametrize("pinned", [False, True])
+@pytest.mark.parametrize("row_bytes", [48, 12])
+def test_mapped_host_deck_matches_oracle(oracle_api, pinned, row_bytes):
+    """A host deck shuffled where it lies (mapped, page-locked for the call or already pinned)."""
+    n, P, V, offsets = 100_003, 32, 4, [0, 1, 2, 5]
+    host = random_rows(n, row_bytes, seed=row_bytes + pinned)
+    if pinned:
+        buf = torch.empty((n, row_bytes), dtype=torch.uint8, pin_memory=True)
+        arr = buf.numpy()
+        arr[...] = host
+    else:
+        arr = host.copy()
+    povs.shuffle_mapped(arr, iterations=3, options=povs.Options(V, P, offsets), seed=8)
+    povs.check_device_status(0)
+    want = host.copy()
+    oracle_api.shuffle(want, 3, P, V, offsets, 8)
+    assert np.array_equal(arr, want)
+
+
+def test_host_decks_that_do_not_fit_stay_in_host_memory(oracle_api, monkeypatch):
+    """povs.shuffle on a host deck switches to the mapped route when the device lacks room; a
+    non-contiguous deck is staged through a contiguous copy either way."""
+    from povs import _native as native_mod
+
+    calls = []
+    real = native_mod.shuffle_mapped
+    monkeypatch.setattr(native_mod, "shuffle_mapped", lambda *a, **k: (calls.append(1), real(*a, **k)))
+    monkeypatch.setattr(torch.cuda, "mem_get_info", lambda *a, **k: (1 << 20, 1 << 34))
+    n, R, P, V, offsets = 20_011, 32, 16, 2, [0, 1, 2]
+    host = random_rows(n, 2 * R, seed=4)
+    arr = host.copy()
+    view = arr[:, :R]  # every other half-row: not C-contiguous
+    povs.shuffle(view, iterations=2, options=povs.Options(V, P, offsets), seed=3)
+    assert calls, "the mapped route was not taken"
+    want = np.ascontiguousarray(host[:, :R])
+    oracle_api.shuffle(want, 2, P, V, offsets, 3)
+    assert np.array_equal(arr[:, :R], want) and np.array_equal(arr[:, R:], host[:, R:])
+
+
 def test_randomness_option_selects_the_mode():
     deck = torch.arange(4096 * 4, dtype=torch.float32, device=DEV).view(4096, 4)
     a, b = deck.clone(), deck.clone()
@@ -358,6 +397,25 @@ def test_shards_smaller_than_a_pblock_are_rejected():
     shards = [torch.zeros((8, 4), device=DEV), torch.zeros((100, 4), device=DEV)]
     with pytest.raises(AssertionError, match="at least physical_block_size"):
         povs.shuffle_shards(shards, iterations=1, options=povs.Options(2, 16, [0, 4], 32), seed=1)
+
+
+def test_host_batch_repeated_decks_with_three_buffers(oracle_api):
+    """Host decks A, B, A, C, A through three device buffers: each listing of A starts from the
+    previous listing's result (its copy in waits for that copy back), whichever buffer it uses."""
+    n, R, P, V, offsets = 30_011, 32, 16, 4, [0, 1, 2]
+    pins = [torch.empty((n, R), dtype=torch.uint8, pin_memory=True) for _ in range(3)]
+    originals = [random_rows(n, R, seed=60 + i) for i in range(3)]
+    for t, o in zip(pins, originals):
+        t.numpy()[...] = o
+    order = [0, 1, 0, 2, 0]
+    seeds = [11, 12, 13, 14, 15]
+    buffers = [torch.empty(n * R, dtype=torch.uint8, device=DEV) for _ in range(3)]
+    _native.shuffle_host_batch([pins[i].data_ptr() for i in order], buffers, n, R, offsets, 2, P, V, seeds)
+    want = [o.copy() for o in originals]
+    for i, sd in zip(order, seeds):
+        oracle_api.shuffle(want[i], 2, P, V, offsets, sd)
+    for t, w in zip(pins, want):
+        assert np.array_equal(t.numpy(), w)
 
 
 def test_shuffle_many_matches_one_deck_at_a_time():
