@@ -58,27 +58,37 @@ int ilog2(int64_t x)
 
 using KernelFn = void (*)(IterParams);
 
-template <bool INJ, bool BULK, bool PUSH>
+template <bool INJ, bool BULK, bool PUSH, bool RING>
 KernelFn kernel_for_epl(int epl)
 {
     switch (epl) {
-    case 1: return povs::povs_iteration_kernel<1, INJ, BULK, PUSH>;
-    case 2: return povs::povs_iteration_kernel<2, INJ, BULK, PUSH>;
-    case 4: return povs::povs_iteration_kernel<4, INJ, BULK, PUSH>;
-    case 8: return povs::povs_iteration_kernel<8, INJ, BULK, PUSH>;
-    case 16: return povs::povs_iteration_kernel<16, INJ, BULK, PUSH>;
-    case 32: return povs::povs_iteration_kernel<32, INJ, BULK, PUSH>;
+    case 1: return povs::povs_iteration_kernel<1, INJ, BULK, PUSH, RING>;
+    case 2: return povs::povs_iteration_kernel<2, INJ, BULK, PUSH, RING>;
+    case 4: return povs::povs_iteration_kernel<4, INJ, BULK, PUSH, RING>;
+    case 8: return povs::povs_iteration_kernel<8, INJ, BULK, PUSH, RING>;
+    case 16: return povs::povs_iteration_kernel<16, INJ, BULK, PUSH, RING>;
+    case 32: return povs::povs_iteration_kernel<32, INJ, BULK, PUSH, RING>;
     default: return nullptr;
     }
 }
 
-// Push mode exists for device randomness only.
-KernelFn select_kernel(int epl, bool injected, bool bulk, bool push = false)
+template <bool INJ, bool PUSH>
+KernelFn kernel_for(int epl, bool bulk, bool ring)
 {
-    if (push) return bulk ? kernel_for_epl<false, true, true>(epl) : kernel_for_epl<false, false, true>(epl);
-    if (injected) return bulk ? kernel_for_epl<true, true, false>(epl) : kernel_for_epl<true, false, false>(epl);
-    return bulk ? kernel_for_epl<false, true, false>(epl) : kernel_for_epl<false, false, false>(epl);
+    if (!bulk) return kernel_for_epl<INJ, false, PUSH, true>(epl);
+    return ring ? kernel_for_epl<INJ, true, PUSH, true>(epl) : kernel_for_epl<INJ, true, PUSH, false>(epl);
 }
+
+// Push mode exists for device randomness only.  Plain-load kernels always carry ring positions.
+KernelFn select_kernel(int epl, bool injected, bool bulk, bool push = false, bool ring = false)
+{
+    if (push) return kernel_for<false, true>(epl, bulk, ring);
+    if (injected) return kernel_for<true, false>(epl, bulk, ring);
+    return kernel_for<false, false>(epl, bulk, ring);
+}
+
+// Bulk-loaded units (stages) of at most this many bytes use the ring-position kernels.
+constexpr int RING_STAGE_BYTES = 16 * 1024;
 
 // ------------------------------------------------------------------------------------------
 // Tuning knobs (process-wide; defaults chosen by measurement on B200).
@@ -168,12 +178,13 @@ int set_smem_attr_all(int smem)
 {
     for (int mode = 0; mode < 3; ++mode)
         for (int bulk = 0; bulk < 2; ++bulk)
-            for (int epl = 1; epl <= 32; epl <<= 1) {
-                KernelFn fn = select_kernel(epl, mode == 1, bulk != 0, mode == 2);
-                cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
-                                                     cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-                if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
-            }
+            for (int ring = 0; ring < 2; ++ring)
+                for (int epl = 1; epl <= 32; epl <<= 1) {
+                    KernelFn fn = select_kernel(epl, mode == 1, bulk != 0, mode == 2, ring != 0);
+                    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+                    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+                }
     return POVS_OK;
 }
 
@@ -301,7 +312,7 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out, boo
     p.n_movers = movers;
     p.n_permuters = permuters;
 
-    out.fn = select_kernel(epl, injected, bulk, push);
+    out.fn = select_kernel(epl, injected, bulk, push, stage_bytes <= RING_STAGE_BYTES);
     out.grid = std::max(1, grid);
     out.block = warps * 32;
     out.smem = cta_smem;

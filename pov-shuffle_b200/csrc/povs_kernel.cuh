@@ -736,9 +736,14 @@ __device__ __forceinline__ RingPos ring_at(uint64_t u, uint32_t n)
     return RingPos{static_cast<uint32_t>(u % n), static_cast<uint32_t>((u / n) & 1u)};
 }
 
-template <int EPL, bool INJECTED, bool BULK, bool PUSH>
+// RING: the permuter and mover warps carry their units' stage / slot ring positions from unit to
+// unit (small units, where per-unit bookkeeping is a visible share of the work, and every
+// plain-load kernel); otherwise they recompute them per unit, which measured faster on large
+// bulk-loaded units.
+template <int EPL, bool INJECTED, bool BULK, bool PUSH, bool RING>
 __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_constant__ IterParams p)
 {
+    static_assert(BULK || RING, "plain-load kernels carry ring positions");
     static_assert(!(PUSH && INJECTED), "push mode draws its randomness on the device");
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const int lane = threadIdx.x & 31;
@@ -808,8 +813,8 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
         for (int64_t u = q; u < n_units; u += p.n_permuters) {
             int k;
             int64_t entry;
-            if constexpr (BULK) {
-                // Bulk path: positions recomputed per unit (measured faster there).
+            if constexpr (!RING) {
+                // Large bulk units: positions recomputed per unit (measured faster there).
                 k = static_cast<int>(u % kp);
                 if (u >= kp && !warp_wait(&sm.pempty[k], static_cast<uint32_t>(((u / kp) - 1) & 1), p.status)) return;
                 entry = blockIdx.x + (u / p.n_slabs) * static_cast<int64_t>(gridDim.x);
@@ -949,8 +954,8 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
     const int64_t ahead = nst - 1;
     int64_t last_issued = -1;
 
-    if constexpr (BULK) {
-        // TMA bulk loads.  Unit u's stage (u % nst), permutation slot (u % kp) and phases are
+    if constexpr (!RING) {
+        // Large TMA-loaded units.  Unit u's stage (u % nst), permutation slot (u % kp) and phases are
         // recomputed per unit (on large units this measured faster than carrying ring counters).
         auto issue = [&](int64_t u) -> bool {
             const int st = static_cast<int>(u % nst);
@@ -1048,9 +1053,8 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
             }
         }
     } else {
-        // Plain vector loads (rows not a multiple of 16 bytes, or an unaligned deck).  The stage and
-        // slot ring positions are carried from unit to unit without divisions: with small rows the
-        // per-unit bookkeeping is a visible share of the work.
+        // Ring positions carried from unit to unit.  Loads: TMA bulk copies (BULK) or plain vector
+        // loads (rows not a multiple of 16 bytes, or an unaligned deck).
         auto issue = [&](RingPos sr, RingPos kr, int slab, bool wait_empty) -> bool {
             const int st = static_cast<int>(sr.i);
             const int k = static_cast<int>(kr.i);
@@ -1060,14 +1064,55 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
             const int64_t col = static_cast<int64_t>(slab) * p.slab_bytes;
             const int slen = static_cast<int>(min(static_cast<int64_t>(p.slab_bytes), p.row_bytes - col));
             uint8_t* stage = sm.data + static_cast<size_t>(st) * p.stage_bytes;
-            switch (p.vec_bytes) {
-            case 16: lsu_load_unit<16, PUSH>(p, m, stage, col, slen, lane); break;
-            case 8: lsu_load_unit<8, PUSH>(p, m, stage, col, slen, lane); break;
-            case 4: lsu_load_unit<4, PUSH>(p, m, stage, col, slen, lane); break;
-            case 2: lsu_load_unit<2, PUSH>(p, m, stage, col, slen, lane); break;
-            default: lsu_load_unit<1, PUSH>(p, m, stage, col, slen, lane); break;
+            if constexpr (BULK) {
+                fence_proxy_async_smem();
+                const int n_load = PUSH ? m.rows_mine : m.n_valid;
+                if (lane == 0)
+                    mbar_expect_tx(&sm.full[st], static_cast<uint32_t>(n_load) * static_cast<uint32_t>(slen));
+                __syncwarp();
+                if (p.n_slabs == 1) {
+                    // Whole rows: each member is <= 2 contiguous runs, copied in pieces of at most
+                    // copy_rows rows; pieces are spread over the lanes.
+                    const int ppm = (p.pblock + p.copy_rows - 1) / p.copy_rows;
+                    const int n_mem = PUSH ? 1 : (n_load + pmask) >> p.pblock_shift;
+                    for (int q = lane; q < n_mem * ppm; q += 32) {
+                        const int r = ppm == 1 ? q : q / ppm;
+                        const int i0 = (q - r * ppm) * p.copy_rows;
+                        const int first = r << p.pblock_shift;
+                        const int rows_r = min(p.pblock, n_load - first);
+                        if (i0 >= rows_r) continue;
+                        const int len = min(p.copy_rows, rows_r - i0);
+                        const int na = PUSH ? m.src_na : m.n_a[r];
+                        const uintptr_t ra = PUSH ? m.src_a : m.run_a[r];
+                        const uintptr_t rb = PUSH ? m.src_b : m.run_b[r];
+                        const int n1 = i0 < na ? min(len, na - i0) : 0;
+                        uint8_t* dst = stage + static_cast<size_t>(first + i0) * p.slab_bytes;
+                        if (n1 > 0)
+                            bulk_load(dst, reinterpret_cast<const uint8_t*>(ra + static_cast<uintptr_t>(i0) * p.row_bytes),
+                                      static_cast<uint32_t>(n1) * static_cast<uint32_t>(p.row_bytes), &sm.full[st]);
+                        if (len > n1)
+                            bulk_load(dst + static_cast<size_t>(n1) * p.slab_bytes,
+                                      reinterpret_cast<const uint8_t*>(rb + static_cast<uintptr_t>(i0 + n1) * p.row_bytes),
+                                      static_cast<uint32_t>(len - n1) * static_cast<uint32_t>(p.row_bytes), &sm.full[st]);
+                    }
+                } else {
+                    for (int f = lane; f < n_load; f += 32) {
+                        const uint8_t* src = PUSH ? src_row_ptr(m, f, p.row_bytes) + col
+                                                  : slot_ptr(m, f, p.pblock_shift, pmask, p.row_bytes) + col;
+                        bulk_load(stage + static_cast<size_t>(f) * p.slab_bytes, src, static_cast<uint32_t>(slen),
+                                  &sm.full[st]);
+                    }
+                }
+            } else {
+                switch (p.vec_bytes) {
+                case 16: lsu_load_unit<16, PUSH>(p, m, stage, col, slen, lane); break;
+                case 8: lsu_load_unit<8, PUSH>(p, m, stage, col, slen, lane); break;
+                case 4: lsu_load_unit<4, PUSH>(p, m, stage, col, slen, lane); break;
+                case 2: lsu_load_unit<2, PUSH>(p, m, stage, col, slen, lane); break;
+                default: lsu_load_unit<1, PUSH>(p, m, stage, col, slen, lane); break;
+                }
+                __syncwarp();
             }
-            __syncwarp();
             mbar_arrive(&sm.full[st]);
             return true;
         };
@@ -1081,25 +1126,39 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
             const uint8_t* stage = sm.data + static_cast<size_t>(st) * p.stage_bytes;
             const int64_t col = static_cast<int64_t>(slab) * p.slab_bytes;
             const int slen = static_cast<int>(min(static_cast<int64_t>(p.slab_bytes), p.row_bytes - col));
-            switch (p.vec_bytes) {
-            case 16: store_share<16, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
-            case 8: store_share<8, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
-            case 4: store_share<4, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
-            case 2: store_share<2, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
-            default: store_share<1, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
+            if constexpr (BULK) {
+                store_share<16, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers);
+            } else {
+                switch (p.vec_bytes) {
+                case 16: store_share<16, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
+                case 8: store_share<8, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
+                case 4: store_share<4, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
+                case 2: store_share<2, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
+                default: store_share<1, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
+                }
             }
             mbar_arrive(&sm.empty[st]);  // this thread's reads of the data stage are done
             mbar_arrive(&sm.pempty[k]);  // ... and of the permutation slot
             return true;
         };
-        // Plain loads complete before a unit's `full` arrival, so a timeout needs no draining.
-        (void)last_issued;
+        // On a timeout: wait (bounded) for the bulk copies of the units this warp issued and stop
+        // (plain loads complete before a unit's `full` arrival: nothing to wait for).
+        auto drain_and_stop = [&](int64_t from) {
+            if constexpr (BULK) {
+                for (int64_t u = from; u <= last_issued; ++u)
+                    if (u % n_movers == mw)
+                        warp_wait(&sm.full[u % nst], static_cast<uint32_t>((u / nst) & 1), p.status);
+            }
+        };
         const uint32_t n_slabs = static_cast<uint32_t>(p.n_slabs);
         for (int64_t u = mw; u < ahead && u < n_units; u += n_movers) {
             if (!issue(ring_at(static_cast<uint64_t>(u), static_cast<uint32_t>(nst)),
                        ring_at(static_cast<uint64_t>(u), static_cast<uint32_t>(kp)),
-                       static_cast<int>(static_cast<uint64_t>(u) % n_slabs), u >= nst))
+                       static_cast<int>(static_cast<uint64_t>(u) % n_slabs), u >= nst)) {
+                drain_and_stop(0);
                 return;
+            }
+            last_issued = u;
         }
         // Store before issuing: the issue of unit j+NST-1 waits for every mover's share of unit j-1.
         // Ring positions of unit j (stores) and of unit j + ahead (issues) advance one unit per step.
@@ -1110,10 +1169,17 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
         uint32_t slab_u = static_cast<uint32_t>(static_cast<uint64_t>(ahead) % n_slabs);
         uint32_t mover_u = static_cast<uint32_t>(ahead % n_movers);
         for (int64_t j = 0; j < n_units; ++j) {
-            if (!store(sj, kj, static_cast<int>(slab_j))) return;
+            if (!store(sj, kj, static_cast<int>(slab_j))) {
+                drain_and_stop(j);
+                return;
+            }
             const int64_t u = j + ahead;
             if (u < n_units && mover_u == static_cast<uint32_t>(mw)) {
-                if (!issue(su, ku, static_cast<int>(slab_u), u >= nst)) return;
+                if (!issue(su, ku, static_cast<int>(slab_u), u >= nst)) {
+                    drain_and_stop(j + 1);
+                    return;
+                }
+                last_issued = u;
             }
             sj.next(static_cast<uint32_t>(nst));
             kj.next(static_cast<uint32_t>(kp));
