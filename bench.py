@@ -301,7 +301,7 @@ def run_ours(args, w: dict, wname: str) -> None:
                 "peak_kind": roof_kind,
                 "unit": "GB/s",
                 "frac": round(achieved / roof_peak, 4),
-                "traffic": traffic_per_launch("povs_iteration_kernel", wname) if world == 1 and args.rows is None else None,
+                "traffic": traffic_per_launch("povs_iteration_kernel", wname) if world == 1 and not (args.rows or args.vblock or args.pblock) else None,
                 "alg_bytes_per_launch": 2 * deck_bytes // world,
                 "hbm_frac_per_gpu": round(2 * deck_bytes / world / per_launch_s / 1e9 / peak, 4),
             },
@@ -488,6 +488,8 @@ def main() -> None:
     ap.add_argument("--sharded-order", default="push", choices=["push", "inplace"],
                     help="with --gpus N > 1: double-buffered push order (default) or in place")
     ap.add_argument("--rows", type=int, default=None, help="override the workload's row count (profiling captures)")
+    ap.add_argument("--vblock", type=int, default=None, help="override the workload's V (profiling captures)")
+    ap.add_argument("--pblock", type=int, default=None, help="override the workload's P (profiling captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
@@ -495,6 +497,10 @@ def main() -> None:
     if args.rows:
         w["desc"] = w["desc"] + f" [rows overridden: {args.rows:,}]"
         w["rows"] = args.rows
+    for key, val in (("V", args.vblock), ("P", args.pblock)):
+        if val:
+            w["desc"] = w["desc"] + f" [{key} overridden: {val}]"
+            w[key] = val
     if args.impl == "reference":
         run_reference(args, w, args.workload)
     else:
