@@ -41,7 +41,7 @@ for _p in (REPO, REPO / "pov-shuffle_b200"):
 
 METRIC = "effective shuffle GB/s (2×bytes×iters/time), % HBM peak, 1/2/4/8×B200"
 FALLBACK_HBM_GBS = 6650.0
-NVLINK_PEER_GBS = 770.0  # measured peer copy per direction per GPU on this pool
+NVLINK_PEER_GBS = 770.0  # measured peer copy per direction per GPU (B200, NVLink 5 through NVSwitch)
 
 WORKLOADS = {
     "bf16_32GiB": dict(
@@ -252,7 +252,7 @@ def run_ours(args, w: dict, wname: str) -> None:
         crossings = 1 if args.sharded_order == "push" else 2
         link_bytes = crossings * (world - 1) / world * (deck_bytes / world)
         bound, achieved, roof_peak, roof_kind = "nvlink", link_bytes / per_launch_s / 1e9, NVLINK_PEER_GBS, (
-            "measured peer copy per direction on this pool")
+            "measured peer copy per direction per GPU")
 
     # End to end: the same work with the deck in pinned host memory, copies inside the timed region.
     e2e = None

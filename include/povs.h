@@ -25,7 +25,7 @@ extern "C" {
 /* Return codes. */
 #define POVS_OK 0
 #define POVS_ERR_INVALID_ARGUMENT (-1) /* a size, option or pointer is out of range */
-#define POVS_ERR_UNSUPPORTED (-2)      /* valid for the algorithm but outside this build's limits */
+#define POVS_ERR_UNSUPPORTED (-2)      /* valid for the algorithm but outside this library's limits */
 #define POVS_ERR_CUDA (-3)             /* a CUDA runtime call failed */
 #define POVS_ERR_DEVICE_STATUS (-4)    /* a kernel reported a failure through the device status word */
 
@@ -45,7 +45,7 @@ extern "C" {
  * for it to complete before touching the deck). */
 #define POVS_FLAG_NO_PDL 8u
 
-/* Limits of this build. */
+/* Limits of this library. */
 #define POVS_MAX_OFFSETS 256 /* offsets are passed to the device inline in the launch parameters */
 #define POVS_MAX_VBLOCK 32   /* one warp lane per member pblock */
 #define POVS_MAX_VP 1024     /* V * P rows per vblock: one warp sorts the permutation in registers */

@@ -108,7 +108,7 @@ MODES = {"uniform": 0, "reference_cuda": 1}
 
 def device_randomness(seed: int, iteration: int, n_rows: int, pblock: int, vblock: int,
                       offsets: list[int], mode: str = "uniform") -> tuple[int, np.ndarray, np.ndarray]:
-    """This build's device randomness for one iteration: (offset, assign [n_v,V], perms [n_v,V*P])."""
+    """The library's device randomness for one iteration: (offset, assign [n_v,V], perms [n_v,V*P])."""
     n_p, n_v = block_counts(n_rows, pblock, vblock)
     offs = np.array(offsets, dtype=np.int64)
     off = np.zeros(1, dtype=np.int64)
@@ -123,7 +123,7 @@ def device_randomness(seed: int, iteration: int, n_rows: int, pblock: int, vbloc
 
 def shuffle(deck: np.ndarray, iterations: int, pblock: int, vblock: int, offsets: list[int], seed: int,
             mode: str = "uniform") -> None:
-    """This build's full shuffle (device randomness of ``seed``), in place on a host deck."""
+    """The library's full shuffle (device randomness of ``seed``), in place on a host deck."""
     rows = as_rows(deck)
     n, r = rows.shape
     offs = np.array(offsets, dtype=np.int64)

@@ -1,13 +1,13 @@
 /*
  * ORACLE - test infrastructure only.  Nothing in the product links, loads or calls this file;
- * it is the CPU checker the parity tests compare the CUDA library against.
+ * it is the CPU reference the parity tests compare the CUDA library against.
  *
  * Plain-C restatement of
  *   (1) one POV iteration with given randomness: the reference kernel's semantics
  *       (src/povs/__cuda/lib/povs.cu:203-221 member sort, :225-278 gather at offset-wrapped
  *       rows, :282-321 gap-free slot index, :325-348 permuted write-back), with the NumPy
  *       path's member order as an option (src/povs/numpy.py:120-136);
- *   (2) this build's device randomness (Philox4x32-10 of Salmon et al., SC'11; a 12-round
+ *   (2) the library's device randomness (Philox4x32-10 of Salmon et al., SC'11; a 12-round
  *       Feistel bijection with cycle walking for the pblock -> vblock map; per-vblock orders
  *       from sorting packed 32-bit (key | element) words), so the default GPU mode can be
  *       checked bit-exactly.
@@ -227,7 +227,7 @@ int oracle_apply_iteration(uint8_t* data, int64_t N, int64_t R, int P, int V, in
     return 0;
 }
 
-/* ---------------------------------------------------------------- this build's device randomness */
+/* ---------------------------------------------------------------- the library's device randomness */
 
 /* Seed in [1, 999] of vblock v (reference-CUDA mode). */
 static uint32_t vblock_seed(uint64_t seed, uint32_t iteration, uint64_t v)
@@ -332,7 +332,7 @@ int oracle_device_randomness(uint64_t seed, uint32_t iteration, int64_t N, int P
     return 0;
 }
 
-/* Full shuffle with this build's device randomness: iterations 0..iterations-1 of `seed` in `mode`. */
+/* Full shuffle with the library's device randomness: iterations 0..iterations-1 of `seed` in `mode`. */
 int oracle_shuffle(uint8_t* data, int64_t N, int64_t R, int P, int V, const int64_t* offsets, int n_offsets,
                    int iterations, uint64_t seed, int mode)
 {

@@ -143,7 +143,7 @@ def optim_options_for_dataset(
     :param data: ``torch.Tensor`` or ``numpy.ndarray``.
     :param options: Starting point.
     :param tuning: ``"reference"`` (default): the reference's choices, so the same dataset gets the
-        same options; ``"b200"``: ``physical_block_size`` chosen for this build's B200 kernel
+        same options; ``"b200"``: ``physical_block_size`` chosen for this library's B200 kernel
         (vblocks of up to 64 KiB / 512 rows; several times faster than the reference's choice for
         small rows).  Addition to the reference API.
     :returns: Complete options for the dataset's route (CUDA options include ``gpu_thread_block_size``).

@@ -7,7 +7,7 @@ class BuildParams(NamedTuple):
     """Build-time parameters of the native library.
 
     The reference compiles one template instantiation per (vblock, pblock, instance size, dtype)
-    and lists them here; this build's kernels are runtime-general, so the instantiation lists are
+    and lists them here; this library's kernels are runtime-general, so the instantiation lists are
     empty and ``cartesian_instancing`` is False.
     """
 

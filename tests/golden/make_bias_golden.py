@@ -10,9 +10,9 @@ shuffled deck is the episode.  Statistics (positional TVD, bigram TVD) for:
 * ``reference_cuda``   - the reference CUDA path's randomness (oracle/ref_cuda_rng.cpp: std::mt19937
                          host draws + the kernel's xorshift32 Fisher-Yates) applied by the C oracle;
 * ``numpy_shuffle``    - ``numpy.random.default_rng(episode).shuffle`` (the reference's baseline);
-* ``this_build``       - this build's device randomness through the oracle port; the GPU run must
+* ``library``       - the library's device randomness through the oracle port; the GPU run must
                          reproduce these episodes exactly;
-* ``this_build_reference_cuda`` - the same with ``randomness="reference_cuda"`` (the reference CUDA
+* ``library_reference_cuda`` - the same with ``randomness="reference_cuda"`` (the reference CUDA
                          path's distribution drawn on the device).
 
 Pass ``--reuse`` to keep the ``reference_numpy`` statistics already in the file (they take minutes).
@@ -76,7 +76,7 @@ def oracle_episodes(n_episodes: int, kind: str, mode: str = "uniform") -> np.nda
     for i, it in enumerate(ITERATIONS):
         for s in range(n_episodes):
             d = fresh_deck()
-            if kind == "this_build":
+            if kind == "library":
                 api.shuffle(d, it, P, V, OFFSETS, s, mode)
             else:
                 offs, assign, perms = api.refcuda_randomness(s, N_ROWS, P, V, OFFSETS, it)
@@ -97,8 +97,8 @@ def main(reference_root: str = "/root/reference", n_episodes: int = 3000, reuse:
         "episodes": n_episodes,
     }
     sets = {
-        "this_build": oracle_episodes(n_episodes, "this_build"),
-        "this_build_reference_cuda": oracle_episodes(n_episodes, "this_build", "reference_cuda"),
+        "library": oracle_episodes(n_episodes, "library"),
+        "library_reference_cuda": oracle_episodes(n_episodes, "library", "reference_cuda"),
         "reference_cuda": oracle_episodes(n_episodes, "reference_cuda"),
     }
     previous = json.loads(OUT.read_text()) if (reuse and OUT.exists()) else {}
@@ -117,8 +117,8 @@ def main(reference_root: str = "/root/reference", n_episodes: int = 3000, reuse:
         np.random.default_rng(s).shuffle(a)
         base[s] = a
     result["numpy_shuffle"] = {"positional_tvd": metrics.positional_tvd(base), "bigram_tvd": metrics.bigram_tvd(base)}
-    # Checksums of this build's episodes, so the GPU run can be compared exactly.
-    for key in ("this_build", "this_build_reference_cuda"):
+    # Checksums of the library's episodes, so the GPU run can be compared exactly.
+    for key in ("library", "library_reference_cuda"):
         tb = sets[key].astype(np.int64)
         result[f"{key}_checksums"] = [
             int((tb[i] * np.arange(1, N_ROWS + 1)).sum() % (2**61 - 1)) for i in range(len(ITERATIONS))

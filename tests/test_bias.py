@@ -2,7 +2,7 @@
 
 Workload (tests/golden/make_bias_golden.py): int32 deck 1000 x 16 with row i = i, V = 2, P = 8,
 offsets 0..7; 3000 episodes seeded 0..2999; for it = 1..8 every episode shuffles a fresh deck with
-``iterations=it``.  The GPU must reproduce this build's episodes exactly (checksums from the
+``iterations=it``.  The GPU must reproduce the library's episodes exactly (checksums from the
 oracle port) and its TVDs must match the reference's within the stated tolerance.
 """
 
@@ -21,7 +21,7 @@ BIAS = json.loads((GOLDEN / "bias_suite.json").read_text())
 N_ROWS, WIDTH, V, P = 1000, 16, 2, 8
 OFFSETS = list(range(8))
 
-# |TVD(this build) - TVD(reference)| per iteration count, absolute:
+# |TVD(library) - TVD(reference)| per iteration count, absolute:
 # * randomness="reference_cuda" reproduces the reference CUDA path's distribution -> within 0.005 of it;
 # * the default uniform mode draws exactly uniform per-vblock permutations, while the reference's NumPy
 #   path draws them from only 999 seeds per vblock (RandomState(1..999)); at 1-2 iterations that shows
@@ -56,8 +56,8 @@ def _checksum(col0: np.ndarray) -> int:
     return int((col0.astype(np.int64) * np.arange(1, N_ROWS + 1)).sum() % (2**61 - 1))
 
 
-def test_golden_this_build_statistics_regenerate(oracle_api):
-    """The golden statistics of this build come from the oracle port: spot-check a subset."""
+def test_golden_library_statistics_regenerate(oracle_api):
+    """The golden statistics of the library come from the oracle port: spot-check a subset."""
     n = 100
     for i, it in enumerate(BIAS["iterations"][:3]):
         eps = np.zeros((n, N_ROWS), dtype=np.int64)
@@ -66,29 +66,29 @@ def test_golden_this_build_statistics_regenerate(oracle_api):
             oracle_api.shuffle(d, it, P, V, OFFSETS, s)
             eps[s] = d[:, 0]
         assert metrics.positional_tvd(eps) > 0.0
-    assert len(BIAS["this_build_checksums"]) == 8
+    assert len(BIAS["library_checksums"]) == 8
 
 
 def test_reference_statistics_are_recorded():
-    for name in ("this_build", "reference_cuda"):
+    for name in ("library", "reference_cuda"):
         assert len(BIAS[name]["positional_tvd"]) == 8 and len(BIAS[name]["bigram_tvd"]) == 8
     # Bias shrinks with iterations for every implementation.
-    for name in ("this_build", "reference_cuda", "reference_numpy"):
+    for name in ("library", "reference_cuda", "reference_numpy"):
         if name in BIAS:
             pos = BIAS[name]["positional_tvd"]
             assert pos[0] > pos[3] > pos[7]
 
 
 def test_golden_statistics_meet_the_stated_tolerances():
-    ref_mode, ref_cuda = BIAS["this_build_reference_cuda"], BIAS["reference_cuda"]
+    ref_mode, ref_cuda = BIAS["library_reference_cuda"], BIAS["reference_cuda"]
     for key in ("positional_tvd", "bigram_tvd"):
         assert max(abs(a - b) for a, b in zip(ref_mode[key], ref_cuda[key])) <= TVD_TOLERANCE_REFERENCE_MODE
     if "reference_numpy" in BIAS:
-        uni, ref_np = BIAS["this_build"], BIAS["reference_numpy"]
+        uni, ref_np = BIAS["library"], BIAS["reference_numpy"]
         for key in ("positional_tvd", "bigram_tvd"):
             assert max(abs(a - b) for a, b in zip(uni[key], ref_np[key])) <= TVD_TOLERANCE_UNIFORM_VS_NUMPY
     # The uniform mode is never more biased than the reference CUDA path.
-    for a, b in zip(BIAS["this_build"]["positional_tvd"], BIAS["reference_cuda"]["positional_tvd"]):
+    for a, b in zip(BIAS["library"]["positional_tvd"], BIAS["reference_cuda"]["positional_tvd"]):
         assert a <= b + 1e-3
 
 
@@ -115,7 +115,7 @@ def _gpu_episodes(it: int, randomness: str):
 @pytest.mark.parametrize("randomness", ["uniform", "reference_cuda"])
 def test_gpu_bias_suite(randomness):
     """3000 GPU episodes per iteration count: identical to the oracle port, TVDs within tolerance."""
-    key = "this_build" if randomness == "uniform" else "this_build_reference_cuda"
+    key = "library" if randomness == "uniform" else "library_reference_cuda"
     got_pos, got_bi = [], []
     for i, it in enumerate(BIAS["iterations"]):
         eps = _gpu_episodes(it, randomness)
@@ -130,7 +130,7 @@ def test_gpu_bias_suite(randomness):
         ref = BIAS["reference_cuda"]
         tol = TVD_TOLERANCE_REFERENCE_MODE
     else:
-        ref = BIAS.get("reference_numpy", BIAS["this_build"])
+        ref = BIAS.get("reference_numpy", BIAS["library"])
         tol = TVD_TOLERANCE_UNIFORM_VS_NUMPY
     assert max(abs(a - b) for a, b in zip(got_pos, ref["positional_tvd"])) <= tol
     assert max(abs(a - b) for a, b in zip(got_bi, ref["bigram_tvd"])) <= tol

@@ -1,4 +1,4 @@
-"""CPU checks that pin the oracle before it is trusted as the GPU checker."""
+"""CPU checks that pin the oracle before the GPU parity tests compare the library against it."""
 
 from __future__ import annotations
 
