@@ -139,8 +139,10 @@ def preflight(data: np.ndarray, iterations: int, options: Options) -> None:
 def shuffle_many(decks: list, iterations: int, options: Options | None, seeds: list[int], flags: int = 0) -> None:
     """Shuffle several host decks of one shape in place, overlapping their copies with the GPU work.
 
-    Two device staging buffers are used, so deck d's copy back overlaps deck d+1's copy in and
-    iterations.  Arrays that are not C-contiguous are staged through contiguous copies.
+    Up to three device staging buffers (as many as fit the device's free memory) are used in
+    rotation, so one deck's copy back overlaps another's copy in and a third's iterations; decks
+    that do not fit at all are shuffled in host memory one by one (mapped).  Arrays that are not
+    C-contiguous are staged through contiguous copies (one per distinct array).
     """
     if not decks:
         return
@@ -157,15 +159,32 @@ def shuffle_many(decks: list, iterations: int, options: Options | None, seeds: l
         return
     if not torch.cuda.is_available():
         raise RuntimeError("povs requires a CUDA device (B200, sm_100a); none is available")
-    hosts = [d if d.flags.c_contiguous else np.ascontiguousarray(d) for d in decks]
+    staged: dict[int, np.ndarray] = {}
+    for d in decks:
+        if not d.flags.c_contiguous and id(d) not in staged:
+            staged[id(d)] = np.ascontiguousarray(d)
+    hosts = [staged.get(id(d), d) for d in decks]
     n_rows = first.shape[0]
     device = torch.device("cuda", torch.cuda.current_device())
-    buffers = [torch.empty(n_rows * row_bytes, dtype=torch.uint8, device=device) for _ in range(min(2, len(decks)))]
-    _native.shuffle_host_batch(
-        [h.ctypes.data for h in hosts], buffers, n_rows, row_bytes, list(options.offsets), iterations,
-        options.physical_block_size, options.virtual_block_size, [seed_to_u64(s) for s in seeds],
-        flags | randomness_flags(options),
-    )
-    for d, h in zip(decks, hosts):
-        if h is not d:
+    deck_bytes = n_rows * row_bytes
+    free, _ = torch.cuda.mem_get_info(device)
+    n_buffers = min(3, len(decks))
+    while n_buffers > 0 and n_buffers * deck_bytes + DEVICE_HEADROOM_BYTES > free:
+        n_buffers -= 1
+    if n_buffers == 0:
+        for h, sd in zip(hosts, seeds):
+            _native.shuffle_mapped(
+                h.ctypes.data, n_rows, row_bytes, list(options.offsets), iterations, options.physical_block_size,
+                options.virtual_block_size, seed_to_u64(sd), device.index, flags | randomness_flags(options),
+            )
+    else:
+        buffers = [torch.empty(deck_bytes, dtype=torch.uint8, device=device) for _ in range(n_buffers)]
+        _native.shuffle_host_batch(
+            [h.ctypes.data for h in hosts], buffers, n_rows, row_bytes, list(options.offsets), iterations,
+            options.physical_block_size, options.virtual_block_size, [seed_to_u64(sd) for sd in seeds],
+            flags | randomness_flags(options),
+        )
+    for d in decks:
+        h = staged.get(id(d))
+        if h is not None:
             d[...] = h

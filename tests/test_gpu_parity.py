@@ -418,6 +418,27 @@ def test_host_batch_repeated_decks_with_three_buffers(oracle_api):
         assert np.array_equal(t.numpy(), w)
 
 
+@pytest.mark.parametrize("free_bytes", [None, 1 << 20])
+def test_shuffle_many_strided_deck_listed_twice(oracle_api, monkeypatch, free_bytes):
+    """A non-contiguous deck listed twice is shuffled twice in order, through device buffers or,
+    when the device has no room (``free_bytes``), in host memory."""
+    if free_bytes is not None:
+        monkeypatch.setattr(torch.cuda, "mem_get_info", lambda *a, **k: (free_bytes, 1 << 34))
+    n, R, P, V, offsets = 12_007, 16, 16, 2, [0, 1, 2]
+    base = random_rows(n, 2 * R, seed=31)
+    whole = base.copy()
+    strided = whole[:, R:]
+    other = random_rows(n, R, seed=32)
+    other_copy = other.copy()
+    povs.shuffle_many([strided, other, strided], iterations=2, options=povs.Options(V, P, offsets), seed=40)
+    want = np.ascontiguousarray(base[:, R:])
+    oracle_api.shuffle(want, 2, P, V, offsets, 40)
+    oracle_api.shuffle(want, 2, P, V, offsets, 42)
+    assert np.array_equal(whole[:, R:], want) and np.array_equal(whole[:, :R], base[:, :R])
+    oracle_api.shuffle(other_copy, 2, P, V, offsets, 41)
+    assert np.array_equal(other, other_copy)
+
+
 def test_shuffle_many_matches_one_deck_at_a_time():
     """Pipelined host decks: deck d gets seed + d, exactly like separate host-route calls."""
     rng = np.random.default_rng(4)
