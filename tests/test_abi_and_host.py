@@ -66,6 +66,35 @@ def test_invalid_arguments_are_rejected_before_any_device_call():
     assert lib.povs_shuffle_v1(ctypes.c_void_p(16), 64, 4, many, 300, 1, 16, 2, 0, 0, None, 0) == -2
 
 
+def test_added_entry_points_reject_invalid_arguments_before_any_device_call():
+    """Batched decks, mapped host decks and the metric kernels check their arguments on the host."""
+    lib = _native.load()
+    offs = (ctypes.c_int64 * 2)(0, 4)
+    seeds = ctypes.c_void_p(64)
+    data = ctypes.c_void_p(16)
+    # Batched decks: NULL seeds, no decks, overlapping decks, unknown flags.
+    assert lib.povs_shuffle_batch_v1(data, 2, 256, 64, 4, offs, 2, 1, 16, 2, None, 0, None, 0) == -1
+    assert b"seeds" in lib.povs_last_error_string()
+    assert lib.povs_shuffle_batch_v1(data, 0, 256, 64, 4, offs, 2, 1, 16, 2, seeds, 0, None, 0) == -1
+    assert lib.povs_shuffle_batch_v1(data, 2, 100, 64, 4, offs, 2, 1, 16, 2, seeds, 0, None, 0) == -1
+    assert b"deck_stride" in lib.povs_last_error_string()
+    assert lib.povs_shuffle_batch_v1(data, 2, 256, 64, 4, offs, 2, 1, 16, 2, seeds, 0, None, 64) == -1
+    assert b"flags" in lib.povs_last_error_string()
+    # Mapped host decks: NULL deck, bad pblock.
+    assert lib.povs_shuffle_mapped_v1(None, 64, 4, offs, 2, 1, 16, 2, 0, 0, None, 0) == -1
+    assert lib.povs_shuffle_mapped_v1(data, 64, 4, offs, 2, 1, 12, 2, 0, 0, None, 0) == -1
+    # Metric kernels: NULL ids, bad id width, unknown kind, n-gram degree below 2.
+    counts = ctypes.c_void_p(32)
+    assert lib.povs_travel_histogram_v1(None, 4, 10, 10, 10, 1, 0, 1, counts, 0, None) == -1
+    assert lib.povs_travel_histogram_v1(data, 3, 10, 10, 10, 1, 0, 1, counts, 0, None) == -1
+    assert b"id_bytes" in lib.povs_last_error_string()
+    assert lib.povs_travel_histogram_v1(data, 4, 10, 10, 10, 1, 2, 1, counts, 0, None) == -1
+    assert lib.povs_travel_histogram_v1(data, 4, 10, 10, 10, 1, 1, 0, counts, 0, None) == -1
+    assert lib.povs_ngram_keys_v1(data, 8, 10, 10, 10, 1, 1, 1, None, 0, counts, 0, None) == -1
+    assert b"degree" in lib.povs_last_error_string()
+    assert lib.povs_ngram_keys_v1(data, 8, 0, 10, 10, 1, 3, 1, None, 0, counts, 0, None) == -1
+
+
 def test_unsupported_container_raises_type_error():
     with pytest.raises(TypeError):
         povs.shuffle([1, 2, 3])
