@@ -13,6 +13,8 @@
 #include <unordered_map>
 #include <vector>
 
+#include <unistd.h>
+
 #include "../../include/povs.h"
 #include "povs_kernel.cuh"
 #include "povs_metrics.cuh"
@@ -1347,7 +1349,8 @@ extern "C" int povs_shuffle_mapped_v1(void* host_data, int64_t n_rows, int64_t r
     POVS_CUDA_TRY(cudaPointerGetAttributes(&attr, host_data));
     void* registered = nullptr;
     if (attr.type == cudaMemoryTypeUnregistered) {
-        const uintptr_t page = 4096;
+        const long sys_page = sysconf(_SC_PAGESIZE);
+        const uintptr_t page = sys_page > 0 ? static_cast<uintptr_t>(sys_page) : 4096u;
         const uintptr_t begin = reinterpret_cast<uintptr_t>(host_data) & ~(page - 1);
         const uintptr_t end = (reinterpret_cast<uintptr_t>(host_data) + static_cast<uintptr_t>(n_rows * row_bytes) +
                                page - 1) & ~(page - 1);
