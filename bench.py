@@ -332,6 +332,11 @@ def run_e2e(args, w, deck, opts, offsets, iters, world, rank, local, stream, sha
     # busy (a deck's copy in never waits for its own previous copy out); two when host memory is short.
     avail = psutil.virtual_memory().available
     n_host = (3 if avail >= 3.5 * total_bytes else 2) if world == 1 else 1
+    if world == 1:
+        # The extra device buffers must fit next to the resident deck.
+        free_dev, _ = torch.cuda.mem_get_info(deck.device)
+        while n_host > 1 and (n_host - 1) * shard_bytes + (2 << 30) > free_dev:
+            n_host -= 1
     # Decide once (rank 0, before anything is pinned) so that every rank takes the same steps.
     ok = torch.tensor([1 if avail >= (n_host + 0.5) * total_bytes else 0], device=deck.device)
     if world > 1:
