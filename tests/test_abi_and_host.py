@@ -37,6 +37,41 @@ def test_library_loads_and_exports_every_declared_symbol():
     assert set(_native.SIGNATURES) == _declared_functions()
 
 
+C_CALLER = r"""
+#include <stdio.h>
+#include "povs.h"
+int main(void)
+{
+    int64_t offsets[2] = {0, 4};
+    if (povs_version() < 100) return 2;
+    /* A NULL deck is rejected on the host, before any device call. */
+    int rc = povs_shuffle_v1(NULL, 64, 4, offsets, 2, 1, 16, 2, 42u, 0, NULL, 0);
+    if (rc != POVS_ERR_INVALID_ARGUMENT) return 3;
+    printf("%s\n", povs_last_error_string());
+    return 0;
+}
+"""
+
+
+def test_header_serves_plain_c_callers(tmp_path):
+    """include/povs.h compiles as C99 and a C program links and calls the library."""
+    import shutil
+    import subprocess
+
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("gcc is not available")
+    src = tmp_path / "caller.c"
+    src.write_text(C_CALLER)
+    exe = tmp_path / "caller"
+    lib = _build.LIB_PATH
+    subprocess.run([gcc, "-std=c99", "-Wall", "-Werror", f"-I{_build.INCLUDE_DIR}", str(src), "-o", str(exe),
+                    str(lib), f"-Wl,-rpath,{lib.parent}"], check=True, capture_output=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, (out.returncode, out.stderr)
+    assert "NULL" in out.stdout
+
+
 def test_library_is_built_for_sm100a():
     params = povs.get_build_params()
     assert params.cuda_arch == ["100a"]
