@@ -34,15 +34,18 @@ extern "C" {
 #define POVS_DEV_BAD_INJECTED 2 /* an injected permutation entry was out of range and was ignored */
 
 /* Flags of povs_shuffle_v1(). */
-#define POVS_FLAG_NO_GRAPH 1u /* launch the iterations one by one instead of replaying a CUDA graph */
+/* Launch the iterations one by one (by default decks under 32 MiB replay a cached CUDA graph and
+ * larger decks are launched one by one). */
+#define POVS_FLAG_NO_GRAPH 1u
 #define POVS_FLAG_SYNC 2u     /* synchronize the stream and check the device status before returning */
 /* Draw the randomness with the distribution of the reference's CUDA path (per-vblock seeds 1..999,
  * xorshift32 forward Fisher-Yates, padding in the last vblock; src/povs/__cuda/lib/povs.cu:396-430,
  * 294-316) instead of uniform per-vblock permutations.  For statistical comparisons with it. */
 #define POVS_FLAG_REFERENCE_RNG 4u
-/* Chain the iterations of one call with ordinary stream order instead of programmatic dependent
- * launches (by default iteration i+1's CTAs start their set-up while iteration i drains, and wait
- * for it to complete before touching the deck). */
+/* Order the iteration kernels with ordinary stream order instead of programmatic dependent
+ * launches (by default each iteration kernel's CTAs start their set-up while the kernel before it
+ * on the stream drains - the previous iteration, or for decks of 32 MiB and more the previous
+ * call's last iteration - and wait for it to complete before touching the deck). */
 #define POVS_FLAG_NO_PDL 8u
 
 /* Limits of this library. */

@@ -162,6 +162,28 @@ def test_graph_and_direct_launches_agree(oracle_api):
     assert not np.array_equal(a, c)
 
 
+def test_back_to_back_calls_on_a_large_deck(oracle_api):
+    """Decks of 32 MiB and more launch every iteration chained to the kernel before it on the
+    stream, the previous call's last iteration included: two calls in a row and a host-side
+    write in between must still see each other's results."""
+    n, R, P, V, offsets = 300_007, 128, 32, 4, [0, 1, 2, 3]
+    host = random_rows(n, R, seed=17)
+    deck = torch.from_numpy(host.copy()).to(DEV)
+    assert n * R >= 32 << 20
+    _native.shuffle_device(deck, R, offsets, 3, P, V, 5)
+    _native.shuffle_device(deck, R, offsets, 2, P, V, 6)
+    deck[:1000] = 0  # a torch kernel between two shuffle calls
+    _native.shuffle_device(deck, R, offsets, 1, P, V, 7)
+    torch.cuda.synchronize()
+    povs.check_device_status(0)
+    want = host.copy()
+    oracle_api.shuffle(want, 3, P, V, offsets, 5)
+    oracle_api.shuffle(want, 2, P, V, offsets, 6)
+    want[:1000] = 0
+    oracle_api.shuffle(want, 1, P, V, offsets, 7)
+    assert np.array_equal(deck.cpu().numpy(), want)
+
+
 def test_misaligned_deck_uses_plain_loads(oracle_api):
     n_rows, row_bytes, P, V, offsets = 3000, 16, 16, 2, [0, 1, 2]
     host = random_rows(n_rows, row_bytes, seed=5)
