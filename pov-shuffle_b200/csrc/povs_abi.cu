@@ -1372,11 +1372,17 @@ extern "C" int povs_shuffle_mapped_v1(void* host_data, int64_t n_rows, int64_t r
                                page - 1) & ~(page - 1);
         registered = reinterpret_cast<void*>(begin);
         POVS_CUDA_TRY(cudaHostRegister(registered, end - begin, cudaHostRegisterMapped | cudaHostRegisterPortable));
+        cudaError_t q = cudaPointerGetAttributes(&attr, host_data);
+        if (q != cudaSuccess) {
+            cudaHostUnregister(registered);
+            return cuda_fail(q, "cudaPointerGetAttributes");
+        }
     } else if (attr.type != cudaMemoryTypeHost) {
         return fail(POVS_ERR_INVALID_ARGUMENT, "host_data is not host memory (use povs_shuffle_v1 for device decks)");
     }
-    void* mapped = nullptr;
-    cudaError_t e = cudaHostGetDevicePointer(&mapped, host_data, 0);
+    // The device-side address of this very byte (interior pointers into a pinned block included).
+    void* mapped = attr.devicePointer;
+    cudaError_t e = mapped != nullptr ? cudaSuccess : cudaErrorInvalidValue;
     if (e == cudaSuccess) {
         // Plain vector loads and stores over the interconnect; TMA copies are not used on host memory.
         r = shuffle_on_device(mapped, n_rows, row_bytes, offsets, n_offsets, iterations, pblock, vblock, seed, *c, s,
@@ -1386,7 +1392,7 @@ extern "C" int povs_shuffle_mapped_v1(void* host_data, int64_t n_rows, int64_t r
             if (e != cudaSuccess) r = cuda_fail(e, "cudaStreamSynchronize");
         }
     } else {
-        r = cuda_fail(e, "cudaHostGetDevicePointer");
+        r = fail(POVS_ERR_INVALID_ARGUMENT, "host_data is page-locked but not mapped into the device's address space");
     }
     if (registered != nullptr) {
         if (r != POVS_OK) cudaStreamSynchronize(s);  // the deck must not be unmapped under a running kernel

@@ -97,13 +97,18 @@ def test_b200_tuned_options_shuffle_like_the_oracle(oracle_api, row_bytes):
     assert np.array_equal(deck.cpu().numpy(), want)
 
 
-@pytest.mark.parametrize("pinned", [False, True])
+@pytest.mark.parametrize("pinned", [False, True, "interior"])
 @pytest.mark.parametrize("row_bytes", [48, 12])
 def test_mapped_host_deck_matches_oracle(oracle_api, pinned, row_bytes):
-    """A host deck shuffled where it lies (mapped, page-locked for the call or already pinned)."""
+    """A host deck shuffled where it lies (mapped, page-locked for the call or already pinned,
+    or a view that starts inside a pinned block)."""
     n, P, V, offsets = 100_003, 32, 4, [0, 1, 2, 5]
-    host = random_rows(n, row_bytes, seed=row_bytes + pinned)
-    if pinned:
+    host = random_rows(n, row_bytes, seed=row_bytes + (pinned is True))
+    if pinned == "interior":
+        buf = torch.empty((n + 7, row_bytes), dtype=torch.uint8, pin_memory=True)
+        arr = buf.numpy()[7:]
+        arr[...] = host
+    elif pinned:
         buf = torch.empty((n, row_bytes), dtype=torch.uint8, pin_memory=True)
         arr = buf.numpy()
         arr[...] = host
