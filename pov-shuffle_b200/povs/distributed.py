@@ -8,8 +8,8 @@ indices only.  Options are resolved and validated against the whole deck.
 One process per GPU (``ShardedDeck``): every rank maps the other ranks' shards with CUDA IPC at
 construction, with a device barrier between iterations.  Two orders give the same result:
 
-* double-buffered (default; one scratch buffer per shard): every rank moves the pblocks stored in
-  its own shard, reading them locally and storing each row straight into its destination slot in
+* double-buffered (default when every GPU has room for a scratch copy of its shard): every rank
+  moves the pblocks stored in its own shard, reading them locally and storing each row straight into its destination slot in
   the other buffer (local or a peer's), so a row crosses NVLink at most once per iteration;
 * in place (``double_buffer=False``, no extra memory): every rank runs the vblocks
   ``rank, rank + world, ...``, reading member rows from local or peer memory (bulk copies, no
@@ -43,6 +43,8 @@ from .torch import _choose_pblock_size, _choose_thr_block_size, _validate_thr_bl
 from .types import Options
 
 MAX_SHARDS = 8
+# Free device memory to leave next to a shard's scratch copy when double-buffering is automatic.
+SCRATCH_HEADROOM_BYTES = 2 << 30
 
 
 def _row_layout(t: torch.Tensor) -> tuple[tuple[int, ...], torch.dtype]:
@@ -127,11 +129,12 @@ class ShardedDeck:
                   has the same row shape and dtype, and at least ``physical_block_size`` rows.
     :param group: process group (default: the world).  Construction is collective.
     :param double_buffer: allocate a scratch buffer the size of the shard and shuffle in the
-                          double-buffered order (half the NVLink traffic of the in-place order).
+                          double-buffered order (half the NVLink traffic of the in-place order);
+                          None (default) does so when every rank's GPU has room for it.
     """
 
     def __init__(self, shard: torch.Tensor, group: dist.ProcessGroup | None = None, native: Any = None,
-                 double_buffer: bool = True):
+                 double_buffer: bool | None = None):
         self.native = native if native is not None else _native
         self.group = group
         self.rank = dist.get_rank(group)
@@ -140,9 +143,23 @@ class ShardedDeck:
         assert shard.is_contiguous(), "Tensor must be contiguous"
         self.shard = shard
         self.device = shard.device
+        if double_buffer is None:
+            # Double-buffer when a scratch copy of the shard fits next to it (every rank must agree).
+            room = True
+            if shard.is_cuda:
+                free, _ = torch.cuda.mem_get_info(shard.device)
+                room = free >= shard.numel() * shard.element_size() + SCRATCH_HEADROOM_BYTES
+        else:
+            room = bool(double_buffer)
         meta = [None] * self.world
-        dist.all_gather_object(meta, (int(shard.shape[0]), tuple(shard.shape[1:]), str(shard.dtype)), group=group)
-        assert all(m[1:] == meta[0][1:] for m in meta), f"shards differ in row shape or dtype: {meta}"
+        dist.all_gather_object(meta, (int(shard.shape[0]), tuple(shard.shape[1:]), str(shard.dtype), room),
+                               group=group)
+        assert all(m[1:3] == meta[0][1:3] for m in meta), f"shards differ in row shape or dtype: {meta}"
+        if double_buffer is None:
+            double_buffer = all(m[3] for m in meta)
+        else:
+            assert all(m[3] == double_buffer for m in meta), "every rank must pass the same double_buffer"
+        self.double_buffer = double_buffer
         self.shard_rows = [m[0] for m in meta]
         self.n_rows = sum(self.shard_rows)
         self.instance_size = math.prod(shard.shape[1:]) if shard.ndim > 1 else 1
