@@ -9,8 +9,9 @@ One process per GPU (``ShardedDeck``): every rank maps the other ranks' shards w
 construction, with a device barrier between iterations.  Two orders give the same result:
 
 * double-buffered (default when every GPU has room for a scratch copy of its shard): every rank
-  moves the pblocks stored in its own shard, reading them locally and storing each row straight into its destination slot in
-  the other buffer (local or a peer's), so a row crosses NVLink at most once per iteration;
+  moves the pblocks stored in its own shard, reading them locally and storing each row straight
+  into its destination slot in the other buffer (local or a peer's), so a row crosses NVLink at
+  most once per iteration;
 * in place (``double_buffer=False``, no extra memory): every rank runs the vblocks
   ``rank, rank + world, ...``, reading member rows from local or peer memory (bulk copies, no
   multicast) and writing them back with peer stores, so a remote row crosses twice.
