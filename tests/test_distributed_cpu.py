@@ -56,6 +56,13 @@ def _worker(rank: int, world: int, port: int, out_dir: str):
     except AssertionError as e:
         errors.append(str(e))
     deck.close()
+    # Ranks that disagree on double_buffer are told so on every rank (collective check).
+    try:
+        ShardedDeck(shard, native=RecordingNative(), double_buffer=(rank == 0))
+    except AssertionError as e:
+        errors.append(str(e))
+    in_place = ShardedDeck(shard, native=RecordingNative(), double_buffer=False)
+    errors.append(f"in_place scratch={in_place.scratch_ptrs}")
     calls = [c for c in native.calls if c[0] == "shuffle"]
     result = {
         "shard_rows": deck.shard_rows,
@@ -83,6 +90,7 @@ def test_two_rank_control_plane(tmp_path):
         assert res["epochs"] == [0, 4], "epoch base advances by iterations + 1 per shuffle"
         assert res["seeds"] == [11, 12], "every rank uses rank 0's seed"
         assert res["errors"] and "at least physical_block_size" in res["errors"][0]
+        assert "same double_buffer" in res["errors"][1] and res["errors"][2] == "in_place scratch=None"
         assert res["closed"] == 3, "shard, barrier flags and scratch of the one peer are unmapped"
         assert len(res["scratch"]) == 2 and all(len(p) == 2 for p in res["scratch"])
     assert r0["shard_ptrs"][1] == 1000 + 1 and r1["shard_ptrs"][0] == 1000 + 0
