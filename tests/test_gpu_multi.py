@@ -35,7 +35,7 @@ def _split(world: int) -> list[int]:
     return rows
 
 
-def _worker(rank: int, world: int, port: int, out_dir: str, randomness: str, double_buffer: bool):
+def _worker(rank: int, world: int, port: int, out_dir: str, randomness: str, double_buffer: bool | None):
     sys.path[:0] = [str(REPO), str(REPO / "pov-shuffle_b200")]
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -57,14 +57,18 @@ def _worker(rank: int, world: int, port: int, out_dir: str, randomness: str, dou
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("randomness", ["uniform", "reference_cuda"])
-@pytest.mark.parametrize("double_buffer", [False, True])
+CASES = [("uniform", False), ("uniform", True), ("reference_cuda", False), ("reference_cuda", True),
+         ("uniform", None)]
+
+
+@pytest.mark.parametrize("randomness,double_buffer", CASES)
 def test_sharded_deck_matches_oracle(oracle_api, tmp_path, randomness, double_buffer):
-    """Odd (3) then even (2) iteration counts: the double-buffered order ends in the shard both ways."""
+    """Odd (3) then even (2) iteration counts: the double-buffered order ends in the shard both ways.
+    double_buffer=None lets the ranks choose together (double-buffered when every GPU has room)."""
     world = min(torch.cuda.device_count(), 8)
     if world < 2:
         pytest.skip("needs at least two GPUs")
-    port = 31000 + (os.getpid() % 2000) + (7 if randomness == "uniform" else 0) + (3 if double_buffer else 0)
+    port = 31000 + (os.getpid() % 2000) + 11 * CASES.index((randomness, double_buffer))
     mp.start_processes(_worker, args=(world, port, str(tmp_path), randomness, double_buffer), nprocs=world,
                        start_method="spawn", join=True)
     got = np.concatenate([np.load(tmp_path / f"rank{r}.npy") for r in range(world)])
