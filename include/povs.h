@@ -59,7 +59,7 @@ extern "C" {
  * bijection of pblocks onto vblock slots, per-vblock permutations).
  *
  * Replaces the reference's native entry `torch_binding(X, O, iterations,
- * pblock, vblock, block_size, seed)` (src/povs/_cuda.pyi:7-15,
+ * pblock, vblock, block_size, seed)` (src/povs/_cuda.pyi:9-17,
  * src/povs/__cuda/binds/torch.cpp:19-60) and the host loop it dispatches to
  * (src/povs/__cuda/lib/povs.cu:356-467).  Differences: the device pointer and
  * the row size replace the typed tensor (any dtype); offsets are a host array;
@@ -241,12 +241,17 @@ int povs_describe_plan_v1(void* data, int64_t n_rows, int64_t row_bytes, int32_t
  * Limit: one iteration needs 256 + round_up(8 * n_v * V, 256) + 4 * n_v * V * P bytes; larger
  * decks are rejected with POVS_ERR_UNSUPPORTED (use povs_apply_v1 then).
  * The first call on a device looks up the scratch array's device address (with that device
- * current) and reads its limits; make that first call before any stream capture.
+ * current) and reads its limits; make that first call before any stream capture.  With lazy
+ * module loading (the CUDA 12 default) the array and the kernels come into being on the library's
+ * first use on a device, so make one povs call there (iterations = 0 is enough: the set-up still
+ * runs) before a memory pool reserves the GPU's free memory or the process stops allocating.
  * Every call shares the one array, which keeps the last call's contents (the status word in it is
- * cleared at the start of each call): calls that overlap on the GPU race.  With POVS_FLAG_SYNC the
- * call synchronizes `stream` and returns POVS_ERR_DEVICE_STATUS if a kernel reported a failure;
- * otherwise it returns after enqueueing, and the host arrays must stay unchanged until the stream
- * has run the work (pinned host memory is read asynchronously).
+ * cleared at the start of each call): calls that overlap on the GPU race.  Device failures (a
+ * wait that timed out, an out-of-range injected permutation entry) are reported only with
+ * POVS_FLAG_SYNC, the one flag accepted: the call then synchronizes `stream` and returns
+ * POVS_ERR_DEVICE_STATUS; povs_device_status_v1 does not see this entry's status word.  Without it
+ * the call returns after enqueueing, and the host arrays must stay unchanged until the stream has
+ * run the work (pinned host memory is read asynchronously).
  */
 #define POVS_STATIC_SCRATCH_BYTES (8u * 1024u * 1024u)
 int povs_apply_static_v1(void* data, int64_t n_rows, int64_t row_bytes, int32_t pblock, int32_t vblock,
@@ -261,7 +266,7 @@ int povs_apply_static_v1(void* data, int64_t n_rows, int64_t row_bytes, int32_t 
  * leave it.  `seeds` is a DEVICE array of n_decks seeds that must stay unchanged until the stream
  * has run the work.  Flags as povs_shuffle_v1.
  * Replaces the reference's loop of one povs.shuffle call per episode in its bias exercises
- * (src/povs/eval/exercises.py:387-389, 268-270).
+ * (src/povs/eval/exercises.py:387-389, 247-249).
  */
 int povs_shuffle_batch_v1(void* data, int64_t n_decks, int64_t deck_stride, int64_t n_rows, int64_t row_bytes,
                           const int64_t* offsets, int32_t n_offsets, int32_t iterations, int32_t pblock,

@@ -15,6 +15,7 @@ from . import build as _build
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
 _ref: ctypes.CDLL | None = None
+_ref_cuda: ctypes.CDLL | None = None
 
 _P = ctypes.c_void_p
 
@@ -46,6 +47,8 @@ def lib() -> ctypes.CDLL:
             L.oracle_refcuda_randomness.argtypes = [ctypes.c_int32, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, _P,
                                                     ctypes.c_int32, ctypes.c_int32, _P, _P, _P]
             L.oracle_refcuda_randomness.restype = ctypes.c_int
+            L.oracle_refcuda_perms.argtypes = [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, _P, _P, _P]
+            L.oracle_refcuda_perms.restype = ctypes.c_int
             _lib = L
         return _lib
 
@@ -64,6 +67,70 @@ def ref_lib() -> ctypes.CDLL | None:
             R.ref_assign_sequence.restype = ctypes.c_int
             _ref = R
         return _ref
+
+
+def ref_cuda_lib() -> ctypes.CDLL | None:
+    """The reference's own CUDA path compiled for sm_100a (oracle/_ref/libref_povs_cuda.so), or None.
+
+    Loading it needs no GPU; running it does.
+    """
+    global _ref_cuda
+    with _lock:
+        if _ref_cuda is None:
+            path = _build.build_ref_cuda()
+            if path is None or not path.exists():
+                return None
+            R = ctypes.CDLL(str(path))
+            R.ref_povs_shapes.argtypes = [_P, ctypes.c_int32]
+            R.ref_povs_shapes.restype = ctypes.c_int
+            R.ref_povs_layout_check.argtypes = [ctypes.c_int32]
+            R.ref_povs_layout_check.restype = ctypes.c_int
+            R.ref_povs_layout_check_small_rows.argtypes = []
+            R.ref_povs_layout_check_small_rows.restype = ctypes.c_int
+            R.ref_povs_cuda.argtypes = [ctypes.c_int32, _P, ctypes.c_int64, _P, ctypes.c_int64, ctypes.c_int32,
+                                        ctypes.c_int32, ctypes.c_int32]
+            R.ref_povs_cuda.restype = ctypes.c_int
+            R.ref_povs_kernel.argtypes = [ctypes.c_int32, _P, ctypes.c_int64, _P, _P, ctypes.c_int64, _P]
+            R.ref_povs_kernel.restype = ctypes.c_int
+            _ref_cuda = R
+        return _ref_cuda
+
+
+def ref_cuda_shapes() -> list[dict]:
+    """Shapes the reference-built CUDA library instantiates: V, P, instance size, element bytes, block size."""
+    R = ref_cuda_lib()
+    if R is None:
+        return []
+    out = np.zeros(5 * 64, dtype=np.int32)
+    n = R.ref_povs_shapes(out.ctypes.data, 64)
+    keys = ("V", "P", "inst", "elem_bytes", "block")
+    return [dict(zip(keys, (int(x) for x in out[5 * i:5 * i + 5])), index=i,
+                 row_bytes=int(out[5 * i + 2] * out[5 * i + 3])) for i in range(n)]
+
+
+def ref_cuda_shape(V: int, P: int, row_bytes: int) -> int | None:
+    for sh in ref_cuda_shapes():
+        if (sh["V"], sh["P"], sh["row_bytes"]) == (V, P, row_bytes):
+            return sh["index"]
+    return None
+
+
+def ref_povs_cuda(shape: int, data_ptr: int, n_rows: int, offsets: list[int], iterations: int, seed: int,
+                  device: int = 0) -> None:
+    """The reference's CUDA host loop and kernel (povs.cu:356-467) on a device deck; synchronizes."""
+    offs = np.array(offsets, dtype=np.int64)
+    rc = ref_cuda_lib().ref_povs_cuda(shape, data_ptr, n_rows, offs.ctypes.data, len(offs), iterations, int(seed),
+                                      device)
+    if rc != 0:
+        raise RuntimeError(f"ref_povs_cuda failed ({rc})")
+
+
+def ref_povs_kernel(shape: int, data_ptr: int, n_rows: int, assign_ptr: int, seeds_ptr: int, offset: int,
+                    stream: int = 0) -> None:
+    """One launch of the reference kernel (povs.cu:116-349) with device assignments and seeds."""
+    rc = ref_cuda_lib().ref_povs_kernel(shape, data_ptr, n_rows, assign_ptr, seeds_ptr, int(offset), stream or None)
+    if rc != 0:
+        raise RuntimeError(f"ref_povs_kernel failed ({rc})")
 
 
 def _ptr(a: np.ndarray) -> int:
@@ -164,6 +231,18 @@ def refcuda_randomness(seed: int, n_rows: int, pblock: int, vblock: int, offsets
     if rc != 0:
         raise ValueError(f"oracle_refcuda_randomness failed ({rc})")
     return out_off, out_assign, out_perms
+
+
+def refcuda_perms(n_rows: int, pblock: int, vblock: int, assign: np.ndarray, seeds: np.ndarray) -> np.ndarray:
+    """The reference kernel's Stage 0 + Stage 2 for given members [n_v,V] and seeds [n_v]: perms [n_v,V*P]."""
+    n_p, n_v = block_counts(n_rows, pblock, vblock)
+    a = np.ascontiguousarray(assign, dtype=np.int64).reshape(n_v, vblock)
+    s = np.ascontiguousarray(seeds, dtype=np.int32).reshape(n_v)
+    out = np.zeros((n_v, vblock * pblock), dtype=np.int32)
+    rc = lib().oracle_refcuda_perms(n_rows, pblock, vblock, _ptr(a), _ptr(s), _ptr(out))
+    if rc != 0:
+        raise ValueError(f"oracle_refcuda_perms failed ({rc})")
+    return out
 
 
 def ref_assign_sequence(seed: int, n_rows: int, pblock: int, vblock: int, n_offsets: int,

@@ -515,7 +515,10 @@ int shuffle_on_device(void* data, int64_t n_rows, int64_t row_bytes, const int64
     // 64-256 MiB decks against one graph per call).  Smaller decks, whose iterations take a few
     // microseconds, replay a cached graph to keep the host's launch cost off the GPU's timeline.
     // Routes whose stream holds copies or event waits before the first iteration (host decks) pass
-    // chain_first = false: their first launch keeps ordinary stream order.
+    // chain_first = false: their first launch keeps ordinary stream order.  So does a batch with a
+    // device seed array: the permuter warps read it before they wait for the prior grid, and the
+    // caller may have written it with the kernel just before this call.
+    if (deck_seeds != nullptr) chain_first = false;
     const int64_t deck_bytes = n_rows * row_bytes * std::max<int64_t>(1, n_decks);
     const bool direct = iterations == 1 || (flags & POVS_FLAG_NO_GRAPH) || (pdl && deck_bytes >= GRAPH_MAX_BYTES);
     if (direct) {
@@ -889,6 +892,8 @@ extern "C" int povs_apply_static_v1(void* data, int64_t n_rows, int64_t row_byte
                                     uint32_t flags)
 {
     g_err[0] = '\0';
+    if (flags & ~POVS_FLAG_SYNC)
+        return fail(POVS_ERR_INVALID_ARGUMENT, "povs_apply_static_v1 accepts only POVS_FLAG_SYNC (flags 0x%x)", flags);
     int r = check_common(data, n_rows, row_bytes, pblock, vblock, iterations);
     if (r != POVS_OK) return r;
     if (iterations > 0 && (offsets_per_iter == nullptr || assign_host == nullptr || perms_host == nullptr))

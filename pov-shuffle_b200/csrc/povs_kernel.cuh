@@ -19,8 +19,9 @@
 //   * Mover warps own a ring of NST shared-memory data stages.  Unit u is issued
 //     by mover u % n_movers: it waits for its permutation slot and for every
 //     mover to have read the stage's previous unit (mbarrier `empty`), then
-//     starts cp.async.bulk copies (TMA, non-multicast, local HBM only) of the
-//     <= 2 wrapped runs per member into the stage, completing on `full`.
+//     starts cp.async.bulk copies (non-multicast; from local HBM, or from a peer
+//     GPU's shard in the sharded in-place order) of the <= 2 wrapped runs per
+//     member into the stage, completing on `full`.
 //     Every mover then takes its share of every unit: it waits for `full` and
 //     writes its destination rows from shared memory with 16-byte vector stores
 //     (lanes cover consecutive bytes of consecutive destination rows, so each

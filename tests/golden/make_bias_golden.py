@@ -17,7 +17,7 @@ shuffled deck is the episode.  Statistics (positional TVD, bigram TVD) for:
 
 Pass ``--reuse`` to keep the ``reference_numpy`` statistics already in the file (they take minutes).
 
-Usage: python tests/golden/make_bias_golden.py [reference_root] [episodes]
+Usage: python tests/golden/make_bias_golden.py <reference_root> [episodes] [--reuse]
 """
 
 from __future__ import annotations
@@ -86,7 +86,7 @@ def oracle_episodes(n_episodes: int, kind: str, mode: str = "uniform") -> np.nda
     return out
 
 
-def main(reference_root: str = "/root/reference", n_episodes: int = 3000, reuse: bool = False) -> None:
+def main(reference_root: str, n_episodes: int = 3000, reuse: bool = False) -> None:
     sys.path.insert(0, str(REPO))
     from oracle import metrics
 
@@ -130,4 +130,6 @@ def main(reference_root: str = "/root/reference", n_episodes: int = 3000, reuse:
 if __name__ == "__main__":
     flags = [a for a in sys.argv[1:] if a.startswith("--")]
     args = [a for a in sys.argv[1:] if not a.startswith("--")]
-    main(args[0] if args else "/root/reference", int(args[1]) if len(args) > 1 else 3000, reuse="--reuse" in flags)
+    if not args:
+        sys.exit(__doc__.strip().splitlines()[-1])
+    main(args[0], int(args[1]) if len(args) > 1 else 3000, reuse="--reuse" in flags)

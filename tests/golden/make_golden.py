@@ -10,7 +10,7 @@ For P = 8 the reference's ``MIN_PBLOCK_SIZE`` (16) is lowered for the call; the 
 validator reads that module global (src/povs/common.py:90).  Seeds whose draw makes the
 reference lose rows (a pblock written from a misaligned chunk, numpy.py:133-136) are skipped.
 
-Usage: python tests/golden/make_golden.py [reference_root]
+Usage: python tests/golden/make_golden.py <reference_root>   (the checkout holding src/povs)
 """
 
 from __future__ import annotations
@@ -45,7 +45,7 @@ def make_deck(n_rows: int, shape: tuple[int, ...], dtype: str, input_seed: int) 
     return (rng.standard_normal((n_rows, *shape)) * 100).astype(dtype)
 
 
-def main(reference_root: str = "/root/reference") -> None:
+def main(reference_root: str) -> None:
     sys.path.insert(0, str(REPO))
     sys.path.insert(0, str(Path(reference_root) / "src"))
     import povs as ref_povs  # the reference package
@@ -93,4 +93,6 @@ def main(reference_root: str = "/root/reference") -> None:
 
 
 if __name__ == "__main__":
-    main(*sys.argv[1:])
+    if len(sys.argv) != 2:
+        sys.exit(__doc__.strip().splitlines()[-1])
+    main(sys.argv[1])

@@ -6,7 +6,7 @@ for them: ``get_tvd`` and ``get_ngram_tvd`` for n = 2, 3, 4 and skip = 0, 1, 2
 (src/povs/eval/metrics.py, imported from the reference checkout; it needs only NumPy).  Every
 case stays below the reference's 512 MiB key budget, so no anchor subsampling is involved.
 
-Usage: python tests/golden/make_metrics_golden.py [reference_root]
+Usage: python tests/golden/make_metrics_golden.py <reference_root>   (the checkout holding src/povs)
 """
 
 from __future__ import annotations
@@ -36,7 +36,9 @@ def episodes_for(case: int, deck: int, n_ep: int) -> np.ndarray:
 
 
 def main() -> None:
-    root = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit(__doc__.strip().splitlines()[-1])
+    root = Path(sys.argv[1])
     spec = importlib.util.spec_from_file_location("ref_metrics", root / "src/povs/eval/metrics.py")
     ref = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(ref)

@@ -128,6 +128,11 @@ def test_added_entry_points_reject_invalid_arguments_before_any_device_call():
     assert lib.povs_ngram_keys_v1(data, 8, 10, 10, 10, 1, 1, 1, None, 0, counts, 0, None) == -1
     assert b"degree" in lib.povs_last_error_string()
     assert lib.povs_ngram_keys_v1(data, 8, 0, 10, 10, 1, 3, 1, None, 0, counts, 0, None) == -1
+    # Allocation-free injection: only POVS_FLAG_SYNC is accepted.
+    host = ctypes.c_void_p(64)
+    for flags in (_native.FLAG_NO_GRAPH, _native.FLAG_REFERENCE_RNG, 8, 1 << 20):
+        assert lib.povs_apply_static_v1(data, 64, 4, 16, 2, 1, offs, host, host, 1, 0, None, flags) == -1
+        assert b"POVS_FLAG_SYNC" in lib.povs_last_error_string()
 
 
 def test_unsupported_container_raises_type_error():

@@ -53,6 +53,32 @@ def test_batch_equals_one_deck_at_a_time(n_decks, n_rows, row_bytes, P, V, offse
     assert torch.equal(decks, single)
 
 
+@pytest.mark.parametrize("n_rows,row_bytes", [(1000, 64), (200_000, 256)])
+def test_batch_reads_seeds_written_by_the_kernel_just_before(n_rows, row_bytes):
+    """The seed array is written on the stream by the kernel right before the batched call (one
+    iteration, the launch shape that could be chained to that kernel): every deck gets the new seeds."""
+    from povs import _native
+
+    n_decks, P, V, offsets = 6, 16, 2, [0, 1, 2, 3]
+    decks = _bytes_deck(n_decks, n_rows, row_bytes, seed=n_rows)
+    single = decks.clone()
+    want_seeds = [90_001 + 31 * d for d in range(n_decks)]
+    seeds = torch.zeros(n_decks, dtype=torch.int64, device=DEV)
+    increment = torch.tensor(want_seeds, dtype=torch.int64).to(DEV)
+    torch.cuda.synchronize()
+    # Long kernels first, then the kernel that writes the seeds, then the batched call.
+    spin = torch.ones(1 << 26, dtype=torch.float32, device=DEV)
+    for _ in range(4):
+        spin.mul_(1.0001)
+    seeds.add_(increment)
+    _native.shuffle_batch(decks, row_bytes, offsets, 1, P, V, seeds)
+    for d in range(n_decks):
+        _native.shuffle_device(single[d], row_bytes, offsets, 1, P, V, want_seeds[d])
+    torch.cuda.synchronize()
+    povs.check_device_status(0)
+    assert torch.equal(decks, single)
+
+
 def test_batch_matches_oracle(oracle_api):
     n_decks, n_rows, row_bytes, P, V, offsets, iterations = 4, 3001, 32, 16, 4, [0, 1, 2, 7], 3
     decks = _bytes_deck(n_decks, n_rows, row_bytes, seed=3)

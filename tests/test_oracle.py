@@ -119,3 +119,20 @@ def test_numpy_replay_padding_before_member_is_identity():
     """V = 2 with the padding id first: the reference leaves that member's rows untouched."""
     src = numpy_path._effective_vblock_perm([10**6, 3], n_rows=64, pblock=16, p=np.arange(16)[::-1].copy())
     assert np.array_equal(src, np.arange(16))
+
+
+def test_reference_cuda_library_shapes_stay_in_bounds(oracle_api):
+    """The reference's CUDA path compiled into oracle/_ref (no GPU needed to load it or run the host
+    check): every instantiated shape's Stage 1 copy partition stays inside the pblock, while the
+    options the reference's chooser picks for 32-byte float rows on a B200 do not."""
+    lib = oracle_api.ref_cuda_lib()
+    if lib is None:
+        pytest.skip("oracle/_ref/libref_povs_cuda.so is not built (needs the reference checkout)")
+    shapes = oracle_api.ref_cuda_shapes()
+    assert len(shapes) >= 8
+    assert {(s["V"], s["P"], s["row_bytes"]) for s in shapes} >= {(2, 64, 256), (4, 32, 256), (4, 64, 128)}
+    for s in shapes:
+        assert lib.ref_povs_layout_check(s["index"]) == 0, s
+        assert s["inst"] % s["block"] == 0
+    assert lib.ref_povs_layout_check_small_rows() != 0
+    assert lib.ref_povs_layout_check(len(shapes)) == -1

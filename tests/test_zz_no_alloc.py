@@ -76,3 +76,23 @@ def test_static_entry_rejects_decks_beyond_its_scratch():
                                   None, 0)
     assert rc == -2
     assert b"scratch" in lib.povs_last_error_string()
+
+
+def test_static_entry_reports_a_bad_injected_entry_only_when_synchronous():
+    """An out-of-range permutation entry is ignored by the kernel (identity used) and flagged in the
+    entry's own status word, which POVS_FLAG_SYNC reads back as POVS_ERR_DEVICE_STATUS."""
+    lib = _native.load()
+    n_rows, row_bytes, P, V = 256, 16, 16, 2
+    n_p = n_rows // P
+    n_v = n_p // V
+    deck = _deck(n_rows, row_bytes, 13)
+    assign = np.arange(n_v * V, dtype=np.int64)
+    perms = np.tile(np.arange(V * P, dtype=np.int32), n_v)
+    perms[5] = V * P + 3  # outside the vblock's rows
+    offs = (ctypes.c_int64 * 1)(0)
+    args = (ctypes.c_void_p(deck.data_ptr()), n_rows, row_bytes, P, V, 1, offs, ctypes.c_void_p(assign.ctypes.data),
+            ctypes.c_void_p(perms.ctypes.data), 1, 0, None)
+    assert lib.povs_apply_static_v1(*args, _native.FLAG_SYNC) == -4
+    assert b"device status" in lib.povs_last_error_string()
+    perms[5] = 5
+    assert lib.povs_apply_static_v1(*args, _native.FLAG_SYNC) == 0
