@@ -18,7 +18,10 @@ shards, one per GPU, and shuffled as one deck (povs.ShardedDeck: member rows mov
 the total work is fixed, so the scaling is strong.
 
 ``--impl reference`` times the CPU implementation of the same path (the oracle's C restatement,
-all host threads) on a bounded sample of the workload and prints the same JSON line.
+all host threads) on a bounded sample of the workload and prints the same JSON line.  Its line also
+carries ``reference_cuda_path``: the reference's own CUDA path (src/povs/__cuda/lib/povs.cu, its
+host loop and kernel, compiled into oracle/_ref) timed on this GPU on the full workload deck, when
+the reference instantiates that shape.
 """
 
 from __future__ import annotations
@@ -41,7 +44,10 @@ for _p in (REPO, REPO / "pov-shuffle_b200"):
 
 METRIC = "effective shuffle GB/s (2×bytes×iters/time), % HBM peak, 1/2/4/8×B200"
 FALLBACK_HBM_GBS = 6650.0
-NVLINK_PEER_GBS = 770.0  # measured peer copy per direction per GPU (B200, NVLink 5 through NVSwitch)
+# NVLink 5 per direction per GPU (18 links through NVSwitch): the denominator of the sharded mode's
+# roofline.  The bandwidth a peer copy reaches in the same run is measured and reported beside it.
+NVLINK_NOMINAL_GBS = 900.0
+DTYPE_NAMES = {"bfloat16": "bf16", "float16": "fp16", "float32": "fp32", "uint8": "u8"}
 
 WORKLOADS = {
     "bf16_32GiB": dict(
@@ -243,6 +249,7 @@ def run_ours(args, w: dict, wname: str) -> None:
     value = alg_bytes_per_step / (ms_per_step / 1e3) / 1e9
     per_launch_s = (ms / 1e3) / (args.steps * iters)
     peak, peak_kind = measured_peaks()
+    peer_copy = None
     if world == 1:
         bound, achieved, roof_peak, roof_kind = "hbm", 2 * deck_bytes / per_launch_s / 1e9, peak, peak_kind
     else:
@@ -251,8 +258,9 @@ def run_ours(args, w: dict, wname: str) -> None:
         # every remote member row is read and written back, twice that.
         crossings = 1 if args.sharded_order == "push" else 2
         link_bytes = crossings * (world - 1) / world * (deck_bytes / world)
-        bound, achieved, roof_peak, roof_kind = "nvlink", link_bytes / per_launch_s / 1e9, NVLINK_PEER_GBS, (
-            "measured peer copy per direction per GPU")
+        bound, achieved, roof_peak, roof_kind = "nvlink", link_bytes / per_launch_s / 1e9, NVLINK_NOMINAL_GBS, (
+            "nominal NVLink 5 bandwidth per direction per GPU")
+        peer_copy = measure_peer_copy(device, rank, world, local, dist)
 
     # End to end: the same work with the deck in pinned host memory, copies inside the timed region.
     e2e = None
@@ -263,6 +271,7 @@ def run_ours(args, w: dict, wname: str) -> None:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(w, threads=1, target_s=args.cpu_seconds)
+        cpu["reference_povs_shuffle"] = reference_cpu_path(wname)
 
     if rank == 0:
         line = {
@@ -276,7 +285,7 @@ def run_ours(args, w: dict, wname: str) -> None:
             "higher_is_better": True,
             "scaling": "strong",
             "vs_baseline": None,
-            "dtype": "u8",
+            "dtype": DTYPE_NAMES[w["dtype"]],
             "data": "synthetic",
             "config": {
                 "workload": w["desc"],
@@ -304,6 +313,9 @@ def run_ours(args, w: dict, wname: str) -> None:
                 "traffic": traffic_per_launch("povs_iteration_kernel", wname) if world == 1 and not (args.rows or args.vblock or args.pblock) else None,
                 "alg_bytes_per_launch": 2 * deck_bytes // world,
                 "hbm_frac_per_gpu": round(2 * deck_bytes / world / per_launch_s / 1e9 / peak, 4),
+                **({"peer_copy_gbs_measured": peer_copy,
+                    "frac_of_measured_peer_copy": round(achieved / peer_copy, 4) if peer_copy else None}
+                   if world > 1 else {}),
             },
             "gpu_launches": args.steps * iters if world == 1 else args.steps * (2 * iters + 1),
             "clocks": clocks,
@@ -314,6 +326,37 @@ def run_ours(args, w: dict, wname: str) -> None:
     if world > 1:
         sharded.close()
         dist.destroy_process_group()
+
+
+def measure_peer_copy(device, rank: int, world: int, local: int, dist, nbytes: int = 1 << 30, reps: int = 5) -> float:
+    """GB/s per direction per GPU of a ring exchange (every rank sends 1 GiB to the next rank and
+    receives 1 GiB from the previous one at the same time), after the timed region; max time over ranks."""
+    import torch
+
+    send = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    recv = torch.empty_like(send)
+    nxt, prv = (rank + 1) % world, (rank - 1) % world
+
+    def exchange() -> None:
+        reqs = dist.batch_isend_irecv([dist.P2POp(dist.isend, send, nxt), dist.P2POp(dist.irecv, recv, prv)])
+        for r in reqs:
+            r.wait()
+
+    exchange()
+    torch.cuda.synchronize(device)
+    dist.barrier(device_ids=[local])
+    stream = torch.cuda.current_stream(device)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(reps):
+        exchange()
+    stop.record(stream)
+    torch.cuda.synchronize(device)
+    t = torch.tensor([start.elapsed_time(stop)], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    del send, recv
+    torch.cuda.empty_cache()
+    return round(nbytes * reps / (float(t.item()) / 1e3) / 1e9, 1)
 
 
 def run_e2e(args, w, deck, opts, offsets, iters, world, rank, local, stream, sharded, dist) -> dict | None:
@@ -444,6 +487,99 @@ def cpu_baseline(w: dict, threads: int, target_s: float) -> dict:
     return out
 
 
+REFERENCE_CPU_UNAVAILABLE = (
+    "the reference's Python package is not on this host: its setup.py imports cutlass_library at "
+    "line 9, which this image lacks, so it cannot be installed, and its sources do not ship with "
+    "this repository"
+)
+
+
+def reference_cpu_path(wname: str) -> dict:
+    """The reference's own povs.shuffle on a NumPy deck: unavailable here; the figure recorded where
+    the reference checkout is (tests/golden/reference_cpu_timing.json) is reported with its machine."""
+    out = {"value": None, "unit": "GB/s", "unavailable": REFERENCE_CPU_UNAVAILABLE}
+    fixture = REPO / "tests" / "golden" / "reference_cpu_timing.json"
+    if fixture.exists():
+        rec = json.loads(fixture.read_text())
+        sample = rec.get("samples", {}).get(wname)
+        if sample:
+            out["recorded_elsewhere"] = dict(sample, cores=rec.get("cores_used"), host_cpus=rec.get("host_cpus"),
+                                             cpu_model=rec.get("cpu_model"),
+                                             where="the build machine (no GPU), not this host")
+    return out
+
+
+def reference_cuda_path(w: dict, wname: str, steps: int) -> dict:
+    """The reference's own CUDA path on this GPU over the full workload deck (oracle/_ref):
+    ``path`` = whole povs_cuda calls (its host randomness, blocking copies and kernels; wall clock);
+    ``kernel`` = its kernel alone with device-resident assignments and seeds (CUDA events)."""
+    import torch
+
+    from oracle import api as oracle
+    from povs.common import choose_offsets
+
+    if not torch.cuda.is_available():
+        return {"value": None, "unavailable": "no GPU"}
+    if oracle.ref_cuda_lib() is None:
+        return {"value": None, "unavailable": "oracle/_ref/libref_povs_cuda.so is not built"}
+    R = row_bytes_of(w)
+    elem = ELEM_BYTES[w["dtype"]]
+    N, P, V, iters = w["rows"], w["P"], w["V"], w["iterations"]
+    shape = oracle.ref_cuda_shape(V, P, R)
+    if shape is None:
+        smem = V * P * R
+        return {"value": None, "unavailable": (
+            f"the reference kernel stages a whole vblock ({smem:,} B) in static shared memory (48 KB limit, "
+            "src/povs/__cuda/lib/povs.cu:167): no instantiation exists for this shape")}
+    info = next(sh for sh in oracle.ref_cuda_shapes() if sh["index"] == shape)
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    deck = make_deck(w, device)
+    ptr = deck.data_ptr()
+    offsets = choose_offsets(N, R // elem, elem, P)
+    alg = 2 * N * R * iters
+    oracle.ref_povs_cuda(shape, ptr, N, offsets, iters, 1)  # warm-up (module load, first allocations)
+    t0 = time.perf_counter()
+    for k in range(steps):
+        oracle.ref_povs_cuda(shape, ptr, N, offsets, iters, 2 + k)
+    t_path = (time.perf_counter() - t0) / steps
+    # Kernel alone: one launch per iteration, device-resident randomness of the reference's form.
+    n_p = -(-N // P)
+    n_v = -(-n_p // V)
+    g = torch.Generator(device=device).manual_seed(5)
+    slots = torch.randperm(n_v * V, generator=g, device=device)
+    assign = torch.where(slots < n_p, slots, torch.full_like(slots, -1)).to(torch.int64)
+    seeds = torch.randint(1, 1000, (n_v,), generator=g, device=device, dtype=torch.int32)
+    legacy = torch.cuda.default_stream(device)
+    for it in range(iters):
+        oracle.ref_povs_kernel(shape, ptr, N, assign.data_ptr(), seeds.data_ptr(), offsets[it % len(offsets)])
+    torch.cuda.synchronize(device)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(legacy)
+    for k in range(steps):
+        for it in range(iters):
+            oracle.ref_povs_kernel(shape, ptr, N, assign.data_ptr(), seeds.data_ptr(), offsets[it % len(offsets)])
+    stop.record(legacy)
+    torch.cuda.synchronize(device)
+    t_kernel = start.elapsed_time(stop) / 1e3 / steps
+    peak, peak_kind = measured_peaks()
+    del deck, assign, seeds, slots
+    torch.cuda.empty_cache()
+    return {
+        "value": round(alg / t_path / 1e9, 3),
+        "unit": "GB/s",
+        "what": "the reference's povs_cuda (src/povs/__cuda/lib/povs.cu:356-467) on the full deck, per call of "
+        f"{iters} iterations, wall clock",
+        "kernel": {"value": round(alg / t_kernel / 1e9, 1), "unit": "GB/s",
+                   "frac_of_hbm": round(alg / t_kernel / 1e9 / peak, 4), "peak": peak, "peak_kind": peak_kind,
+                   "ms_per_launch": round(t_kernel * 1e3 / iters, 3)},
+        "ms_per_call": round(t_path * 1e3, 2),
+        "instantiation": {k: info[k] for k in ("V", "P", "inst", "elem_bytes", "block")},
+        "steps": steps,
+        "deck": w["desc"],
+    }
+
+
 def run_reference(args, w: dict, wname: str) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -457,6 +593,11 @@ def run_reference(args, w: dict, wname: str) -> None:
             vals.append(cb["value"])
     value = statistics.median(vals) if vals else cb["value"]
     cb = dict(cb, value=round(value, 3))
+    cb["reference_povs_shuffle"] = reference_cpu_path(wname)
+    try:
+        ref_gpu = reference_cuda_path(w, wname, steps=3)
+    except Exception as exc:  # reported, not fatal: the CPU arm above is the line's value
+        ref_gpu = {"value": None, "unavailable": f"{type(exc).__name__}: {exc}"}
     line = {
         "metric": METRIC,
         "impl": "reference",
@@ -468,13 +609,16 @@ def run_reference(args, w: dict, wname: str) -> None:
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
-        "dtype": "u8",
+        "dtype": DTYPE_NAMES[w["dtype"]],
         "data": "synthetic",
         "config": {"workload": w["desc"], "name": wname},
         "cpu_baseline": cb,
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": "CPU implementation of the path on the host cores: the oracle's C restatement of the POV iteration "
-        "(the reference's own CPU path is Python/NumPy and is not available on this machine)",
+        "reference_cuda_path": ref_gpu,
+        "note": "value: the CPU implementation of the path on this host's cores, the oracle's C restatement of the "
+        "POV iteration on all threads (the reference's own CPU path is Python/NumPy and cannot be installed here: "
+        "see cpu_baseline.reference_povs_shuffle); reference_cuda_path: the reference's own CUDA path compiled "
+        "from its sources, timed on this GPU",
     }
     print(json.dumps(line), flush=True)
 

@@ -368,6 +368,47 @@ def test_full_size_cfg3_keeps_every_row():
     assert moved > 0.99
 
 
+def _matches_host_rows(deck: torch.Tensor, want: np.ndarray, chunk_rows: int) -> bool:
+    """Compare a device deck with host rows chunk by chunk on the GPU (no second host copy)."""
+    rows = deck.view(torch.uint8).reshape(deck.shape[0], -1)
+    for s in range(0, rows.shape[0], chunk_rows):
+        if not torch.equal(rows[s:s + chunk_rows], torch.from_numpy(want[s:s + chunk_rows]).to(DEV)):
+            return False
+    return True
+
+
+@pytest.mark.parametrize(
+    "name,n_rows,elems,dtype,P,V,iterations,seed",
+    [
+        ("bf16 32 GiB", 134_217_728, 128, torch.bfloat16, 32, 4, 4, 1),
+        ("uint8 12,288 B rows", 1_000_000, 12_288, torch.uint8, 16, 2, 3, 2),
+    ],
+)
+def test_full_size_decks_match_oracle_byte_for_byte(oracle_api, name, n_rows, elems, dtype, P, V, iterations, seed):
+    """The two largest single-GPU decks at full size, byte for byte against the oracle run on every
+    host core: 134,217,728 x 128 bf16 (32 GiB, uniform [-1, 1) from seed 1, V=4, P=32, 4 iterations)
+    and 1,000,000 x 3x64x64 uint8 (12.3 GB, column slabs, V=2, P=16, 3 iterations).  The host holds
+    one copy of the deck, shuffled by the oracle in place; the GPU result is compared chunk by chunk."""
+    import os
+
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    if dtype == torch.uint8:
+        deck = torch.randint(0, 256, (n_rows, elems), generator=g, device=DEV, dtype=torch.uint8)
+    else:
+        deck = torch.rand((n_rows, elems), generator=g, device=DEV, dtype=dtype) * 2 - 1
+    elem_bytes = deck.element_size()
+    row_bytes = elems * elem_bytes
+    want = deck.view(torch.uint8).reshape(n_rows, row_bytes).cpu().numpy()
+    offsets = povs.common.choose_offsets(n_rows, elems, elem_bytes, P)
+    povs.shuffle(deck, iterations=iterations, options=povs.Options(V, P, offsets, min(64, V * P)), seed=seed)
+    torch.cuda.synchronize()
+    povs.check_device_status(0)
+    oracle_api.shuffle_threads(want, iterations, P, V, offsets, seed, os.cpu_count() or 1)
+    assert _matches_host_rows(deck, want, max(1, (1 << 30) // row_bytes)), f"{name}: differs from the oracle"
+    del deck
+    torch.cuda.empty_cache()
+
+
 @pytest.mark.parametrize(
     "rows,row_bytes,P,V,offsets,iterations",
     [
