@@ -623,6 +623,57 @@ def run_reference(args, w: dict, wname: str) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_one_process_shards(args, w: dict, wname: str) -> None:
+    """Profiling mode (not the benchmark line): the workload deck split into K equal shards on GPUs
+    0..K-1 of this one process and shuffled by povs.shuffle_shards in the double-buffered push order.
+    One kernel per iteration on GPU 0 moves every pblock: it reads the rows of the K-1 remote shards
+    over NVLink (bulk copies, no multicast) and stores the rows whose destination slot is remote
+    over NVLink, so per iteration (K-1)/K of the deck enters GPU 0 over NVLink and as much leaves it."""
+    import torch
+
+    import povs
+    from povs.common import choose_offsets
+
+    K = args.shards_on_gpus
+    assert torch.cuda.device_count() >= K, f"needs {K} GPUs"
+    R = row_bytes_of(w)
+    N, P, V, iters = w["rows"], w["P"], w["V"], w["iterations"]
+    elem = ELEM_BYTES[w["dtype"]]
+    offsets = choose_offsets(N, R // elem, elem, P)
+    opts = povs.Options(virtual_block_size=V, physical_block_size=P, offsets=offsets,
+                        gpu_thread_block_size=min(64, V * P))
+    rows = [N // K] * K
+    rows[-1] += N - sum(rows)
+    shards = [make_deck(w, torch.device("cuda", i), rows=rows[i], seed_offset=i) for i in range(K)]
+    scratch = [torch.empty_like(s) for s in shards]
+    dev0 = torch.device("cuda", 0)
+    for s in range(args.warmup):
+        povs.shuffle_shards(shards, iterations=iters, options=opts, seed=1000 + s, scratch=scratch)
+    for i in range(K):
+        torch.cuda.synchronize(i)
+    stream = torch.cuda.current_stream(dev0)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for s in range(args.steps):
+        povs.shuffle_shards(shards, iterations=iters, options=opts, seed=s, scratch=scratch)
+    stop.record(stream)
+    torch.cuda.synchronize(dev0)
+    povs.check_device_status(0)
+    ms = start.elapsed_time(stop)
+    deck_bytes = N * R
+    per_launch_s = ms / 1e3 / (args.steps * iters)
+    link = (K - 1) / K * deck_bytes
+    print(json.dumps({
+        "mode": f"one process, deck split over GPUs 0..{K - 1}, double-buffered push order, kernels on GPU 0",
+        "workload": w["desc"], "shard_rows": rows,
+        "value": round(2 * deck_bytes / per_launch_s / 1e9, 1), "unit": "GB/s",
+        "ms_per_launch": round(per_launch_s * 1e3, 3),
+        "nvlink_rx_bytes_per_launch": int(link), "nvlink_tx_bytes_per_launch": int(link),
+        "nvlink_gbs_per_direction": round(link / per_launch_s / 1e9, 1),
+        "frac_of_nominal_nvlink": round(link / per_launch_s / 1e9 / NVLINK_NOMINAL_GBS, 4),
+    }), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -639,6 +690,8 @@ def main() -> None:
     ap.add_argument("--rows", type=int, default=None, help="override the workload's row count (profiling captures)")
     ap.add_argument("--vblock", type=int, default=None, help="override the workload's V (profiling captures)")
     ap.add_argument("--pblock", type=int, default=None, help="override the workload's P (profiling captures)")
+    ap.add_argument("--shards-on-gpus", type=int, default=None,
+                    help="profiling mode: split the deck over this many GPUs of one process (povs.shuffle_shards)")
     args = ap.parse_args()
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
@@ -652,6 +705,8 @@ def main() -> None:
             w[key] = val
     if args.impl == "reference":
         run_reference(args, w, args.workload)
+    elif args.shards_on_gpus:
+        run_one_process_shards(args, w, args.workload)
     else:
         run_ours(args, w, args.workload)
 

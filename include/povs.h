@@ -186,6 +186,13 @@ int povs_shuffle_sharded_v1(void* const* shard_ptrs, void* const* scratch_ptrs, 
  */
 int povs_set_peer_wait_limit_v1(uint64_t limit_ns);
 
+/*
+ * Let kernels on `device` read and write `peer`'s memory (cudaDeviceEnablePeerAccess; enabling it
+ * twice is not an error).  Needed before povs_shuffle_shards_v1 gets shards on other GPUs of the
+ * node.  No reference counterpart (the reference is single-GPU).
+ */
+int povs_enable_peer_access_v1(int32_t device, int32_t peer);
+
 /* CUDA IPC of device memory between the processes of a sharded deck (64-byte handles). */
 int povs_ipc_export_v1(const void* ptr, int32_t device, void* handle_out, int64_t* offset_out);
 int povs_ipc_import_v1(const void* handle, int64_t offset, int32_t device, void** ptr_out, void** base_out);
@@ -218,10 +225,18 @@ int povs_set_tuning_v1(int32_t stage_cap, int32_t n_stages, int32_t movers, int3
                        int32_t copy_bytes);
 
 /*
+ * Advanced: largest packed unit, in bytes (process-wide; no reference counterpart).  Vblocks of
+ * device-randomness in-place shuffles whose V*P rows are small travel several per unit (up to 32 / V
+ * vblocks, 1024 rows and this many bytes per unit), so that per-unit costs are paid once for all of
+ * them; the result is the same.  0 turns packing off; the default is 16384.
+ */
+int povs_set_pack_bytes_v1(int32_t pack_bytes);
+
+/*
  * Advanced: report the launch plan povs_shuffle_v1 would use, as int64 values
  * {grid, block, dynamic smem, sort elements per lane, bulk (0/1), slab bytes, slabs,
  *  stages per CTA, stage bytes, vector bytes, vblocks, SM count, rows per bulk copy,
- *  permutation slots, mover warps, permuter warps}; returns how many were written.
+ *  permutation slots, mover warps, permuter warps, vblocks per unit}; returns how many were written.
  */
 int povs_describe_plan_v1(void* data, int64_t n_rows, int64_t row_bytes, int32_t pblock, int32_t vblock,
                           int32_t device, int64_t* out, int32_t n_out);

@@ -81,9 +81,24 @@ KernelFn kernel_for(int epl, bool bulk, bool ring)
     return ring ? kernel_for_epl<INJ, true, PUSH, true>(epl) : kernel_for_epl<INJ, true, PUSH, false>(epl);
 }
 
-// Push mode exists for device randomness only.  Plain-load kernels always carry ring positions.
-KernelFn select_kernel(int epl, bool injected, bool bulk, bool push = false, bool ring = false)
+// Packed units (device randomness, in place, ring positions): 2 to 32 sort elements per lane.
+template <bool BULK>
+KernelFn packed_kernel_for_epl(int epl)
 {
+    switch (epl) {
+    case 2: return povs::povs_iteration_kernel<2, false, BULK, false, true, true>;
+    case 4: return povs::povs_iteration_kernel<4, false, BULK, false, true, true>;
+    case 8: return povs::povs_iteration_kernel<8, false, BULK, false, true, true>;
+    case 16: return povs::povs_iteration_kernel<16, false, BULK, false, true, true>;
+    case 32: return povs::povs_iteration_kernel<32, false, BULK, false, true, true>;
+    default: return nullptr;
+    }
+}
+
+// Push mode exists for device randomness only.  Plain-load kernels always carry ring positions.
+KernelFn select_kernel(int epl, bool injected, bool bulk, bool push = false, bool ring = false, bool packed = false)
+{
+    if (packed) return bulk ? packed_kernel_for_epl<true>(epl) : packed_kernel_for_epl<false>(epl);
     if (push) return kernel_for<false, true>(epl, bulk, ring);
     if (injected) return kernel_for<true, false>(epl, bulk, ring);
     return kernel_for<false, false>(epl, bulk, ring);
@@ -107,6 +122,7 @@ struct Tuning {
     int permuters = 4;         // warps that compute members and permutations
     int force_plain = 0;       // 1 = never use TMA bulk loads
     int copy_bytes = 8192;     // target bytes per bulk copy on the whole-row path
+    int pack_bytes = 16 * 1024; // packed units: several small vblocks per unit up to this size (0 = off)
 };
 Tuning g_tuning;
 std::mutex g_tuning_mu;
@@ -191,6 +207,13 @@ int set_smem_attr_all(int smem)
                                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
                     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
                 }
+    for (int bulk = 0; bulk < 2; ++bulk)
+        for (int epl = 2; epl <= 32; epl <<= 1) {
+            KernelFn fn = select_kernel(epl, false, bulk != 0, false, true, true);
+            cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+        }
     return POVS_OK;
 }
 
@@ -231,6 +254,7 @@ struct Plan {
     KernelFn fn = nullptr;
     int grid = 0, block = 0, smem = 0, epl = 0;
     bool bulk = false;
+    int pack = 1;
 };
 
 int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out, bool push = false,
@@ -245,8 +269,23 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out, boo
     if (vp > POVS_MAX_VP)
         return fail(POVS_ERR_UNSUPPORTED, "virtual_block_size * physical_block_size = %lld exceeds %d",
                     static_cast<long long>(vp), POVS_MAX_VP);
+    // Packed units: small vblocks (device randomness, in place over the whole list of vblocks)
+    // travel `pack` at a time, so the per-unit costs (barrier round trips, member ranks, the sort
+    // network, copy issue) are paid once per pack * V * P rows.  One member per lane (pack * V <= 32),
+    // one sort of pack * V * P <= 1024 keys, at least 2 keys per lane, unit bytes <= pack_bytes.
+    int pack = 1;
+    if (!injected && !push && p.vb_begin == 0 && p.vb_step == 1 && t.pack_bytes > 0 && vp >= 8) {
+        while (2 * pack * p.vblock <= 32 && 2 * pack * vp <= POVS_MAX_VP &&
+               2 * pack * vp * p.row_bytes <= t.pack_bytes && pack < p.n_vblocks)
+            pack *= 2;
+        if (pack * vp < 64) pack = 1;
+    }
+    const int64_t unit_vp = pack * vp;
     int epl = 1;
-    while (32 * epl < vp) epl <<= 1;
+    while (32 * epl < unit_vp) epl <<= 1;
+    p.pack = pack;
+    p.unit_vp = static_cast<int32_t>(unit_vp);
+    p.groups_per_deck = (p.n_vblocks + pack - 1) / pack;
 
     uintptr_t addr = 0;
     for (int i = 0; i < p.n_shards; ++i) addr |= reinterpret_cast<uintptr_t>(p.shard_base[i]);
@@ -258,11 +297,17 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out, boo
     const bool bulk = (vec == 16) && !t.force_plain && !plain_loads;
 
     // Slab width: whole rows when a vblock fits a stage, else the widest 128-byte (or vec) multiple that does.
-    // A stage holds a unit's rows: the vblock's V*P rows in place, one member's P rows in push mode.
-    const int64_t stage_rows = push ? p.pblock : vp;
-    const int max_stages = std::max(2, std::min(t.n_stages, povs::MAX_STAGES));
-    const int movers = std::max(1, std::min(t.movers, 15));
-    const int permuters = std::max(1, std::min(t.permuters, 16 - movers));
+    // A stage holds a unit's rows: the vblock's V*P rows in place (pack of them when packed), one
+    // member's P rows in push mode.
+    const int64_t stage_rows = push ? p.pblock : unit_vp;
+    // Packed units run best as several small CTAs per SM, each its own pipeline (measured on B200,
+    // 2 GiB decks of 16- to 256-byte rows): at most 4 stages with TMA loads; with plain loads, whose
+    // issuing warp waits for its loads, 2 mover and 2 permuter warps and at most 3 stages.
+    const int stage_limit = pack == 1 ? t.n_stages : std::min(t.n_stages, bulk ? 4 : 3);
+    const int max_stages = std::max(2, std::min(stage_limit, povs::MAX_STAGES));
+    const int movers = std::max(1, std::min(pack > 1 && !bulk ? std::min(t.movers, 2) : t.movers, 15));
+    const int permuters =
+        std::max(1, std::min(pack > 1 && !bulk ? std::min(t.permuters, 2) : t.permuters, 16 - movers));
     // Permutation slots: the stages' worth plus room for every permuter to work ahead.
     auto slots_for = [&](int stages) { return std::min(povs::MAX_SLOTS, stages + 2 * permuters); };
     int64_t slab = p.row_bytes;
@@ -275,14 +320,14 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out, boo
         const int64_t wide = std::min<int64_t>(p.row_bytes, ((SLAB_FLOOR_BYTES / vec) * vec));
         if (slab < wide) {
             const int64_t wide_stage = ((stage_rows * wide + 127) / 128) * 128;
-            const int64_t fixed = povs::cta_smem_bytes(0, 0, slots_for(3), static_cast<int>(vp), p.pblock);
+            const int64_t fixed = povs::cta_smem_bytes(0, 0, slots_for(3), static_cast<int>(unit_vp), p.pblock);
             if (fixed + 3 * (wide_stage + 16) <= c.smem_optin) slab = wide;
         }
     }
     auto stages_for = [&](int64_t sl, int64_t& stage_bytes) {
         stage_bytes = ((stage_rows * sl + 127) / 128) * 128;
         const int kp = slots_for(max_stages);
-        const int64_t fixed = povs::cta_smem_bytes(0, 0, kp, static_cast<int>(vp), p.pblock);
+        const int64_t fixed = povs::cta_smem_bytes(0, 0, kp, static_cast<int>(unit_vp), p.pblock);
         const int64_t per_stage = stage_bytes + 16;
         return static_cast<int>(std::min<int64_t>(max_stages, (c.smem_optin - fixed) / per_stage));
     };
@@ -298,14 +343,16 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out, boo
     const int kp = slots_for(nst);
 
     const int warps = movers + permuters;
-    const int cta_smem = povs::cta_smem_bytes(nst, static_cast<int>(stage_bytes), kp, static_cast<int>(vp), p.pblock);
+    const int cta_smem =
+        povs::cta_smem_bytes(nst, static_cast<int>(stage_bytes), kp, static_cast<int>(unit_vp), p.pblock);
     const int per_sm_by_smem = std::max(1, c.smem_per_sm / (cta_smem + 1024));
     const int per_sm_by_threads = std::max(1, c.max_threads_per_sm / (warps * 32));
     const int ctas_per_sm = std::min(per_sm_by_smem, per_sm_by_threads);
     const int64_t n_mine = push ? (p.push_rank < 0 ? p.n_pblocks : p.n_pblocks / std::max(1, p.n_shards) + 1)
-                                : (p.vb_begin < p.n_vblocks * p.n_decks
-                                       ? (p.n_vblocks * p.n_decks - p.vb_begin + p.vb_step - 1) / p.vb_step
-                                       : 0);
+                           : pack > 1 ? p.groups_per_deck * p.n_decks
+                                      : (p.vb_begin < p.n_vblocks * p.n_decks
+                                             ? (p.n_vblocks * p.n_decks - p.vb_begin + p.vb_step - 1) / p.vb_step
+                                             : 0);
     const int grid = static_cast<int>(std::min<int64_t>(std::max<int64_t>(1, n_mine), static_cast<int64_t>(c.sm_count) * ctas_per_sm));
 
     p.slab_bytes = static_cast<int32_t>(slab);
@@ -318,12 +365,13 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out, boo
     p.n_movers = movers;
     p.n_permuters = permuters;
 
-    out.fn = select_kernel(epl, injected, bulk, push, stage_bytes <= RING_STAGE_BYTES);
+    out.fn = select_kernel(epl, injected, bulk, push, stage_bytes <= RING_STAGE_BYTES || pack > 1, pack > 1);
     out.grid = std::max(1, grid);
     out.block = warps * 32;
     out.smem = cta_smem;
     out.epl = epl;
     out.bulk = bulk;
+    out.pack = pack;
     return POVS_OK;
 }
 
@@ -362,6 +410,12 @@ void fill_geometry(IterParams& p, void* data, int64_t n_rows, int64_t row_bytes,
     p.vp = pblock * vblock;
     p.n_pblocks = (n_rows + pblock - 1) / pblock;
     p.n_vblocks = (p.n_pblocks + vblock - 1) / vblock;
+    p.pack = 1;
+    p.unit_vp = p.vp;
+    p.vp_shift = ilog2(p.vp);
+    p.vblock_shift = ilog2(vblock);
+    p.idx_bits = std::max(5, ilog2(p.vp));
+    p.groups_per_deck = p.n_vblocks;
     p.status = status;
     p.n_shards = 1;
     p.shard_base[0] = p.data;
@@ -798,6 +852,15 @@ extern "C" int povs_set_tuning_v1(int32_t stage_cap, int32_t n_stages, int32_t m
     return POVS_OK;
 }
 
+extern "C" int povs_set_pack_bytes_v1(int32_t pack_bytes)
+{
+    g_err[0] = '\0';
+    if (pack_bytes < 0) return fail(POVS_ERR_INVALID_ARGUMENT, "pack_bytes (%d) must be non-negative", pack_bytes);
+    std::lock_guard<std::mutex> lk(g_tuning_mu);
+    g_tuning.pack_bytes = pack_bytes;
+    return POVS_OK;
+}
+
 extern "C" int povs_describe_plan_v1(void* data, int64_t n_rows, int64_t row_bytes, int32_t pblock, int32_t vblock,
                                      int32_t device, int64_t* out, int32_t n_out)
 {
@@ -818,7 +881,7 @@ extern "C" int povs_describe_plan_v1(void* data, int64_t n_rows, int64_t row_byt
     const int64_t vals[] = {pl.grid,      pl.block,       pl.smem,        pl.epl,      pl.bulk ? 1 : 0,
                             p.slab_bytes, p.n_slabs,      p.n_stages,     p.stage_bytes, p.vec_bytes,
                             p.n_vblocks,  c->sm_count,    p.copy_rows,    p.n_slots,     p.n_movers,
-                            p.n_permuters};
+                            p.n_permuters, pl.pack};
     const int n = std::min<int>(n_out, static_cast<int>(sizeof(vals) / sizeof(vals[0])));
     for (int i = 0; i < n; ++i) out[i] = vals[i];
     return n;
@@ -1205,6 +1268,25 @@ extern "C" int povs_ipc_close_v1(void* base, int32_t device)
     int r = dg.enter(device);
     if (r != POVS_OK) return r;
     POVS_CUDA_TRY(cudaIpcCloseMemHandle(base));
+    return POVS_OK;
+}
+
+extern "C" int povs_enable_peer_access_v1(int32_t device, int32_t peer)
+{
+    g_err[0] = '\0';
+    if (device == peer) return POVS_OK;
+    int can = 0;
+    POVS_CUDA_TRY(cudaDeviceCanAccessPeer(&can, device, peer));
+    if (!can) return fail(POVS_ERR_UNSUPPORTED, "device %d cannot access device %d's memory", device, peer);
+    DeviceGuard dg;
+    int r = dg.enter(device);
+    if (r != POVS_OK) return r;
+    const cudaError_t e = cudaDeviceEnablePeerAccess(peer, 0);
+    if (e == cudaErrorPeerAccessAlreadyEnabled) {
+        cudaGetLastError(); // clear the recorded error so that a later cudaGetLastError does not report it
+        return POVS_OK;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceEnablePeerAccess");
     return POVS_OK;
 }
 

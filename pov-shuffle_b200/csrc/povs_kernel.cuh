@@ -49,6 +49,7 @@ constexpr int MAX_STAGES = 16;
 constexpr int MAX_SLOTS = 32;
 constexpr int MAX_SHARDS = 8;
 constexpr unsigned FULL_MASK = 0xffffffffu;
+constexpr uint16_t HOLE = 0xFFFFu; // packed units: a destination slot past its vblock's valid rows
 
 // Device status bits (sticky, OR-ed into the per-device status word).
 enum : int {
@@ -107,6 +108,15 @@ struct IterParams {
     int64_t n_decks;
     int64_t deck_stride;
     const uint64_t* deck_seeds;
+    // Packed units (small vblocks): a unit is `pack` consecutive vblocks of one deck (pack == 1: one
+    // vblock, or one column slab of it).  Unit slot f = s * vp + (slot of the s-th vblock), so the
+    // unit has unit_vp = pack * vp slots; slots past a vblock's valid rows are holes.
+    int32_t pack;
+    int32_t unit_vp;
+    int32_t vp_shift;        // log2(vp)
+    int32_t vblock_shift;    // log2(V)
+    int32_t idx_bits;        // index bits of a vblock's permutation sort keys: max(5, log2(vp))
+    int64_t groups_per_deck; // ceil(n_vblocks / pack)
     int64_t offsets[MAX_INLINE_OFFSETS];
 };
 
@@ -268,6 +278,51 @@ __device__ __forceinline__ void warp_bitonic_sort(T (&x)[EPL], int lane)
     }
 }
 
+// Same network restricted to its phases k = 2 .. seg (seg a power of two, 2 <= seg <= 32 * EPL),
+// the last of them ascending everywhere: every aligned block of seg elements ends sorted ascending
+// on its own (elements of different blocks are never compared).  With seg = 32 * EPL it is
+// warp_bitonic_sort.  Packed units sort the keys of several vblocks at once this way.
+template <int EPL, typename T>
+__device__ __forceinline__ void warp_bitonic_sort_blocks(T (&x)[EPL], int lane, int seg)
+{
+    const int base = lane * EPL;
+#pragma unroll
+    for (int k = 2; k <= EPL; k <<= 1) {
+        if (k <= seg) {
+#pragma unroll
+            for (int j = k >> 1; j > 0; j >>= 1) {
+#pragma unroll
+                for (int r = 0; r < EPL; ++r) {
+                    if ((r & j) == 0) {
+                        const bool up = (k == seg) || (((base + r) & k) == 0);
+                        cx_regs<EPL, T>(x, r, j, up);
+                    }
+                }
+            }
+        }
+    }
+#pragma unroll 1
+    for (int k = 2 * EPL; k <= seg; k <<= 1) {
+        const bool up = (k == seg) || ((base & k) == 0);
+#pragma unroll 1
+        for (int j = k >> 1; j >= EPL; j >>= 1) {
+            const bool keep_min = ((base & j) == 0) == up;
+            const int lm = j / EPL;
+#pragma unroll
+            for (int r = 0; r < EPL; ++r) {
+                const T y = __shfl_xor_sync(FULL_MASK, x[r], lm);
+                x[r] = keep_min ? min(x[r], y) : max(x[r], y);
+            }
+        }
+#pragma unroll
+        for (int j = EPL >> 1; j > 0; j >>= 1) {
+#pragma unroll
+            for (int r = 0; r < EPL; ++r)
+                if ((r & j) == 0) cx_regs<EPL, T>(x, r, j, up);
+        }
+    }
+}
+
 // Sort keys of a vblock's elements e = 0 .. 32*EPL-1: the element's 32-bit Philox word with its
 // low IDX_BITS bits replaced by e (so keys are distinct and the sort is a permutation).  Elements
 // past n_valid get all high bits set: they sort after every valid element (same high bits: the
@@ -360,6 +415,7 @@ struct StageMeta {
     uintptr_t run_a[MAX_VBLOCK];
     uintptr_t run_b[MAX_VBLOCK];
     int32_t n_a[MAX_VBLOCK]; // rows of the member stored contiguously from run_a
+    int16_t mrows[MAX_VBLOCK]; // packed units: rows of every ordered member (0 = padding or no vblock)
     int32_t n_valid;         // valid rows (slots) of the unit
     int32_t rows_mine;       // push mode: rows of the unit's own member
     // push mode: the unit's own member in the source buffer, same (a, b, n_a) convention
@@ -397,8 +453,8 @@ __device__ __forceinline__ CtaSmem carve_smem(uint8_t* base, const IterParams& p
     s.data = base;
     uint8_t* q = base + static_cast<size_t>(p.n_stages) * p.stage_bytes;
     s.perm = reinterpret_cast<uint16_t*>(q);
-    s.perm_stride = perm_bytes_per_slot(p.vp) / 2;
-    q += static_cast<size_t>(p.n_slots) * perm_bytes_per_slot(p.vp);
+    s.perm_stride = perm_bytes_per_slot(p.unit_vp) / 2;
+    q += static_cast<size_t>(p.n_slots) * perm_bytes_per_slot(p.unit_vp);
     s.pos = reinterpret_cast<uint16_t*>(q);
     s.pos_stride = perm_bytes_per_slot(p.pblock) / 2;
     q += static_cast<size_t>(p.n_slots) * perm_bytes_per_slot(p.pblock);
@@ -488,20 +544,26 @@ __device__ __forceinline__ LaneGeom lane_geom(int slen, int lane)
 
 // Identity-order copy global -> stage by one warp (plain loads): the unit's valid rows (in place),
 // or the rows of the unit's own member (push).  Several loads per lane are in flight.
-template <int W, bool PUSH>
+template <int W, bool PUSH, bool PACK = false>
 __device__ __forceinline__ void lsu_load_unit(const IterParams& p, const StageMeta& m, uint8_t* stage, int64_t col,
                                               int slen, int lane)
 {
     using T = typename VecOf<W>::T;
     const LaneGeom lg = lane_geom<W>(slen, lane);
     const int pmask = p.pblock - 1;
-    const int n = PUSH ? m.rows_mine : m.n_valid;
+    // Packed units: every slot of the unit, skipping the holes (rows past a member's row count).
+    const int n = PACK ? p.unit_vp : (PUSH ? m.rows_mine : m.n_valid);
+    auto live = [&](int f) -> bool {
+        if constexpr (PACK) return (f & pmask) < m.mrows[f >> p.pblock_shift];
+        else return true;
+    };
     auto src_of = [&](int f) -> const uint8_t* {
         if constexpr (PUSH) return src_row_ptr(m, f, p.row_bytes) + col;
         else return slot_ptr(m, f, p.pblock_shift, pmask, p.row_bytes) + col;
     };
     if (lg.cpr >= 32) {
         for (int f = 0; f < n; ++f) {
+            if (!live(f)) continue;
             const T* src = reinterpret_cast<const T*>(src_of(f));
             T* dst = reinterpret_cast<T*>(stage + static_cast<size_t>(f) * p.slab_bytes);
             for (int q = lane; q < lg.cpr; q += 32) dst[q] = src[q];
@@ -513,12 +575,12 @@ __device__ __forceinline__ void lsu_load_unit(const IterParams& p, const StageMe
 #pragma unroll
             for (int u = 0; u < UL; ++u) {
                 const int f = f0 + u * lg.g;
-                if (f < n) v[u] = reinterpret_cast<const T*>(src_of(f))[lg.lq];
+                if (f < n && live(f)) v[u] = reinterpret_cast<const T*>(src_of(f))[lg.lq];
             }
 #pragma unroll
             for (int u = 0; u < UL; ++u) {
                 const int f = f0 + u * lg.g;
-                if (f < n) reinterpret_cast<T*>(stage + static_cast<size_t>(f) * p.slab_bytes)[lg.lq] = v[u];
+                if (f < n && live(f)) reinterpret_cast<T*>(stage + static_cast<size_t>(f) * p.slab_bytes)[lg.lq] = v[u];
             }
         }
     }
@@ -589,7 +651,7 @@ __device__ __forceinline__ void store_share_div(const IterParams& p, const Stage
 // This warp's share of the copy stage -> global.  In place: destination slot f receives stage row
 // idx[f] (idx = the permutation).  Push: stage row f (the unit's own member) goes to destination
 // slot idx[f] (idx = the member's destination slots).  Work items are interleaved over the warps.
-template <int W, bool PUSH>
+template <int W, bool PUSH, bool PACK = false>
 __device__ __forceinline__ void store_share(const IterParams& p, const StageMeta& m, const uint8_t* stage,
                                             const uint16_t* idx, int64_t col, int slen, int lane, int warp,
                                             int n_warps)
@@ -598,7 +660,8 @@ __device__ __forceinline__ void store_share(const IterParams& p, const StageMeta
     const LaneGeom lg = lane_geom<W>(slen, lane);
     const int cpr = lg.cpr;
     const int pmask = p.pblock - 1;
-    const int n = PUSH ? m.rows_mine : m.n_valid;
+    // Packed units: every slot of the unit; holes (idx == HOLE) are skipped.
+    const int n = PACK ? p.unit_vp : (PUSH ? m.rows_mine : m.n_valid);
     auto src_row = [&](int f) -> int {
         if constexpr (PUSH) return f;
         else return idx[f];
@@ -609,6 +672,7 @@ __device__ __forceinline__ void store_share(const IterParams& p, const StageMeta
     };
     if (cpr >= 32) {
         for (int f = warp; f < n; f += n_warps) {
+            if (PACK && idx[f] == HOLE) continue;
             const T* src = reinterpret_cast<const T*>(stage + static_cast<size_t>(src_row(f)) * p.slab_bytes);
             T* dst = reinterpret_cast<T*>(slot_ptr(m, dst_slot(f), p.pblock_shift, pmask, p.row_bytes) + col);
 #pragma unroll 4
@@ -627,10 +691,16 @@ __device__ __forceinline__ void store_share(const IterParams& p, const StageMeta
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const int f = (t + u * n_warps) * g + lrow;
+                int src = 0, slot = 0;
                 ok[u] = f < n;
-                const int fs = ok[u] ? f : 0;
-                dst[u] = reinterpret_cast<T*>(slot_ptr(m, dst_slot(fs), p.pblock_shift, pmask, p.row_bytes) + col) + lq;
-                v[u] = reinterpret_cast<const T*>(stage + static_cast<size_t>(src_row(fs)) * p.slab_bytes)[lq];
+                if (ok[u]) {
+                    src = src_row(f);
+                    slot = dst_slot(f);
+                    if constexpr (PACK) ok[u] = src != HOLE;
+                }
+                if (!ok[u]) src = slot = 0;
+                dst[u] = reinterpret_cast<T*>(slot_ptr(m, slot, p.pblock_shift, pmask, p.row_bytes) + col) + lq;
+                v[u] = reinterpret_cast<const T*>(stage + static_cast<size_t>(src) * p.slab_bytes)[lq];
             }
 #pragma unroll
             for (int u = 0; u < U; ++u)
@@ -639,7 +709,9 @@ __device__ __forceinline__ void store_share(const IterParams& p, const StageMeta
         for (; t < n_pass; t += n_warps) {
             const int f = t * g + lrow;
             if (f < n) {
-                const T v = reinterpret_cast<const T*>(stage + static_cast<size_t>(src_row(f)) * p.slab_bytes)[lq];
+                const int src = src_row(f);
+                if (PACK && src == HOLE) continue;
+                const T v = reinterpret_cast<const T*>(stage + static_cast<size_t>(src) * p.slab_bytes)[lq];
                 reinterpret_cast<T*>(slot_ptr(m, dst_slot(f), p.pblock_shift, pmask, p.row_bytes) + col)[lq] = v;
             }
         }
@@ -665,7 +737,7 @@ __device__ __forceinline__ void warp_make_pos(const IterParams& p, uint64_t seed
 
 // ---------------------------------------------------------------------------------------------
 // The iteration kernel.
-// EPL: elements per lane of the permutation sort (32 * EPL >= V * P).
+// EPL: elements per lane of the permutation sort (32 * EPL >= V * P; packed: = pack * V * P).
 // INJECTED: members, permutation and offset come from the caller instead of the device RNG.
 // BULK: rows are 16-byte multiples on a 16-byte aligned deck -> TMA bulk loads.
 //
@@ -737,15 +809,123 @@ __device__ __forceinline__ RingPos ring_at(uint64_t u, uint32_t n)
     return RingPos{static_cast<uint32_t>(u % n), static_cast<uint32_t>((u / n) & 1u)};
 }
 
+// ---------------------------------------------------------------------------------------------
+// Packed units: the permuter warp's work for `n_seg` (<= pack) consecutive vblocks v0 .. v0+n_seg-1
+// of one deck, written to permutation slot `slot`.  Lane l computes member (l mod V) of vblock
+// v0 + l / V (pack * V <= 32), ranks it inside its vblock and records its storage run at ordered
+// member index (l / V) * V + rank.  The permutation is every vblock's own, unchanged: the same sort
+// keys as a vblock processed alone (same Philox words, same index bits), sorted in aligned blocks
+// of vp elements by one warp; destination slots past a vblock's valid rows get HOLE.
+// ---------------------------------------------------------------------------------------------
+
+template <int EPL, typename PI>
+__device__ __forceinline__ void make_packed_unit(const IterParams& p, StageMeta& m, uint16_t* perm, int64_t v0,
+                                                 int n_seg, uint64_t seed, int64_t deck_offset, uintptr_t deck_shift,
+                                                 const PI& pi, bool ref_rng, int lane)
+{
+    const int vshift = p.vblock_shift;
+    const int seg = lane >> vshift;          // this lane's vblock within the unit
+    const int j = lane & (p.vblock - 1);     // this lane's member within its vblock
+    int64_t mem = -1;
+    if (seg < n_seg) {
+        const int64_t slot = (v0 + seg) * p.vblock + j;
+        const int64_t a = (ref_rng && slot >= p.n_pblocks) ? -1 : static_cast<int64_t>(pi(static_cast<uint64_t>(slot)));
+        mem = (a >= 0 && a < p.n_pblocks) ? a : -1;
+    }
+    const bool valid = mem >= 0;
+    int rows = 0;
+    if (valid) {
+        const int64_t left = p.n_rows - mem * p.pblock;
+        rows = left < p.pblock ? static_cast<int>(left) : p.pblock;
+    }
+    // Ascending member ids with padding last (the reference kernel's order, povs.cu:203-221).
+    const uint64_t key = valid ? static_cast<uint64_t>(mem) : ((uint64_t{1} << 63) | static_cast<uint64_t>(j));
+    const int grp = seg << vshift;
+    int rank = 0;
+    for (int t = 0; t < p.vblock; ++t) {
+        const uint64_t k2 = __shfl_sync(FULL_MASK, key, grp + t);
+        rank += (k2 < key || (k2 == key && t < j)) ? 1 : 0;
+    }
+    int nv = rows; // valid rows of this lane's vblock (sum over its V lanes)
+    for (int o = p.vblock >> 1; o > 0; o >>= 1) nv += __shfl_xor_sync(FULL_MASK, nv, o);
+    const int total = __reduce_add_sync(FULL_MASK, rows);
+    const int mi = grp + rank; // ordered member index within the unit
+    m.mrows[mi] = static_cast<int16_t>(rows);
+    if (valid) {
+        int64_t s0 = mem * p.pblock + deck_offset;
+        if (s0 >= p.n_rows) s0 -= p.n_rows;
+        locate_run(p, p.shard_base, s0, rows, m.run_a[mi], m.run_b[mi], m.n_a[mi]);
+        m.run_a[mi] += deck_shift;
+        m.run_b[mi] += deck_shift;
+    }
+    if (lane == 0) m.n_valid = total;
+    // Lane s (< pack) holds the valid rows of vblock s.
+    const int pack_last = p.pack - 1;
+    const int nv_lane = __shfl_sync(FULL_MASK, nv, min(lane, pack_last) << vshift);
+    const int vpm = p.vp - 1;
+    if (ref_rng) {
+        // The reference kernel's xorshift32 Fisher-Yates, one vblock per lane (povs.cu:282-321).
+        for (int f = lane; f < p.unit_vp; f += 32) {
+            const int nvf = __shfl_sync(FULL_MASK, nv_lane, f >> p.vp_shift);
+            perm[f] = (f & vpm) < nvf ? static_cast<uint16_t>(f) : HOLE;
+        }
+        __syncwarp();
+        if (lane < n_seg) {
+            uint16_t* pv = perm + (lane << p.vp_shift);
+            uint32_t r = vblock_seed(seed, p.iteration, static_cast<uint64_t>(v0 + lane));
+            const int last = nv_lane - 1;
+            for (int i = 0; i <= last; ++i) {
+                r ^= r << 13;
+                r ^= r >> 17;
+                r ^= r << 5;
+                const int jj = i + static_cast<int>((static_cast<uint64_t>(r) * static_cast<uint64_t>(last - i + 1)) >> 32);
+                const uint16_t t = pv[i];
+                pv[i] = pv[jj];
+                pv[jj] = t;
+            }
+        }
+        __syncwarp();
+        return;
+    }
+    const uint32_t M = (1u << p.idx_bits) - 1u;
+    uint32_t x[EPL];
+    // Keys come in quads of Philox words (elements 4c .. 4c+3 of a vblock); vp >= 8, so a quad never
+    // straddles two vblocks.  With fewer than 4 keys per lane, the lane's keys share one quad.
+    constexpr int QPL = EPL >= 4 ? EPL / 4 : 1; // quads per lane
+#pragma unroll
+    for (int q = 0; q < QPL; ++q) {
+        const int e0g = lane * EPL + 4 * q;       // unit element of the lane's first key in the quad
+        const int sq = e0g >> p.vp_shift;         // its vblock within the unit
+        const int e0 = e0g & vpm;                 // its element index within the vblock
+        const int nvq = __shfl_sync(FULL_MASK, nv_lane, sq);
+        const U32x4 k = perm_key4(seed, p.iteration, static_cast<uint64_t>(v0 + sq), static_cast<uint32_t>(e0 >> 2));
+#pragma unroll
+        for (int t = 0; t < (EPL >= 4 ? 4 : EPL); ++t) {
+            const uint32_t e = static_cast<uint32_t>(e0 + t);
+            x[4 * q + t] = ((static_cast<int>(e) < nvq) ? (pick_word(k, static_cast<int>(e & 3u)) & ~M) : ~M) | e;
+        }
+    }
+    warp_bitonic_sort_blocks<EPL, uint32_t>(x, lane, p.vp);
+#pragma unroll
+    for (int r = 0; r < EPL; ++r) {
+        const int fg = lane * EPL + r;
+        const int sr = fg >> p.vp_shift;
+        const int nvr = __shfl_sync(FULL_MASK, nv_lane, sr);
+        perm[fg] = (fg & vpm) < nvr ? static_cast<uint16_t>((sr << p.vp_shift) + static_cast<int>(x[r] & M)) : HOLE;
+    }
+}
+
 // RING: the permuter and mover warps carry their units' stage / slot ring positions from unit to
 // unit (small units, where per-unit bookkeeping is a visible share of the work, and every
 // plain-load kernel); otherwise they recompute them per unit, which measured faster on large
 // bulk-loaded units.
-template <int EPL, bool INJECTED, bool BULK, bool PUSH, bool RING>
+// PACK: units are groups of `pack` small vblocks (device randomness, in place, whole rows).
+template <int EPL, bool INJECTED, bool BULK, bool PUSH, bool RING, bool PACK = false>
 __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_constant__ IterParams p)
 {
     static_assert(BULK || RING, "plain-load kernels carry ring positions");
     static_assert(!(PUSH && INJECTED), "push mode draws its randomness on the device");
+    static_assert(!PACK || (RING && !PUSH && !INJECTED), "packed units: device randomness, in place, ring positions");
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -782,6 +962,8 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
     if constexpr (PUSH) {
         plist = push_list(p, offset);
         n_list = plist.size();
+    } else if constexpr (PACK) {
+        n_list = p.groups_per_deck * p.n_decks;
     } else {
         const int64_t total = p.n_vblocks * p.n_decks;
         n_list = p.vb_begin < total ? (total - p.vb_begin + p.vb_step - 1) / p.vb_step : 0;
@@ -809,6 +991,34 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
         const uint32_t step_e = static_cast<uint32_t>(p.n_permuters / p.n_slabs);
         const uint32_t step_s = static_cast<uint32_t>(p.n_permuters % p.n_slabs);
         RingPos kr = ring_at(static_cast<uint64_t>(q), static_cast<uint32_t>(kp));
+        if constexpr (PACK) {
+            // Unit u = group u of this CTA's list (one slab): groups blockIdx.x + u * gridDim.x.
+            for (int64_t u = q; u < n_units; u += p.n_permuters) {
+                const int k = static_cast<int>(kr.i);
+                if (u >= kp && !warp_wait(&sm.pempty[k], kr.ph ^ 1u, p.status)) return;
+                for (int t = 0; t < p.n_permuters; ++t) kr.next(static_cast<uint32_t>(kp));
+                const int64_t group = blockIdx.x + u * static_cast<int64_t>(gridDim.x);
+                const int64_t d = p.n_decks > 1 ? group / p.groups_per_deck : 0;
+                const int64_t v0 = (group - d * p.groups_per_deck) * p.pack;
+                const int n_seg = static_cast<int>(min(static_cast<int64_t>(p.pack), p.n_vblocks - v0));
+                uintptr_t deck_shift = 0;
+                if (p.n_decks > 1) {
+                    if (d != deck) {
+                        deck = d;
+                        seed = p.deck_seeds[d];
+                        pi.init(seed, p.iteration, domain);
+                        deck_offset = p.offsets[reduce_range(offset_draw(seed, p.iteration),
+                                                             static_cast<uint32_t>(p.n_offsets))];
+                    }
+                    deck_shift = static_cast<uintptr_t>(d * p.deck_stride);
+                }
+                make_packed_unit<EPL>(p, sm.meta[k], sm.perm + static_cast<size_t>(k) * sm.perm_stride, v0, n_seg,
+                                      seed, deck_offset, deck_shift, pi, ref_rng, lane);
+                __syncwarp();
+                mbar_arrive(&sm.pfull[k]); // each lane publishes its writes to the slot
+            }
+            return;
+        }
         int64_t entry_local = q / p.n_slabs;
         uint32_t slab_q = static_cast<uint32_t>(q % p.n_slabs);
         for (int64_t u = q; u < n_units; u += p.n_permuters) {
@@ -1073,14 +1283,16 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
                 __syncwarp();
                 if (p.n_slabs == 1) {
                     // Whole rows: each member is <= 2 contiguous runs, copied in pieces of at most
-                    // copy_rows rows; pieces are spread over the lanes.
+                    // copy_rows rows; pieces are spread over the lanes.  Packed units: every member
+                    // slot of the unit, with its own row count (0 for padding).
                     const int ppm = (p.pblock + p.copy_rows - 1) / p.copy_rows;
-                    const int n_mem = PUSH ? 1 : (n_load + pmask) >> p.pblock_shift;
+                    const int n_mem = PACK ? (p.pack << p.vblock_shift)
+                                           : (PUSH ? 1 : (n_load + pmask) >> p.pblock_shift);
                     for (int q = lane; q < n_mem * ppm; q += 32) {
                         const int r = ppm == 1 ? q : q / ppm;
                         const int i0 = (q - r * ppm) * p.copy_rows;
                         const int first = r << p.pblock_shift;
-                        const int rows_r = min(p.pblock, n_load - first);
+                        const int rows_r = PACK ? static_cast<int>(m.mrows[r]) : min(p.pblock, n_load - first);
                         if (i0 >= rows_r) continue;
                         const int len = min(p.copy_rows, rows_r - i0);
                         const int na = PUSH ? m.src_na : m.n_a[r];
@@ -1106,11 +1318,11 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
                 }
             } else {
                 switch (p.vec_bytes) {
-                case 16: lsu_load_unit<16, PUSH>(p, m, stage, col, slen, lane); break;
-                case 8: lsu_load_unit<8, PUSH>(p, m, stage, col, slen, lane); break;
-                case 4: lsu_load_unit<4, PUSH>(p, m, stage, col, slen, lane); break;
-                case 2: lsu_load_unit<2, PUSH>(p, m, stage, col, slen, lane); break;
-                default: lsu_load_unit<1, PUSH>(p, m, stage, col, slen, lane); break;
+                case 16: lsu_load_unit<16, PUSH, PACK>(p, m, stage, col, slen, lane); break;
+                case 8: lsu_load_unit<8, PUSH, PACK>(p, m, stage, col, slen, lane); break;
+                case 4: lsu_load_unit<4, PUSH, PACK>(p, m, stage, col, slen, lane); break;
+                case 2: lsu_load_unit<2, PUSH, PACK>(p, m, stage, col, slen, lane); break;
+                default: lsu_load_unit<1, PUSH, PACK>(p, m, stage, col, slen, lane); break;
                 }
                 __syncwarp();
             }
@@ -1128,14 +1340,14 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
             const int64_t col = static_cast<int64_t>(slab) * p.slab_bytes;
             const int slen = static_cast<int>(min(static_cast<int64_t>(p.slab_bytes), p.row_bytes - col));
             if constexpr (BULK) {
-                store_share<16, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers);
+                store_share<16, PUSH, PACK>(p, m, stage, idx, col, slen, lane, mw, n_movers);
             } else {
                 switch (p.vec_bytes) {
-                case 16: store_share<16, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
-                case 8: store_share<8, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
-                case 4: store_share<4, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
-                case 2: store_share<2, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
-                default: store_share<1, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
+                case 16: store_share<16, PUSH, PACK>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
+                case 8: store_share<8, PUSH, PACK>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
+                case 4: store_share<4, PUSH, PACK>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
+                case 2: store_share<2, PUSH, PACK>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
+                default: store_share<1, PUSH, PACK>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;
                 }
             }
             mbar_arrive(&sm.empty[st]);  // this thread's reads of the data stage are done

@@ -47,6 +47,8 @@ SIGNATURES: dict[str, tuple] = {
     "povs_last_error_string": (ctypes.c_char_p, []),
     "povs_version": (ctypes.c_int32, []),
     "povs_set_tuning_v1": (ctypes.c_int, [_c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32]),
+    "povs_set_pack_bytes_v1": (ctypes.c_int, [_c_i32]),
+    "povs_enable_peer_access_v1": (ctypes.c_int, [_c_i32, _c_i32]),
     "povs_describe_plan_v1": (ctypes.c_int, [_c_vp, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _P_I64, _c_i32]),
     "povs_shuffle_shards_v1": (
         ctypes.c_int,
@@ -486,6 +488,16 @@ def set_tuning(
     )
 
 
+def enable_peer_access(device: int, peer: int) -> None:
+    """Let kernels on ``device`` access ``peer``'s memory (idempotent)."""
+    check(load().povs_enable_peer_access_v1(device, peer), "povs_enable_peer_access_v1")
+
+
+def set_pack_bytes(pack_bytes: int = 16 * 1024) -> None:
+    """Largest packed unit in bytes (0 = one vblock per unit); the default restores the built-in plan."""
+    check(load().povs_set_pack_bytes_v1(pack_bytes), "povs_set_pack_bytes_v1")
+
+
 PLAN_FIELDS = (
     "grid",
     "block",
@@ -503,6 +515,7 @@ PLAN_FIELDS = (
     "perm_slots",
     "movers",
     "permuters",
+    "vblocks_per_unit",
 )
 
 

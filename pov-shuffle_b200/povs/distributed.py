@@ -92,9 +92,10 @@ def shuffle_shards(
 ) -> None:
     """Shuffle, in place, the deck formed by concatenating ``shards`` along axis 0 (one process).
 
-    All shards must be contiguous, share the row layout and dtype, and be addressable from the
-    first shard's device (same device, or peers with peer access enabled).  ``scratch``: optional
-    buffers shaped like the shards, used for the double-buffered order (contents are overwritten).
+    All shards must be contiguous and share the row layout and dtype; shards on other GPUs of the
+    node are reached from the first shard's GPU over NVLink (peer access is enabled here).
+    ``scratch``: optional buffers shaped like the shards, used for the double-buffered order
+    (contents are overwritten).
     """
     assert shards, "at least one shard is required"
     layout = _row_layout(shards[0])
@@ -116,6 +117,11 @@ def shuffle_shards(
                 "scratch buffers must be contiguous CUDA tensors shaped like their shards"
     if row_bytes == 0:
         return
+    # Shards (and scratch buffers) on other GPUs of the node are reached over NVLink by the kernels
+    # running on the first shard's GPU.
+    for t in [*shards, *(scratch or [])]:
+        if t.device.index != dev.index:
+            _native.enable_peer_access(dev.index, t.device.index)
     _native.shuffle_shards(
         [s.data_ptr() for s in shards], rows, row_bytes, list(opts.offsets), iterations, opts.physical_block_size,
         opts.virtual_block_size, seed_to_u64(get_int_seed(seed)), dev.index, randomness_flags(opts),

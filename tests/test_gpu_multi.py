@@ -76,3 +76,27 @@ def test_sharded_deck_matches_oracle(oracle_api, tmp_path, randomness, double_bu
     oracle_api.shuffle(want, ITERATIONS, P, V, OFFSETS, SEED, randomness)
     oracle_api.shuffle(want, 2, P, V, OFFSETS, SEED + 1, randomness)
     assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("double_buffer", [False, True])
+def test_one_process_shards_on_two_gpus(oracle_api, double_buffer):
+    """One process, shards on GPUs 0 and 1 (and their scratch buffers): the kernels on GPU 0 reach GPU 1's
+    shard over NVLink; the result is the oracle's shuffle of the concatenated deck."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs at least two GPUs")
+    sys.path[:0] = [str(REPO), str(REPO / "pov-shuffle_b200")]
+    import povs
+
+    rows = _split(2)
+    host = _deck()
+    shards = [torch.from_numpy(host[:rows[0]].copy()).to("cuda:0"),
+              torch.from_numpy(host[rows[0]:].copy()).to("cuda:1")]
+    scratch = [torch.empty_like(s) for s in shards] if double_buffer else None
+    opts = povs.Options(V, P, OFFSETS, 64)
+    povs.shuffle_shards(shards, iterations=ITERATIONS, options=opts, seed=SEED, scratch=scratch)
+    torch.cuda.synchronize(0)
+    povs.check_device_status(0)
+    got = np.concatenate([s.cpu().numpy() for s in shards])
+    want = host.copy()
+    oracle_api.shuffle(want, ITERATIONS, P, V, OFFSETS, SEED)
+    assert np.array_equal(got, want)

@@ -78,6 +78,49 @@ def test_reference_cuda_randomness_mode_matches_oracle(oracle_api, n_rows, row_b
     assert np.array_equal(got, want)
 
 
+# (n_decks, n_rows, row_bytes, P, V, offsets, iterations): small vblocks that travel several per unit.
+PACKED_CASES = [
+    (1, 1000, 64, 8, 2, list(range(8)), 4),  # 63 vblocks: 16 per unit, the last unit has 15
+    (1, 20_011, 16, 16, 2, [0, 1, 3, 5], 3),  # truncated last pblock; bulk loads
+    (1, 30_000, 12, 16, 4, [0, 1, 2], 2),  # plain 4-byte loads
+    (1, 7_777, 3, 32, 2, [0, 1, 2], 3),  # byte rows
+    (1, 65_536, 256, 8, 2, [0, 1], 2),  # 4 KiB vblocks, 4 per unit
+    (1, 999, 32, 4, 8, [0, 1, 2, 3], 3),  # V = 8, 4 vblocks per unit
+    (37, 1000, 64, 8, 2, list(range(8)), 3),  # batched decks: units never straddle two decks
+]
+
+
+@pytest.mark.parametrize("n_decks,n_rows,row_bytes,P,V,offsets,iterations", PACKED_CASES)
+@pytest.mark.parametrize("randomness", ["uniform", "reference_cuda"])
+def test_packed_units_match_single_vblock_units_and_oracle(oracle_api, n_decks, n_rows, row_bytes, P, V, offsets,
+                                                          iterations, randomness):
+    """Small vblocks travel several per unit; the shuffle is the one-vblock-per-unit plan's and the oracle's."""
+    flags = _native.FLAG_REFERENCE_RNG if randomness == "reference_cuda" else 0
+    host = np.random.default_rng(n_rows + row_bytes).integers(0, 256, size=(n_decks, n_rows, row_bytes), dtype=np.uint8)
+    seeds = torch.arange(7, 7 + n_decks, dtype=torch.int64, device=DEV)
+    results = []
+    try:
+        for pack_bytes in (16 * 1024, 0):
+            _native.set_pack_bytes(pack_bytes)
+            decks = torch.from_numpy(host.copy()).to(DEV)
+            plan = _native.describe_plan(decks[0], row_bytes, P, V)
+            assert (plan["vblocks_per_unit"] > 1) == (pack_bytes > 0), plan
+            if n_decks == 1:
+                _native.shuffle_device(decks[0], row_bytes, offsets, iterations, P, V, 7, flags)
+            else:
+                _native.shuffle_batch(decks, row_bytes, offsets, iterations, P, V, seeds, flags)
+            torch.cuda.synchronize()
+            povs.check_device_status(0)
+            results.append(decks.cpu().numpy())
+    finally:
+        _native.set_pack_bytes(16 * 1024)
+    assert np.array_equal(results[0], results[1])
+    for d in range(n_decks):
+        want = host[d].copy()
+        oracle_api.shuffle(want, iterations, P, V, offsets, 7 + d, randomness)
+        assert np.array_equal(results[0][d], want), f"deck {d}"
+
+
 @pytest.mark.parametrize("row_bytes", [4, 64, 256])
 def test_b200_tuned_options_shuffle_like_the_oracle(oracle_api, row_bytes):
     """``tuning="b200"`` picks the pblock for this kernel; the shuffle is still the oracle's."""
