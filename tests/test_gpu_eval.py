@@ -196,3 +196,56 @@ def test_breaking_point_with_checkpoints(tmp_path):
         assert a.positional_breaking_point is None or 1 <= a.positional_breaking_point <= kw["default_max_iterations"]
     assert (tmp_path / "64" / "baseline" / "episodes.npy").exists()
     assert (tmp_path / "64" / "pov_1" / "metrics.json").exists()
+
+
+def test_shuffle_time_per_deck_size_report(monkeypatch, tmp_path):
+    """The timing exercise (reference eval/exercises.py:29-107) on a few deck sizes: one timing list per
+    deck size, the reference's timings.csv columns, and every timed deck still a permutation of its rows
+    (the exercise allocates zero decks, as the reference does; here they carry row ids)."""
+    import pandas as pd
+
+    from povs.eval import exercises
+
+    timed = []
+    real_shuffle = exercises.shuffle
+
+    def recording_shuffle(data, *args, **kwargs):
+        timed.append(data)
+        return real_shuffle(data, *args, **kwargs)
+
+    real_zeros = torch.zeros
+
+    def id_rows(*shape, dtype=None, device=None, **kw):
+        t = real_zeros(*shape, dtype=dtype, device=device, **kw)
+        if t.is_cuda and t.dim() == 2:
+            t.copy_(torch.arange(t.shape[0], device=t.device, dtype=torch.int64)[:, None].expand_as(t).to(t.dtype))
+        return t
+
+    monkeypatch.setattr(exercises, "shuffle", recording_shuffle)
+    monkeypatch.setattr(exercises.torch, "zeros", id_rows)
+    sizes = [1000, 4096, 65_536]
+    res = exercises.shuffle_time_per_deck_size(
+        deck_sizes=sizes, iterations=3, instance_size=16, num_runs=3, num_warmup_runs=1,
+        povs_options_per_deck_size={4096: povs.Options(virtual_block_size=4)}, default_options=None,
+        dtype=torch.int32, seed=11, tolerate_errors=False)
+    monkeypatch.undo()
+    assert [len(t) for t in res.pov_times_ms] == [3, 3, 3] and all(x > 0 for t in res.pov_times_ms for x in t)
+    assert [len(t) for t in res.baseline_times_ms] == [3, 3, 3]
+    assert res.option_sets[1].virtual_block_size == 4 and res.option_sets[0].virtual_block_size == 2
+    assert res.pov_errors == [None] * 3 and res.baseline_errors == [None] * 3
+    table = exercises.timings_table(sizes, res)
+    assert list(table.columns) == ["deck_size", "pov_mean_ms", "pov_std_ms", "baseline_mean_ms", "baseline_std_ms",
+                                   "speedup"]
+    table.to_csv(tmp_path / "timings.csv", index=False)
+    back = pd.read_csv(tmp_path / "timings.csv")
+    assert back["deck_size"].tolist() == sizes and (back["speedup"] > 0).all()
+    seen = {}
+    for d in timed:
+        seen[id(d)] = d
+    assert len(seen) == len(sizes)
+    torch.cuda.synchronize()
+    for d in seen.values():
+        ids = d[:, 0].to(torch.int64)
+        assert torch.equal(d.to(torch.int64), ids[:, None].expand_as(d)), "a row was torn"
+        assert torch.equal(torch.sort(ids).values, torch.arange(d.shape[0], device=d.device))
+        assert not torch.equal(ids, torch.arange(d.shape[0], device=d.device))
