@@ -13,6 +13,7 @@ Workloads (synthetic data with the shapes and value distributions of the named c
   fp16_256MiB  1,048,576 x 128 fp16 (256 MiB), standard normal from seed 0, 4 iterations, V=2, P=64
   u8_12KiB     1,000,000 x 3x64x64 uint8 (12.3 GB), uniform 0..255 from seed 2, 3 iterations, V=2, P=16
   f32_128GiB   1,073,741,824 x 32 fp32 (128 GiB), standard normal from seed 3, 4 iterations, V=4, P=64
+  i32x16_2GiB  33,554,432 x 16 int32 (2 GiB), the bias suite's 64-byte rows, V=2, P=8, 4 iterations
 With --gpus N > 1 (torchrun, one process per GPU) the workload's deck is split along axis 0 into N
 shards, one per GPU, and shuffled as one deck (povs.ShardedDeck: member rows move over NVLink):
 the total work is fixed, so the scaling is strong.
@@ -47,7 +48,7 @@ FALLBACK_HBM_GBS = 6650.0
 # NVLink 5 per direction per GPU (18 links through NVSwitch): the denominator of the sharded mode's
 # roofline.  The bandwidth a peer copy reaches in the same run is measured and reported beside it.
 NVLINK_NOMINAL_GBS = 900.0
-DTYPE_NAMES = {"bfloat16": "bf16", "float16": "fp16", "float32": "fp32", "uint8": "u8"}
+DTYPE_NAMES = {"bfloat16": "bf16", "float16": "fp16", "float32": "fp32", "uint8": "u8", "int32": "i32"}
 
 WORKLOADS = {
     "bf16_32GiB": dict(
@@ -62,6 +63,11 @@ WORKLOADS = {
         rows=1_073_741_824, shape=(32,), dtype="float32", iterations=4, V=4, P=64, seed=3, init="normal",
         desc="fp32 deck 1,073,741,824 x 32 (128 GiB), standard normal from seed 3, iterations=4, V=4, P=64",
     ),
+    "i32x16_2GiB": dict(
+        rows=33_554_432, shape=(16,), dtype="int32", iterations=4, V=2, P=8, seed=4, init="bytes",
+        desc="int32 deck 33,554,432 x 16 (64-byte rows and V=2, P=8 of the bias suite, 2 GiB), uniform bytes "
+        "from seed 4, iterations=4",
+    ),
     "u8_12KiB": dict(
         rows=1_000_000, shape=(3, 64, 64), dtype="uint8", iterations=3, V=2, P=16, seed=2, init="bytes",
         desc="uint8 deck 1,000,000 x 3x64x64 (12,288 B rows, 12.3 GB), uniform 0..255 from seed 2, iterations=3, V=2, P=16",
@@ -69,7 +75,7 @@ WORKLOADS = {
 }
 
 
-ELEM_BYTES = {"bfloat16": 2, "float16": 2, "uint8": 1, "float32": 4}
+ELEM_BYTES = {"bfloat16": 2, "float16": 2, "uint8": 1, "float32": 4, "int32": 4}
 
 
 def measured_peaks() -> tuple[float, str]:
@@ -167,7 +173,8 @@ def make_deck(w: dict, device, rows: int | None = None, seed_offset: int = 0):
         return torch.rand(shape, generator=g, device=device, dtype=dtype) * 2 - 1
     if w["init"] == "normal":
         return torch.randn(shape, generator=g, device=device, dtype=dtype)
-    return torch.randint(0, 256, shape, generator=g, device=device, dtype=torch.uint8)
+    raw = torch.randint(0, 256, (shape[0], row_bytes_of(w)), generator=g, device=device, dtype=torch.uint8)
+    return raw.view(dtype).reshape(shape)
 
 
 def run_ours(args, w: dict, wname: str) -> None:
@@ -194,7 +201,7 @@ def run_ours(args, w: dict, wname: str) -> None:
     elem = ELEM_BYTES[w["dtype"]]
     offsets = choose_offsets(N, R // elem, elem, P)
     opts = povs.Options(virtual_block_size=V, physical_block_size=P, offsets=offsets,
-                        gpu_thread_block_size=min(64, V * P))
+                        gpu_thread_block_size=max(32, min(64, V * P)))
     stream = torch.cuda.current_stream(device)
     if world > 1:
         # One deck of N rows split into `world` shards; every rank times the same collective steps.
@@ -218,14 +225,15 @@ def run_ours(args, w: dict, wname: str) -> None:
         if world > 1:
             dist.barrier(device_ids=[local])
 
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.5)  # let nvidia-smi start sampling before the timed region
+    # Warm-up right before the timed region, so that its first step does not start on a GPU that
+    # idled through the pause above (on the 256 MiB deck that cost 4 % over 20 steps).
     for s in range(args.warmup):
         step(1000 + s)
     torch.cuda.synchronize(device)
     povs.check_device_status(device)
-
-    sampler = ClockSampler(local)
-    sampler.start()
-    time.sleep(0.5)  # let nvidia-smi start sampling before the timed region
     barrier()
     torch.cuda.synchronize(device)
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -641,7 +649,7 @@ def run_one_process_shards(args, w: dict, wname: str) -> None:
     elem = ELEM_BYTES[w["dtype"]]
     offsets = choose_offsets(N, R // elem, elem, P)
     opts = povs.Options(virtual_block_size=V, physical_block_size=P, offsets=offsets,
-                        gpu_thread_block_size=min(64, V * P))
+                        gpu_thread_block_size=max(32, min(64, V * P)))
     rows = [N // K] * K
     rows[-1] += N - sum(rows)
     shards = [make_deck(w, torch.device("cuda", i), rows=rows[i], seed_offset=i) for i in range(K)]
@@ -690,6 +698,8 @@ def main() -> None:
     ap.add_argument("--rows", type=int, default=None, help="override the workload's row count (profiling captures)")
     ap.add_argument("--vblock", type=int, default=None, help="override the workload's V (profiling captures)")
     ap.add_argument("--pblock", type=int, default=None, help="override the workload's P (profiling captures)")
+    ap.add_argument("--pack-bytes", type=int, default=None,
+                    help="largest packed unit in bytes (0 = one vblock per unit; profiling captures)")
     ap.add_argument("--shards-on-gpus", type=int, default=None,
                     help="profiling mode: split the deck over this many GPUs of one process (povs.shuffle_shards)")
     args = ap.parse_args()
@@ -703,6 +713,11 @@ def main() -> None:
         if val:
             w["desc"] = w["desc"] + f" [{key} overridden: {val}]"
             w[key] = val
+    if args.pack_bytes is not None:
+        from povs import _native
+
+        _native.set_pack_bytes(args.pack_bytes)
+        w["desc"] = w["desc"] + f" [pack_bytes {args.pack_bytes}]"
     if args.impl == "reference":
         run_reference(args, w, args.workload)
     elif args.shards_on_gpus:
