@@ -52,7 +52,7 @@ def shuffle(
     :param options: POV options; partial or missing options are resolved as in ``optim_options_for_dataset``.
     :param seed: Integer seed, ``np.random.Generator`` or ``torch.Generator`` (None draws fresh entropy).
     """
-    seed = get_int_seed(seed)
+    seed = get_int_seed(seed, options)
 
     if isinstance(data, np.ndarray):
         povs_numpy.shuffle(data, iterations, options, seed)
@@ -79,7 +79,7 @@ def shuffle_mapped(
     GPU's memory (``povs.shuffle`` switches to this by itself when a host deck does not fit).
     Same result as ``povs.shuffle`` with the same arguments.  Addition to the reference API.
     """
-    seed = get_int_seed(seed)
+    seed = get_int_seed(seed, options)
     if isinstance(data, t.Tensor):
         if data.get_device() != -1:
             raise TypeError("shuffle_mapped takes host decks; use shuffle for CUDA tensors")
@@ -100,7 +100,7 @@ def shuffle_many(
     The decks stream through the GPU with their host/device copies overlapped; deck ``d`` is
     shuffled with seed ``seed + d``.  Addition to the reference API.
     """
-    base = get_int_seed(seed)
+    base = get_int_seed(seed, options)
     arrays = [d.numpy() if isinstance(d, t.Tensor) else d for d in decks]
     for d in decks:
         if isinstance(d, t.Tensor):
@@ -129,9 +129,9 @@ def shuffle_batch(
     if isinstance(seeds, (int, np.integer)) and not isinstance(seeds, bool):
         per_deck = [int(seeds) + d for d in range(n)]
     elif seeds is None or isinstance(seeds, (np.random.Generator, t.Generator)):
-        per_deck = [get_int_seed(seeds) for _ in range(n)]
+        per_deck = [get_int_seed(seeds, options) for _ in range(n)]
     else:
-        per_deck = [get_int_seed(s) for s in seeds]
+        per_deck = [get_int_seed(s, options) for s in seeds]
     povs_torch.shuffle_batch(decks, iterations, options, per_deck)
 
 

@@ -25,6 +25,7 @@ from .constants import (
     MIN_PBLOCK_SIZE,
     MIN_SEED,
     MIN_VBLOCK_SIZE,
+    REFERENCE_MAX_SEED,
 )
 from .types import BuildParams, Options
 from .utils import is_power_of_2, least_factor_to_make_multiple, round_down_to_power_of_2
@@ -36,16 +37,19 @@ def get_build_params() -> BuildParams:
     return BuildParams(**data)
 
 
-def get_int_seed(seed: int | np.random.Generator | torch.Generator | None) -> int:
-    """Normalise a seed: ints pass through, generators (or None -> fresh entropy) draw one integer."""
+def get_int_seed(seed: int | np.random.Generator | torch.Generator | None, options: Options | None = None) -> int:
+    """Normalise a seed: ints pass through, generators (or None -> fresh entropy) draw one integer,
+    from [1, 2**63 - 1), or from the reference's [1, 1000) (common.py:29-42 there) when ``options``
+    ask for ``randomness="reference_cuda"``."""
     if isinstance(seed, (int, np.integer)) and not isinstance(seed, bool):
         return int(seed)
+    high = REFERENCE_MAX_SEED if options is not None and options.randomness == "reference_cuda" else MAX_SEED
     if seed is None:
         seed = np.random.default_rng()
     if isinstance(seed, np.random.Generator):
-        return int(seed.integers(MIN_SEED, MAX_SEED, dtype=np.int64))
+        return int(seed.integers(MIN_SEED, high, dtype=np.int64))
     if isinstance(seed, torch.Generator):
-        return int(torch.randint(MIN_SEED, MAX_SEED, (1,), generator=seed, dtype=torch.int64).item())
+        return int(torch.randint(MIN_SEED, high, (1,), generator=seed, dtype=torch.int64).item())
     raise TypeError(f"Unsupported seed type: {type(seed)}")
 
 

@@ -4,7 +4,9 @@ Values that differ from the reference, and why:
   * ``MAX_SEED``: a ``numpy.random.Generator`` / ``torch.Generator`` seed is drawn from
     [1, 2**63 - 1) instead of [1, 1000).  The reference narrowed it so that its 32-bit per-vblock
     seeds matched between CPU and CUDA (constants.py:1-4 there); the device RNG here is keyed
-    by the full 64-bit seed, so a generator no longer collapses to 999 distinct shuffles.
+    by the full 64-bit seed, so a generator no longer collapses to 999 distinct shuffles.  With
+    ``randomness="reference_cuda"`` (the reference's distribution) a generator draws from the
+    reference's [1, 1000) again (``REFERENCE_MAX_SEED``).
   * ``MIN_PBLOCK_SIZE`` is 8 (the reference has 16).  With 8-bit instances and P = 8 the offset
     chooser still finds the two offsets [0, 4], which is the invariant the reference's bound
     protects; P = 8 is needed by the bias suite (deck 1000, V = 2, P = 8).
@@ -14,6 +16,7 @@ Values that differ from the reference, and why:
 
 MIN_SEED = 1
 MAX_SEED = 2**63 - 1
+REFERENCE_MAX_SEED = 1000
 
 # At least two offsets so that the per-iteration offset draw is not a constant.
 MIN_OFFSETS = 2

@@ -124,7 +124,7 @@ def shuffle_shards(
             _native.enable_peer_access(dev.index, t.device.index)
     _native.shuffle_shards(
         [s.data_ptr() for s in shards], rows, row_bytes, list(opts.offsets), iterations, opts.physical_block_size,
-        opts.virtual_block_size, seed_to_u64(get_int_seed(seed)), dev.index, randomness_flags(opts),
+        opts.virtual_block_size, seed_to_u64(get_int_seed(seed, opts)), dev.index, randomness_flags(opts),
         scratch_ptrs=[b.data_ptr() for b in scratch] if scratch is not None else None,
     )
 
@@ -207,9 +207,9 @@ class ShardedDeck:
         """Options resolved against the whole deck."""
         return resolve_options(self.n_rows, self.instance_size, self.dtype_bytes, self.device.index or 0, options)
 
-    def broadcast_seed(self, seed: int | Any | None) -> int:
+    def broadcast_seed(self, seed: int | Any | None, options: Options | None = None) -> int:
         """Rank 0's seed, on every rank (the one collective of a shuffle)."""
-        value = get_int_seed(seed) if self.rank == 0 else 0
+        value = get_int_seed(seed, options) if self.rank == 0 else 0
         t = torch.tensor([seed_to_u64(value) - (1 << 64) if seed_to_u64(value) >= (1 << 63) else seed_to_u64(value)],
                          dtype=torch.int64, device=self.device)
         dist.broadcast(t, src=dist.get_global_rank(self.group, 0) if self.group is not None else 0, group=self.group)
@@ -220,7 +220,7 @@ class ShardedDeck:
         """Collective: every rank calls with the same iterations and options."""
         opts = self.options(options)
         validate(self.n_rows, self.instance_size, self.dtype_bytes, iterations, opts, self.shard_rows)
-        seed_u64 = self.broadcast_seed(seed)
+        seed_u64 = self.broadcast_seed(seed, opts)
         if self.row_bytes == 0:
             return
         self.native.shuffle_sharded(

@@ -216,3 +216,23 @@ def test_tuning_option_on_host_decks():
     assert given.physical_block_size == 32
     with pytest.raises(AssertionError, match="tuning"):
         povs.optim_options_for_dataset(deck, tuning="fast")
+
+
+def test_generator_seeds_follow_the_randomness_mode():
+    """A generator seed is a 63-bit draw for the uniform mode and the reference's [1, 1000) draw when
+    the options ask for the reference CUDA path's distribution (its common.py:29-42)."""
+    import numpy as np
+    import torch
+
+    from povs.common import get_int_seed
+    from povs.types import Options
+
+    ref = Options(randomness="reference_cuda")
+    draws = [get_int_seed(np.random.default_rng(s), ref) for s in range(200)]
+    assert all(1 <= d < 1000 for d in draws)
+    assert draws[:5] == [int(np.random.default_rng(s).integers(1, 1000, dtype=np.int64)) for s in range(5)]
+    g = torch.Generator().manual_seed(3)
+    assert 1 <= get_int_seed(g, ref) < 1000
+    wide = [get_int_seed(np.random.default_rng(s), Options()) for s in range(50)]
+    assert max(wide) > 1000
+    assert get_int_seed(12345, ref) == 12345
