@@ -191,13 +191,17 @@ def test_thread_block_hint_for_small_vblocks():
         (256, 2, 1 << 30, 128),   # 64 KiB vblocks
         (256, 4, 1 << 30, 64),
         (128, 2, 1 << 30, 256),   # 512 rows
-        (64, 2, 1 << 30, 256),
-        (4, 2, 1 << 30, 256),
+        (96, 2, 1 << 30, 256),
+        (64, 2, 1 << 30, 128),    # short vblocks for small rows (packed units)
+        (48, 2, 1 << 30, 64),
+        (32, 4, 1 << 30, 32),
+        (16, 2, 1 << 30, 32),
+        (4, 2, 1 << 30, 16),
         (1024, 4, 1 << 30, 16),
         (12288, 2, 1 << 30, 16),  # wide rows: 32-row vblocks of 2 KiB slabs
         (12288, 4, 1 << 30, 8),
         (256, 32, 1 << 30, 8),    # never below the minimum pblock
-        (64, 2, 1000, 128),       # at least two vblocks' worth of pblocks in a small deck
+        (256, 2, 1000, 128),      # at least two vblocks' worth of pblocks in a small deck
     ],
 )
 def test_b200_pblock_choice(row_bytes, V, deck, expected):
@@ -210,7 +214,7 @@ def test_tuning_option_on_host_decks():
     deck = np.zeros((100_000, 64), dtype=np.float32)
     ref = povs.optim_options_for_dataset(deck)
     b200 = povs.optim_options_for_dataset(deck, tuning="b200")
-    assert ref.physical_block_size == 16 and b200.physical_block_size == 128
+    assert ref.physical_block_size == 16 and b200.physical_block_size == 128  # 256-byte rows: 64 KiB vblocks
     assert b200.offsets == list(range(16)) and b200.virtual_block_size == 2
     given = povs.optim_options_for_dataset(deck, povs.Options(physical_block_size=32), tuning="b200")
     assert given.physical_block_size == 32
