@@ -218,7 +218,8 @@ int32_t povs_version(void);
  *   n_stages    max data stages in a CTA's ring, 2..16 (default 8; fewer when shared memory is short)
  *   movers      warps per CTA that copy rows (default 4)
  *   permuters   warps per CTA that compute members and permutations (default 4); movers + permuters <= 16
- *   force_plain 1 = plain vector loads instead of TMA bulk copies
+ *   force_plain 1 = plain vector loads instead of TMA bulk copies (whole rows of 4-byte multiples
+ *               are then copied asynchronously); 2 = plain loads issued synchronously
  *   copy_bytes  target bytes of one bulk copy when whole rows are staged (default 8192)
  */
 int povs_set_tuning_v1(int32_t stage_cap, int32_t n_stages, int32_t movers, int32_t permuters, int32_t force_plain,

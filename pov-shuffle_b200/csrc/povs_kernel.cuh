@@ -111,6 +111,7 @@ struct IterParams {
     // Packed units (small vblocks): a unit is `pack` consecutive vblocks of one deck (pack == 1: one
     // vblock, or one column slab of it).  Unit slot f = s * vp + (slot of the s-th vblock), so the
     // unit has unit_vp = pack * vp slots; slots past a vblock's valid rows are holes.
+    int32_t async_plain;     // plain-load path: asynchronous copies (whole rows, 4-byte multiples)
     int32_t pack;
     int32_t unit_vp;
     int32_t vp_shift;        // log2(vp)
@@ -183,6 +184,26 @@ __device__ __forceinline__ void bulk_load(void* dst_smem, const void* src_gmem, 
                  "l"(src_gmem), "r"(bytes), "r"(smem_addr(bar))
                  : "memory");
 }
+
+// Per-thread asynchronous copies global -> shared of 4 or 8 bytes (both addresses aligned to the
+// size), and the arrival of this thread on `bar` once all of its earlier such copies have landed
+// (.noinc: the arrival counts as one of the barrier's expected arrivals).
+__device__ __forceinline__ void cp_async4(void* dst_smem, const void* src)
+{
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst_smem)), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async8(void* dst_smem, const void* src)
+{
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_addr(dst_smem)), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar)
+{
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // Programmatic dependent launch: the next kernel of a chain may start its CTAs (set-up and
 // permutations, which read no data) while this grid drains; its movers wait for this grid's
@@ -584,6 +605,78 @@ __device__ __forceinline__ void lsu_load_unit(const IterParams& p, const StageMe
             }
         }
     }
+}
+
+// One contiguous piece (len bytes, a multiple of 4; both addresses 4-byte aligned) global -> stage,
+// asynchronously, by the whole warp.  When the two addresses agree modulo 16, the 16-byte aligned
+// middle is one bulk copy (TMA, no multicast) issued by lane `piece % 32` after it registers the
+// bytes on `bar`, and the unaligned head and tail (< 16 bytes each) are 4-byte copies; otherwise the
+// piece goes as 8-byte copies (addresses agreeing modulo 8) or 4-byte copies spread over the lanes.
+__device__ __forceinline__ void async_copy_piece(uint8_t* dst, uintptr_t src, uint32_t len, uint64_t* bar, int lane,
+                                                 int piece)
+{
+    const uint32_t d = smem_addr(dst);
+    const uint32_t mis = d ^ static_cast<uint32_t>(src);
+    if ((mis & 15u) == 0) {
+        const uint32_t head = min(len, (16u - (static_cast<uint32_t>(src) & 15u)) & 15u);
+        const uint32_t body = (len - head) & ~15u;
+        const uint32_t tail_at = head + body;
+        if (body != 0 && lane == (piece & 31)) {
+            mbar_expect_tx(bar, body);
+            bulk_load(dst + head, reinterpret_cast<const void*>(src + head), body, bar);
+        }
+        const uint32_t n_head = head >> 2;
+        const uint32_t n_tail = (len - tail_at) >> 2;
+        if (static_cast<uint32_t>(lane) < n_head) {
+            cp_async4(dst + 4 * lane, reinterpret_cast<const void*>(src + 4 * lane));
+        } else if (lane >= 4 && static_cast<uint32_t>(lane - 4) < n_tail) {
+            const uint32_t o = tail_at + 4 * (lane - 4);
+            cp_async4(dst + o, reinterpret_cast<const void*>(src + o));
+        }
+    } else if ((mis & 7u) == 0) {
+        const uint32_t head = min(len, (8u - (static_cast<uint32_t>(src) & 7u)) & 7u); // 0 or 4
+        const uint32_t body = (len - head) & ~7u;
+        if (lane == 0 && head != 0) cp_async4(dst, reinterpret_cast<const void*>(src));
+        for (uint32_t o = head + 8u * lane; o < head + body; o += 256u)
+            cp_async8(dst + o, reinterpret_cast<const void*>(src + o));
+        if (lane == 1 && head + body < len) {
+            const uint32_t o = head + body;
+            cp_async4(dst + o, reinterpret_cast<const void*>(src + o));
+        }
+    } else {
+        for (uint32_t o = 4u * lane; o < len; o += 128u) cp_async4(dst + o, reinterpret_cast<const void*>(src + o));
+    }
+}
+
+// Whole-row units whose rows are a multiple of 4 bytes but not of 16 (or a deck that is not 16-byte
+// aligned): every member's <= 2 contiguous runs copied asynchronously into the stage
+// (async_copy_piece), so the issuing warp does not wait for its loads.  Each lane then arrives on
+// `bar` when its own copies have landed (the 32 arrivals the barrier expects), and the bulk bytes
+// keep the phase open until they land too.
+template <bool PUSH, bool PACK>
+__device__ __forceinline__ void async_load_unit(const IterParams& p, const StageMeta& m, uint8_t* stage, uint64_t* bar,
+                                                int lane)
+{
+    const int pmask = p.pblock - 1;
+    const int n_load = PUSH ? m.rows_mine : m.n_valid;
+    const int n_mem = PACK ? (p.pack << p.vblock_shift) : (PUSH ? 1 : (n_load + pmask) >> p.pblock_shift);
+    const uint32_t R = static_cast<uint32_t>(p.row_bytes);
+    int piece = 0;
+    for (int r = 0; r < n_mem; ++r) {
+        const int first = PUSH ? 0 : (r << p.pblock_shift);
+        const int rows_r = PACK ? static_cast<int>(m.mrows[r]) : (PUSH ? m.rows_mine : min(p.pblock, n_load - first));
+        if (rows_r <= 0) continue;
+        const int na = PUSH ? m.src_na : m.n_a[r];
+        const uintptr_t ra = PUSH ? m.src_a : m.run_a[r];
+        const uintptr_t rb = PUSH ? m.src_b : m.run_b[r];
+        const int n1 = min(rows_r, na);
+        if (n1 > 0)
+            async_copy_piece(stage + static_cast<size_t>(first) * R, ra, static_cast<uint32_t>(n1) * R, bar, lane, piece++);
+        if (rows_r > n1)
+            async_copy_piece(stage + static_cast<size_t>(first + n1) * R, rb + static_cast<uintptr_t>(n1) * R,
+                             static_cast<uint32_t>(rows_r - n1) * R, bar, lane, piece++);
+    }
+    cp_async_arrive_noinc(bar);
 }
 
 // store_share with the lane geometry computed by divisions: the form the bulk (TMA) path uses,
@@ -1316,6 +1409,12 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
                                   &sm.full[st]);
                     }
                 }
+            } else if (p.async_plain) {
+                // Whole rows of 4-byte multiples: asynchronous copies; each lane's arrival on `full`
+                // comes when its copies land (no separate arrival below).
+                fence_proxy_async_smem();
+                async_load_unit<PUSH, PACK>(p, m, stage, &sm.full[st], lane);
+                return true;
             } else {
                 switch (p.vec_bytes) {
                 case 16: lsu_load_unit<16, PUSH, PACK>(p, m, stage, col, slen, lane); break;
@@ -1354,13 +1453,14 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
             mbar_arrive(&sm.pempty[k]);  // ... and of the permutation slot
             return true;
         };
-        // On a timeout: wait (bounded) for the bulk copies of the units this warp issued and stop
-        // (plain loads complete before a unit's `full` arrival: nothing to wait for).
+        // On a timeout: wait (bounded) for the asynchronous copies of the units this warp issued and
+        // stop (synchronous plain loads complete before a unit's `full` arrival: nothing to wait for).
         auto drain_and_stop = [&](int64_t from) {
-            if constexpr (BULK) {
+            if (BULK || p.async_plain) {
                 for (int64_t u = from; u <= last_issued; ++u)
                     if (u % n_movers == mw)
                         warp_wait(&sm.full[u % nst], static_cast<uint32_t>((u / nst) & 1), p.status);
+                cp_async_wait_all(); // this thread's 4/8-byte copies (they always complete)
             }
         };
         const uint32_t n_slabs = static_cast<uint32_t>(p.n_slabs);

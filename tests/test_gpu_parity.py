@@ -248,6 +248,46 @@ def test_misaligned_deck_uses_plain_loads(oracle_api):
     assert np.array_equal(view.cpu().numpy(), want)
 
 
+# (n_rows, row_bytes, P, V, byte offset of the deck in its buffer): plain loads of whole rows.
+ASYNC_PLAIN_CASES = [
+    (20_011, 12, 16, 4, 0),   # 12-byte rows: runs agree mod 16 with the stage (bulk middle + 4-byte ends)
+    (20_011, 12, 32, 2, 0),
+    (9_999, 24, 32, 2, 0),    # 24-byte rows
+    (5_003, 20, 64, 2, 0),    # 20-byte rows: runs agree mod 4 only
+    (4_000, 64, 16, 2, 4),    # 16-byte multiple rows on a deck 4 bytes past a 16-byte boundary
+    (4_000, 48, 8, 4, 8),     # 8 bytes past: 8-byte copies
+    (3_000, 4, 128, 2, 0),    # 4-byte rows
+    (70_001, 28, 64, 4, 0),   # vblocks too large to pack
+]
+
+
+@pytest.mark.parametrize("n_rows,row_bytes,P,V,shift", ASYNC_PLAIN_CASES)
+def test_async_plain_loads_match_synchronous_loads_and_oracle(oracle_api, n_rows, row_bytes, P, V, shift):
+    """Rows that are not a 16-byte multiple (or a deck off a 16-byte boundary) are copied into the stages
+    asynchronously; the result equals the synchronous plain loads' and the oracle's."""
+    offsets = [0, 1, 2, 5]
+    host = random_rows(n_rows, row_bytes, seed=n_rows + shift)
+    results = []
+    try:
+        for force_plain in (0, 2):  # 2: plain loads issued synchronously
+            assert _native.load().povs_set_tuning_v1(32 * 1024, 8, 4, 4, force_plain, 8192) == 0
+            buf = torch.zeros(n_rows * row_bytes + shift, dtype=torch.uint8, device=DEV)
+            view = buf[shift:].view(n_rows, row_bytes)
+            view.copy_(torch.from_numpy(host))
+            plan = _native.describe_plan(view, row_bytes, P, V)
+            assert plan["bulk"] == 0
+            _native.shuffle_device(view, row_bytes, offsets, 3, P, V, 31)
+            torch.cuda.synchronize()
+            povs.check_device_status(0)
+            results.append(view.cpu().numpy())
+    finally:
+        _native.set_tuning()
+    want = host.copy()
+    oracle_api.shuffle(want, 3, P, V, offsets, 31)
+    assert np.array_equal(results[1], want), "synchronous plain loads differ from the oracle"
+    assert np.array_equal(results[0], want), "asynchronous plain loads differ from the oracle"
+
+
 def test_plans_cover_bulk_and_slab_paths():
     t = torch.empty((1200, 12288), dtype=torch.uint8, device=DEV)
     plan = _native.describe_plan(t, 12288, 16, 2)
