@@ -312,6 +312,24 @@ int povs_ngram_keys_v1(const void* ids, int32_t id_bytes, int64_t n_episodes, in
                        int64_t element_stride, int32_t n, int64_t step, const int64_t* positions,
                        int64_t n_positions, int64_t* keys, int32_t device, void* stream);
 
+/*
+ * The distinct n-gram keys of povs_ngram_keys_v1 (same arguments) counted without sorting, for the
+ * sparse n-gram TVD (metrics.py:173-248, which sorts the keys with np.unique): an open-addressing
+ * hash table in `table` (device, 2 * slots + 1 uint64, overwritten; slots a power of two above the
+ * number of keys, twice it or more keeps probes short), then the multiplicities of the counts:
+ * mult[c] (device, mult_bins uint64, overwritten) = distinct keys seen exactly c times for
+ * 1 <= c < mult_bins, mult[0] = distinct keys seen mult_bins times or more, whose counts go to
+ * overflow[0 .. min(mult[0], overflow_cap) - 1] (device, any order).  The TVD needs only these:
+ * observed keys = sum of mult, and sum over keys of |count / observations - p_ref|.  A key that
+ * finds no free slot sets POVS_DEV_TABLE_FULL in the device status word.  No reference
+ * counterpart as an entry point (the reference counts on the host).
+ */
+#define POVS_DEV_TABLE_FULL 8
+int povs_ngram_count_v1(const void* ids, int32_t id_bytes, int64_t n_episodes, int64_t deck, int64_t episode_stride,
+                        int64_t element_stride, int32_t n, int64_t step, const int64_t* positions,
+                        int64_t n_positions, uint64_t* table, int64_t slots, uint64_t* mult, int64_t mult_bins,
+                        uint64_t* overflow, int64_t overflow_cap, int32_t device, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

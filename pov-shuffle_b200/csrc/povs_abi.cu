@@ -1426,6 +1426,63 @@ extern "C" int povs_ngram_keys_v1(const void* ids, int32_t id_bytes, int64_t n_e
     return POVS_OK;
 }
 
+extern "C" int povs_ngram_count_v1(const void* ids, int32_t id_bytes, int64_t n_episodes, int64_t deck,
+                                   int64_t episode_stride, int64_t element_stride, int32_t n, int64_t step,
+                                   const int64_t* positions, int64_t n_positions, uint64_t* table, int64_t slots,
+                                   uint64_t* mult, int64_t mult_bins, uint64_t* overflow, int64_t overflow_cap,
+                                   int32_t device, void* stream)
+{
+    g_err[0] = '\0';
+    int r = check_metric_args(ids, id_bytes, n_episodes, deck);
+    if (r != POVS_OK) return r;
+    if (n < 2) return fail(POVS_ERR_INVALID_ARGUMENT, "n-gram degree (%d) must be at least 2", n);
+    if (step < 1) return fail(POVS_ERR_INVALID_ARGUMENT, "step (%lld) must be positive", static_cast<long long>(step));
+    if (positions != nullptr && n_positions < 1) return fail(POVS_ERR_INVALID_ARGUMENT, "n_positions must be positive");
+    if (table == nullptr || mult == nullptr) return fail(POVS_ERR_INVALID_ARGUMENT, "table and mult are required");
+    const int64_t total = n_episodes * (positions != nullptr ? n_positions : deck);
+    if (!is_pow2(slots) || slots <= total)
+        return fail(POVS_ERR_INVALID_ARGUMENT, "slots (%lld) must be a power of two above the %lld keys",
+                    static_cast<long long>(slots), static_cast<long long>(total));
+    if (mult_bins < 2) return fail(POVS_ERR_INVALID_ARGUMENT, "mult_bins (%lld) must be at least 2", static_cast<long long>(mult_bins));
+    if (overflow_cap < 0 || (overflow_cap > 0 && overflow == nullptr))
+        return fail(POVS_ERR_INVALID_ARGUMENT, "overflow must hold overflow_cap entries");
+    DeviceGuard dg;
+    r = dg.enter(device);
+    if (r != POVS_OK) return r;
+    DeviceCtx* c = nullptr;
+    r = get_ctx(device, &c);
+    if (r != POVS_OK) return r;
+    povs::MetricParams q{};
+    q.ids = ids;
+    q.id_bytes = id_bytes;
+    q.kind = n;
+    q.n_episodes = n_episodes;
+    q.deck = deck;
+    q.episode_stride = episode_stride;
+    q.element_stride = element_stride;
+    q.step = step;
+    q.positions = positions;
+    q.n_positions = positions != nullptr ? n_positions : 0;
+    povs::NgramTable t{};
+    t.keys = reinterpret_cast<unsigned long long*>(table);
+    t.counts = reinterpret_cast<unsigned long long*>(table) + slots;
+    t.slots = slots;
+    t.mult = reinterpret_cast<unsigned long long*>(mult);
+    t.mult_bins = mult_bins;
+    t.overflow = reinterpret_cast<unsigned long long*>(overflow);
+    t.overflow_cap = overflow_cap;
+    t.status = c->status;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int grid_t = metric_grid(*c, std::max<int64_t>(slots + 1, mult_bins), 1);
+    const int grid_k = metric_grid(*c, total, 1);
+    povs::povs_ngram_table_clear_kernel<<<grid_t, 256, 0, s>>>(t);
+    povs::povs_ngram_count_kernel<<<grid_k, 256, 0, s>>>(q, t);
+    povs::povs_ngram_tally_kernel<<<grid_t, 256, 0, s>>>(t);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "n-gram count kernels");
+    return POVS_OK;
+}
+
 extern "C" int povs_set_peer_wait_limit_v1(uint64_t limit_ns)
 {
     g_err[0] = '\0';

@@ -56,6 +56,7 @@ enum : int {
     DEV_ERR_WAIT_TIMEOUT = 1, // an mbarrier wait gave up after the time limit
     DEV_ERR_BAD_INJECTED = 2, // an injected permutation entry was out of range (identity used instead)
     DEV_ERR_PEER_TIMEOUT = 4, // a cross-GPU barrier gave up waiting for a peer
+    DEV_ERR_TABLE_FULL = 8,   // an n-gram count table had no free slot for a key (key not counted)
 };
 
 constexpr unsigned long long PEER_WAIT_LIMIT_NS = 20000000000ull; // default: 20 s for a peer GPU to reach the barrier

@@ -81,23 +81,112 @@ __global__ void __launch_bounds__(256) povs_travel_histogram_kernel(const __grid
     }
 }
 
+// Key of observation o (episode o / per_episode, anchor o % per_episode).
+__device__ __forceinline__ uint64_t ngram_key(const MetricParams& q, int64_t o, int64_t per_episode)
+{
+    const int64_t e = o / per_episode;
+    const int64_t j = o - e * per_episode;
+    const int64_t anchor = q.positions != nullptr ? floor_mod(q.positions[j], q.deck) : j;
+    const int64_t v0 = metric_id(q, e, anchor);
+    const uint64_t base = static_cast<uint64_t>(q.deck);
+    uint64_t key = 0; // wraps modulo 2^64 like the reference's int64 key arithmetic
+    for (int k = 1; k < q.kind; ++k) {
+        const int64_t vk = metric_id(q, e, floor_mod(anchor + k * q.step, q.deck));
+        key = key * base + static_cast<uint64_t>(floor_mod((vk - v0) - k * q.step, q.deck));
+    }
+    return key;
+}
+
 __global__ void __launch_bounds__(256) povs_ngram_keys_kernel(const __grid_constant__ MetricParams q)
 {
     const int64_t per_episode = q.positions != nullptr ? q.n_positions : q.deck;
     const int64_t total = q.n_episodes * per_episode;
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    const uint64_t base = static_cast<uint64_t>(q.deck);
+    for (int64_t o = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; o < total; o += stride)
+        q.keys[o] = static_cast<int64_t>(ngram_key(q, o, per_episode));
+}
+
+// ---------------------------------------------------------------------------------------------
+// Distinct n-gram keys and their counts without sorting: an open-addressing hash table in global
+// memory (keys[slots] then counts[slots + 1]; the extra count is for the one key value that marks
+// an empty slot), linear probing from a 64-bit mix of the key, then the multiplicities of the counts.
+// ---------------------------------------------------------------------------------------------
+
+constexpr unsigned long long NGRAM_EMPTY = ~0ull;
+
+struct NgramTable {
+    unsigned long long* keys;   // slots entries, NGRAM_EMPTY when free
+    unsigned long long* counts; // slots + 1 entries
+    int64_t slots;              // a power of two, more than the distinct keys
+    unsigned long long* mult;   // mult[c]: distinct keys seen exactly c times (1 <= c < mult_bins);
+                                // mult[0]: distinct keys seen mult_bins times or more
+    int64_t mult_bins;
+    unsigned long long* overflow; // counts of the keys tallied in mult[0], first overflow_cap of them
+    int64_t overflow_cap;
+    int* status;                  // device status word: DEV_ERR_TABLE_FULL if a key found no free slot
+};
+
+// A 64-bit finaliser (xor-shift / multiply rounds) spreading keys over the table.
+__device__ __forceinline__ uint64_t mix64(uint64_t x)
+{
+    x ^= x >> 31;
+    x *= 0x7fb5d329728ea185ull;
+    x ^= x >> 27;
+    x *= 0x81dadef4bc2dd44dull;
+    x ^= x >> 33;
+    return x;
+}
+
+__global__ void __launch_bounds__(256) povs_ngram_table_clear_kernel(NgramTable t)
+{
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i <= t.slots; i += stride) {
+        if (i < t.slots) t.keys[i] = NGRAM_EMPTY;
+        t.counts[i] = 0;
+        if (i < t.mult_bins) t.mult[i] = 0;
+    }
+}
+
+__global__ void __launch_bounds__(256) povs_ngram_count_kernel(const __grid_constant__ MetricParams q, NgramTable t)
+{
+    const int64_t per_episode = q.positions != nullptr ? q.n_positions : q.deck;
+    const int64_t total = q.n_episodes * per_episode;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    const uint64_t mask = static_cast<uint64_t>(t.slots) - 1;
     for (int64_t o = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; o < total; o += stride) {
-        const int64_t e = o / per_episode;
-        const int64_t j = o - e * per_episode;
-        const int64_t anchor = q.positions != nullptr ? floor_mod(q.positions[j], q.deck) : j;
-        const int64_t v0 = metric_id(q, e, anchor);
-        uint64_t key = 0; // wraps modulo 2^64 like the reference's int64 key arithmetic
-        for (int k = 1; k < q.kind; ++k) {
-            const int64_t vk = metric_id(q, e, floor_mod(anchor + k * q.step, q.deck));
-            key = key * base + static_cast<uint64_t>(floor_mod((vk - v0) - k * q.step, q.deck));
+        const unsigned long long key = ngram_key(q, o, per_episode);
+        if (key == NGRAM_EMPTY) {
+            atomicAdd(&t.counts[t.slots], 1ull);
+            continue;
         }
-        q.keys[o] = static_cast<int64_t>(key);
+        uint64_t h = mix64(key) & mask;
+        bool placed = false;
+        for (int64_t probe = 0; probe < t.slots; ++probe) {
+            unsigned long long k = t.keys[h];
+            if (k == NGRAM_EMPTY) k = atomicCAS(&t.keys[h], NGRAM_EMPTY, key);
+            if (k == NGRAM_EMPTY || k == key) {
+                atomicAdd(&t.counts[h], 1ull);
+                placed = true;
+                break;
+            }
+            h = (h + 1) & mask;
+        }
+        if (!placed) atomicOr(t.status, DEV_ERR_TABLE_FULL);
+    }
+}
+
+__global__ void __launch_bounds__(256) povs_ngram_tally_kernel(NgramTable t)
+{
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i <= t.slots; i += stride) {
+        const unsigned long long c = t.counts[i];
+        if (c == 0) continue;
+        if (c < static_cast<unsigned long long>(t.mult_bins)) {
+            atomicAdd(&t.mult[c], 1ull);
+        } else {
+            const unsigned long long at = atomicAdd(&t.mult[0], 1ull);
+            if (at < static_cast<unsigned long long>(t.overflow_cap)) t.overflow[at] = c;
+        }
     }
 }
 

@@ -78,6 +78,11 @@ SIGNATURES: dict[str, tuple] = {
         ctypes.c_int,
         [_c_vp, _c_i32, _c_i64, _c_i64, _c_i64, _c_i64, _c_i32, _c_i64, _c_vp, _c_i64, _c_vp, _c_i32, _c_vp],
     ),
+    "povs_ngram_count_v1": (
+        ctypes.c_int,
+        [_c_vp, _c_i32, _c_i64, _c_i64, _c_i64, _c_i64, _c_i32, _c_i64, _c_vp, _c_i64, _c_vp, _c_i64, _c_vp, _c_i64,
+         _c_vp, _c_i64, _c_i32, _c_vp],
+    ),
     "povs_set_peer_wait_limit_v1": (ctypes.c_int, [_c_u64]),
     "povs_apply_static_v1": (
         ctypes.c_int,
@@ -221,6 +226,46 @@ def ngram_keys(ids: torch.Tensor, n: int, step: int, positions: torch.Tensor | N
     )
     check(code, "povs_ngram_keys_v1")
     return keys
+
+
+def ngram_count(ids: torch.Tensor, n: int, step: int, positions: torch.Tensor | None = None,
+                mult_bins: int = 1 << 16, overflow_cap: int = 1 << 20) -> tuple[np.ndarray, np.ndarray]:
+    """Multiplicities of the distinct n-gram keys (``povs_ngram_count_v1``): ``mult`` (mult[c] =
+    keys seen exactly c times, mult[0] = keys seen ``mult_bins`` times or more) and the counts of the
+    latter, as NumPy arrays.  Raises if a key found no room in the table."""
+    import numpy as np
+
+    lib = load()
+    id_bytes, n_ep, deck, ep_stride = _episode_layout(ids)
+    dev = ids.device
+    count = deck if positions is None else positions.numel()
+    total = n_ep * count
+    slots = 1
+    while slots < 2 * total:
+        slots <<= 1
+    if positions is not None:
+        assert positions.is_cuda and positions.dtype == torch.int64 and positions.is_contiguous()
+    while True:
+        table = torch.empty(2 * slots + 1, dtype=torch.int64, device=dev)
+        mult = torch.empty(mult_bins, dtype=torch.int64, device=dev)
+        overflow = torch.empty(max(1, overflow_cap), dtype=torch.int64, device=dev)
+        code = lib.povs_ngram_count_v1(
+            ctypes.c_void_p(ids.data_ptr()), id_bytes, n_ep, deck, ep_stride, ids.stride(1), n, step,
+            ctypes.c_void_p(positions.data_ptr()) if positions is not None else None,
+            count if positions is not None else 0, ctypes.c_void_p(table.data_ptr()), slots,
+            ctypes.c_void_p(mult.data_ptr()), mult_bins, ctypes.c_void_p(overflow.data_ptr()), overflow_cap,
+            dev.index, ctypes.c_void_p(current_stream_handle(dev)),
+        )
+        check(code, "povs_ngram_count_v1")
+        del table
+        m = mult.cpu().numpy().astype(np.uint64)
+        if int(m[0]) <= overflow_cap:
+            break
+        overflow_cap = int(m[0])  # more keys above mult_bins than room: once more with room for all
+    status = device_status(dev.index)
+    if status:
+        raise RuntimeError(f"device status 0x{status:x} after povs_ngram_count_v1 (8: the hash table was full)")
+    return m, overflow[: int(m[0])].cpu().numpy().astype(np.uint64)
 
 
 def shuffle_host(

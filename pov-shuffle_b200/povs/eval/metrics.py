@@ -3,8 +3,8 @@
 Episodes are arrays of shape (num_episodes, deck_size) whose rows are permutations of the ids
 0 .. deck_size-1 (shuffled ``arange`` decks).  They may be NumPy arrays or torch tensors; they
 are moved to a CUDA device (the tensor's own, else ``device``, else the current one) and the
-per-observation work - travel distances, their histograms, n-gram keys - runs in the native
-library's kernels.  The O(deck) TVD arithmetic on the resulting counts is done on the host with
+per-observation work - travel distances, their histograms, n-gram keys and their counts - runs in
+the native library's kernels.  The O(deck) TVD arithmetic on the resulting counts is done on the host with
 the reference's formulas, so results match the reference's NumPy implementation up to the
 summation order of the final float64 sum.
 """
@@ -83,8 +83,8 @@ def get_ngram_tvd(episodes, n: int, skip: int = 0, device: torch.device | str | 
 
     Reference: get_ngram_tvd (metrics.py:90-248), adaptive formula included: for n = 2 a dense
     histogram of the ``deck - 1`` possible distances (built on the GPU); for n > 2 the distinct
-    n-gram keys (computed on the GPU, counted with ``torch.unique``) and the unobserved events
-    accounted analytically.  When the keys would exceed 512 MiB, the same number of anchor
+    n-gram keys (computed and counted on the GPU in a hash table, ``povs_ngram_count_v1``) and the
+    unobserved events accounted analytically.  When the keys would exceed 512 MiB, the same number of anchor
     positions per episode as the reference's is drawn from NumPy's global generator, as there.
     """
     assert n >= 2, f"n-gram degree ({n}) must be at least 2"
@@ -112,10 +112,13 @@ def get_ngram_tvd(episodes, n: int, skip: int = 0, device: torch.device | str | 
         positions = torch.from_numpy(chosen.astype(np.int64)).to(ids.device)
         effective = int(num_episodes) * per_episode
     p_ref = 1.0 / min(effective, event_space)
-    keys = _native.ngram_keys(ids, n, step, positions)
-    _, key_counts = torch.unique(keys, sorted=True, return_counts=True)
-    del keys
-    observed = key_counts.numel()
-    p_obs = key_counts.cpu().numpy() / effective
+    # Distinct keys counted in a hash table on the GPU; what comes back is how many keys were seen
+    # exactly c times, so the reference's sum over keys of |count / effective - p_ref| is a sum over c.
+    mult, big = _native.ngram_count(ids, n, step, positions)
+    c = np.arange(1, len(mult), dtype=np.float64)
+    per_key = mult[1:].astype(np.float64)
+    observed = int(mult[1:].sum()) + int(mult[0])
+    deviation = float(np.sum(per_key * np.abs(c / effective - p_ref)))
+    deviation += float(np.sum(np.abs(np.sort(big).astype(np.float64) / effective - p_ref)))
     missing = min(event_space, effective) - observed
-    return float(1 / 2 * (missing * p_ref + np.sum(np.abs(p_obs - p_ref))))
+    return float(1 / 2 * (missing * p_ref + deviation))

@@ -128,6 +128,12 @@ def test_added_entry_points_reject_invalid_arguments_before_any_device_call():
     assert lib.povs_ngram_keys_v1(data, 8, 10, 10, 10, 1, 1, 1, None, 0, counts, 0, None) == -1
     assert b"degree" in lib.povs_last_error_string()
     assert lib.povs_ngram_keys_v1(data, 8, 0, 10, 10, 1, 3, 1, None, 0, counts, 0, None) == -1
+    # n-gram counting: the table must be a power of two above the number of keys.
+    tab = ctypes.c_void_p(128)
+    assert lib.povs_ngram_count_v1(data, 8, 10, 10, 10, 1, 3, 1, None, 0, tab, 64, counts, 16, counts, 4, 0, None) == -1
+    assert b"slots" in lib.povs_last_error_string()
+    assert lib.povs_ngram_count_v1(data, 8, 10, 10, 10, 1, 3, 1, None, 0, tab, 256, counts, 1, counts, 4, 0, None) == -1
+    assert lib.povs_ngram_count_v1(data, 8, 10, 10, 10, 1, 3, 1, None, 0, None, 256, counts, 16, counts, 4, 0, None) == -1
     # Allocation-free injection: only POVS_FLAG_SYNC is accepted.
     host = ctypes.c_void_p(64)
     for flags in (_native.FLAG_NO_GRAPH, _native.FLAG_REFERENCE_RNG, 8, 1 << 20):

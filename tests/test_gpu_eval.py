@@ -249,3 +249,25 @@ def test_shuffle_time_per_deck_size_report(monkeypatch, tmp_path):
         assert torch.equal(d.to(torch.int64), ids[:, None].expand_as(d)), "a row was torn"
         assert torch.equal(torch.sort(ids).values, torch.arange(d.shape[0], device=d.device))
         assert not torch.equal(ids, torch.arange(d.shape[0], device=d.device))
+
+
+@pytest.mark.parametrize("n,skip", [(3, 0), (4, 1)])
+def test_ngram_counts_hash_table_against_sorting(n, skip):
+    """The hash-table counts (povs_ngram_count_v1) against sorting the same keys (torch.unique): the
+    same multiplicities, also when every count goes through the overflow list (mult_bins = 2)."""
+    from povs import _native
+
+    ids = torch.from_numpy(episodes_for(3, 1000, 300)).to(DEV)
+    keys = _native.ngram_keys(ids, n, skip + 1)
+    _, counts = torch.unique(keys, return_counts=True)
+    want = np.bincount(counts.cpu().numpy())
+    mult, big = _native.ngram_count(ids, n, skip + 1)
+    assert int(mult[0]) == 0 and len(big) == 0
+    got = np.zeros(max(len(want), len(mult)), dtype=np.int64)
+    got[:len(mult)] = mult.astype(np.int64)
+    got[0] = 0
+    assert np.array_equal(got[:len(want)], want) and not got[len(want):].any()
+    c = counts.cpu().numpy()
+    mult2, big2 = _native.ngram_count(ids, n, skip + 1, mult_bins=2, overflow_cap=1)
+    assert int(mult2[1]) == int((c == 1).sum()) and int(mult2[0]) == int((c >= 2).sum())
+    assert np.array_equal(np.sort(big2.astype(np.int64)), np.sort(c[c >= 2]))
