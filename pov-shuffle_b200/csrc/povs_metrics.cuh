@@ -140,9 +140,10 @@ __device__ __forceinline__ uint64_t mix64(uint64_t x)
 __global__ void __launch_bounds__(256) povs_ngram_table_clear_kernel(NgramTable t)
 {
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i <= t.slots; i += stride) {
+    const int64_t n = t.slots + 1 > t.mult_bins ? t.slots + 1 : t.mult_bins;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
         if (i < t.slots) t.keys[i] = NGRAM_EMPTY;
-        t.counts[i] = 0;
+        if (i <= t.slots) t.counts[i] = 0;
         if (i < t.mult_bins) t.mult[i] = 0;
     }
 }

@@ -22,7 +22,8 @@ BUILD_PARAMS_PATH = PKG_DIR / "build_params.json"
 CUDA_ARCH = "100a"
 
 SOURCES = [CSRC_DIR / "povs_abi.cu"]
-DEPENDS = [*SOURCES, CSRC_DIR / "povs_kernel.cuh", CSRC_DIR / "povs_rng.cuh", INCLUDE_DIR / "povs.h"]
+DEPENDS = [*SOURCES, CSRC_DIR / "povs_kernel.cuh", CSRC_DIR / "povs_rng.cuh", CSRC_DIR / "povs_metrics.cuh",
+           INCLUDE_DIR / "povs.h"]
 
 
 def _nvcc() -> str:
