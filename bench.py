@@ -535,10 +535,15 @@ def reference_cuda_path(w: dict, wname: str, steps: int) -> dict:
     N, P, V, iters = w["rows"], w["P"], w["V"], w["iterations"]
     shape = oracle.ref_cuda_shape(V, P, R)
     if shape is None:
-        smem = V * P * R
-        return {"value": None, "unavailable": (
-            f"the reference kernel stages a whole vblock ({smem:,} B) in static shared memory (48 KB limit, "
-            "src/povs/__cuda/lib/povs.cu:167): no instantiation exists for this shape")}
+        if V * P < 32:
+            why = (f"the reference kernel needs a thread block of 32 to V*P = {V * P} threads "
+                   "(src/povs/__cuda/lib/povs.cu:139-142): this shape has no valid instantiation")
+        elif V * P * R + 4 * V * P > 48 * 1024:
+            why = (f"the reference kernel stages a whole vblock ({V * P * R:,} B) in static shared memory (48 KB "
+                   "limit, src/povs/__cuda/lib/povs.cu:167): no instantiation exists for this shape")
+        else:
+            why = "the reference-built library has no instantiation of this shape"
+        return {"value": None, "unavailable": why}
     info = next(sh for sh in oracle.ref_cuda_shapes() if sh["index"] == shape)
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
