@@ -193,6 +193,14 @@ int povs_set_peer_wait_limit_v1(uint64_t limit_ns);
  */
 int povs_enable_peer_access_v1(int32_t device, int32_t peer);
 
+/*
+ * Host only (no GPU needed): numpy.random.RandomState(seed).shuffle(arange(n)) into out[0 .. n-1],
+ * the permutation the reference's NumPy path applies to a vblock of n rows under per-vblock seed
+ * `seed` (src/povs/numpy.py:125-136).  The tables of the POVS_FLAG_REFERENCE_NUMPY mode are built
+ * from it.
+ */
+int povs_numpy_path_perm_v1(uint32_t seed, int32_t n, int32_t* out);
+
 /* CUDA IPC of device memory between the processes of a sharded deck (64-byte handles). */
 int povs_ipc_export_v1(const void* ptr, int32_t device, void* handle_out, int64_t* offset_out);
 int povs_ipc_import_v1(const void* handle, int64_t offset, int32_t device, void** ptr_out, void** base_out);

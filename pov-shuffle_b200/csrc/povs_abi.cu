@@ -18,6 +18,7 @@
 #include "../../include/povs.h"
 #include "povs_kernel.cuh"
 #include "povs_metrics.cuh"
+#include "povs_mt19937.h"
 
 using povs::IterParams;
 
@@ -1480,6 +1481,14 @@ extern "C" int povs_ngram_count_v1(const void* ids, int32_t id_bytes, int64_t n_
     povs::povs_ngram_tally_kernel<<<grid_t, 256, 0, s>>>(t);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "n-gram count kernels");
+    return POVS_OK;
+}
+
+extern "C" int povs_numpy_path_perm_v1(uint32_t seed, int32_t n, int32_t* out)
+{
+    g_err[0] = '\0';
+    if (n < 0 || (n > 0 && out == nullptr)) return fail(POVS_ERR_INVALID_ARGUMENT, "n must be >= 0 and out given");
+    povs::numpy_legacy_shuffle(seed, n, out);
     return POVS_OK;
 }
 

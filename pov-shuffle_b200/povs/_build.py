@@ -23,7 +23,7 @@ CUDA_ARCH = "100a"
 
 SOURCES = [CSRC_DIR / "povs_abi.cu"]
 DEPENDS = [*SOURCES, CSRC_DIR / "povs_kernel.cuh", CSRC_DIR / "povs_rng.cuh", CSRC_DIR / "povs_metrics.cuh",
-           INCLUDE_DIR / "povs.h"]
+           CSRC_DIR / "povs_mt19937.h", INCLUDE_DIR / "povs.h"]
 
 
 def _nvcc() -> str:

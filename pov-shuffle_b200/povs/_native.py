@@ -83,6 +83,7 @@ SIGNATURES: dict[str, tuple] = {
         [_c_vp, _c_i32, _c_i64, _c_i64, _c_i64, _c_i64, _c_i32, _c_i64, _c_vp, _c_i64, _c_vp, _c_i64, _c_vp, _c_i64,
          _c_vp, _c_i64, _c_i32, _c_vp],
     ),
+    "povs_numpy_path_perm_v1": (ctypes.c_int, [_c_u32, _c_i32, _c_vp]),
     "povs_set_peer_wait_limit_v1": (ctypes.c_int, [_c_u64]),
     "povs_apply_static_v1": (
         ctypes.c_int,

@@ -182,3 +182,17 @@ def test_host_route_requires_a_gpu():
     deck = np.arange(64 * 4, dtype=np.float32).reshape(64, 4)
     with pytest.raises(RuntimeError, match="CUDA device"):
         povs.shuffle(deck, seed=1)
+
+
+def test_numpy_path_permutations_match_numpy():
+    """The host restatement of MT19937 and NumPy's legacy shuffle (povs_mt19937.h) against
+    numpy.random.RandomState itself, for the reference's seeds 1..999 and beyond."""
+    lib = _native.load()
+    for seed in list(range(0, 1000, 7)) + [999, 2**31, 2**32 - 1]:
+        for n in (1, 2, 16, 17, 128, 1000):
+            out = np.zeros(n, dtype=np.int32)
+            assert lib.povs_numpy_path_perm_v1(seed, n, ctypes.c_void_p(out.ctypes.data)) == 0
+            want = np.arange(n)
+            np.random.RandomState(seed).shuffle(want)
+            assert np.array_equal(out, want), (seed, n)
+    assert lib.povs_numpy_path_perm_v1(1, -1, None) == -1
