@@ -47,6 +47,12 @@ extern "C" {
  * on the stream drains - the previous iteration, or for decks of 32 MiB and more the previous
  * call's last iteration - and wait for it to complete before touching the deck). */
 #define POVS_FLAG_NO_PDL 8u
+/* Draw the randomness with the distribution of the reference's NumPy path (padding ids anywhere,
+ * members in slot order, per-vblock seeds 1..999 and numpy.random.RandomState(seed).shuffle of the
+ * vblock's rows; src/povs/numpy.py:43-61,125-136).  The permutations come from tables built on the
+ * host once per (P, V, n_rows % P) and device (at most 128 MiB; a larger geometry is rejected with
+ * POVS_ERR_UNSUPPORTED), freed by povs_release_v1.  Excludes POVS_FLAG_REFERENCE_RNG. */
+#define POVS_FLAG_REFERENCE_NUMPY 16u
 
 /* Limits of this library. */
 #define POVS_MAX_OFFSETS 256 /* offsets are passed to the device inline in the launch parameters */

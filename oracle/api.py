@@ -49,6 +49,8 @@ def lib() -> ctypes.CDLL:
             L.oracle_refcuda_randomness.restype = ctypes.c_int
             L.oracle_refcuda_perms.argtypes = [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, _P, _P, _P]
             L.oracle_refcuda_perms.restype = ctypes.c_int
+            L.oracle_set_numpy_table.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int64]
+            L.oracle_set_numpy_table.restype = None
             _lib = L
         return _lib
 
@@ -170,13 +172,41 @@ def apply_iteration(deck: np.ndarray, pblock: int, vblock: int, offset: int, ass
         raise ValueError(f"oracle_apply_iteration failed ({rc})")
 
 
-MODES = {"uniform": 0, "reference_cuda": 1}
+MODES = {"uniform": 0, "reference_cuda": 1, "reference_numpy": 2}
+
+_np_tables: dict = {}
+
+
+def _use_numpy_table(n_rows: int, pblock: int, vblock: int) -> None:
+    """Hand the C oracle the NumPy path's per-vblock permutations for this geometry, built with NumPy
+    itself: numpy.random.RandomState(s).shuffle(arange(n)) for s = 1..999 and every valid-row count n."""
+    trunc = n_rows % pblock
+    key = (pblock, vblock, trunc)
+    if key not in _np_tables:
+        sizes = [m * pblock for m in range(1, vblock + 1)]
+        sizes += [(m - 1) * pblock + trunc if trunc else 0 for m in range(1, vblock + 1)]
+        off = np.full(64, -1, dtype=np.int64)
+        parts, at = [], 0
+        for c, n in enumerate(sizes):
+            if n <= 0:
+                continue
+            off[c] = at
+            for s in range(1, 1000):
+                a = np.arange(n, dtype=np.int32)
+                np.random.RandomState(s).shuffle(a)
+                parts.append(a)
+            at += 999 * n
+        _np_tables[key] = (np.ascontiguousarray(np.concatenate(parts)), off)
+    table, off = _np_tables[key]
+    lib().oracle_set_numpy_table(_ptr(table), _ptr(off), pblock, vblock, trunc)
 
 
 def device_randomness(seed: int, iteration: int, n_rows: int, pblock: int, vblock: int,
                       offsets: list[int], mode: str = "uniform") -> tuple[int, np.ndarray, np.ndarray]:
     """The library's device randomness for one iteration: (offset, assign [n_v,V], perms [n_v,V*P])."""
     n_p, n_v = block_counts(n_rows, pblock, vblock)
+    if mode == "reference_numpy":
+        _use_numpy_table(n_rows, pblock, vblock)
     offs = np.array(offsets, dtype=np.int64)
     off = np.zeros(1, dtype=np.int64)
     assign = np.zeros((n_v, vblock), dtype=np.int64)
@@ -193,6 +223,8 @@ def shuffle(deck: np.ndarray, iterations: int, pblock: int, vblock: int, offsets
     """The library's full shuffle (device randomness of ``seed``), in place on a host deck."""
     rows = as_rows(deck)
     n, r = rows.shape
+    if mode == "reference_numpy":
+        _use_numpy_table(n, pblock, vblock)
     offs = np.array(offsets, dtype=np.int64)
     rc = lib().oracle_shuffle(_ptr(rows), n, r, pblock, vblock, _ptr(offs), len(offs), iterations,
                               seed & (2**64 - 1), MODES[mode])

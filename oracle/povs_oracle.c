@@ -56,7 +56,33 @@ void oracle_philox4x32_10(const uint32_t ctr_in[4], const uint32_t key_in[2], ui
 enum { DOM_OFFSET = 1, DOM_ASSIGN = 2, DOM_PERM = 3, DOM_VSEED = 4, N_FEISTEL = 12 };
 
 /* Randomness modes: 0 = uniform permutations; 1 = the reference CUDA path's distribution. */
-enum { MODE_UNIFORM = 0, MODE_REFERENCE_CUDA = 1 };
+enum { MODE_UNIFORM = 0, MODE_REFERENCE_CUDA = 1, MODE_REFERENCE_NUMPY = 2 };
+
+/*
+ * Mode 2 (the reference NumPy path's distribution): the permutation of a vblock of n valid rows
+ * under per-vblock seed s in 1..999 is numpy.random.RandomState(s).shuffle(arange(n)), taken from a
+ * table that the caller builds with NumPy itself (oracle/api.py): np_table[np_off[c] + (s-1)*n + f],
+ * class c = n/P - 1 for whole members, V + (n - n_rows % P)/P with the truncated last pblock.
+ */
+static const int32_t* np_table = NULL;
+static int64_t np_off[64];
+static int np_P = 0, np_V = 0;
+static int64_t np_trunc = 0;
+
+void oracle_set_numpy_table(const int32_t* table, const int64_t* off, int P, int V, int64_t trunc)
+{
+    np_table = table;
+    for (int i = 0; i < 2 * V && i < 64; ++i) np_off[i] = off[i];
+    np_P = P;
+    np_V = V;
+    np_trunc = trunc;
+}
+
+static const int32_t* numpy_perm(int n, uint32_t s)
+{
+    const int cls = (n % np_P) == 0 ? n / np_P - 1 : np_V + (int)((n - np_trunc) / np_P);
+    return np_table + np_off[cls] + (int64_t)(s - 1u) * n;
+}
 
 static void draw(uint64_t seed, uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, uint32_t out[4])
 {
@@ -310,7 +336,18 @@ int oracle_device_randomness(uint64_t seed, uint32_t iteration, int64_t N, int P
     int64_t starts[64];
     for (int64_t v = 0; v < n_v; ++v) {
         int nm = 0;
-        int n_valid = order_members(out_assign + v * V, V, N, P, n_p, offset, 1, starts, &nm);
+        int n_valid = order_members(out_assign + v * V, V, N, P, n_p, offset, mode == MODE_REFERENCE_NUMPY ? 0 : 1,
+                                    starts, &nm);
+        if (mode == MODE_REFERENCE_NUMPY) {
+            int32_t* pv = out_perms + v * VP;
+            if (np_table == NULL || np_P != P || np_V != V || np_trunc != N % P) {
+                free(keys);
+                return -3;
+            }
+            const int32_t* src = n_valid > 0 ? numpy_perm(n_valid, vblock_seed(seed, iteration, (uint64_t)v)) : NULL;
+            for (int f = 0; f < VP; ++f) pv[f] = f < n_valid ? src[f] : -1;
+            continue;
+        }
         if (mode == MODE_REFERENCE_CUDA) {
             int32_t* pv = out_perms + v * VP;
             xorshift_fisher_yates(vblock_seed(seed, iteration, (uint64_t)v), n_valid, pv);
@@ -349,7 +386,7 @@ int oracle_shuffle(uint8_t* data, int64_t N, int64_t R, int P, int V, const int6
     for (int it = 0; it < iterations && rc == 0; ++it) {
         int64_t offset = 0;
         rc = oracle_device_randomness(seed, (uint32_t)it, N, P, V, offsets, n_offsets, &offset, assign, perms, mode);
-        if (rc == 0) rc = oracle_apply_iteration(data, N, R, P, V, offset, assign, perms, 1);
+        if (rc == 0) rc = oracle_apply_iteration(data, N, R, P, V, offset, assign, perms, mode == MODE_REFERENCE_NUMPY ? 0 : 1);
     }
     free(assign);
     free(perms);

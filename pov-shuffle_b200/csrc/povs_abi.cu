@@ -161,6 +161,12 @@ struct CachedGraph {
     std::vector<cudaGraphNode_t> nodes;
 };
 
+// Permutation tables of the reference NumPy path's distribution for one (P, V, n_rows % P).
+struct NpTable {
+    uint16_t* dev = nullptr;
+    std::vector<int64_t> off; // 2 * MAX_VBLOCK entries, -1 where a class cannot occur
+};
+
 struct DeviceCtx {
     bool ready = false;
     int sm_count = 0;
@@ -170,6 +176,8 @@ struct DeviceCtx {
     int* status = nullptr;
     std::mutex mu; // guards the graph cache and launches that reuse it
     std::unordered_map<GraphKey, CachedGraph, GraphKeyHash> graphs;
+    std::mutex np_mu; // guards np_tables
+    std::unordered_map<uint64_t, NpTable> np_tables;
 };
 
 constexpr int MAX_DEVICES = 64;
@@ -398,6 +406,70 @@ int check_common(void* data, int64_t n_rows, int64_t row_bytes, int32_t pblock, 
     return POVS_OK;
 }
 
+// Randomness mode of a flag set (POVS_ERR_INVALID_ARGUMENT when both reference modes are asked for).
+int rng_mode_of(uint32_t flags, int32_t* mode)
+{
+    const bool cuda_rng = (flags & POVS_FLAG_REFERENCE_RNG) != 0;
+    const bool numpy_rng = (flags & POVS_FLAG_REFERENCE_NUMPY) != 0;
+    if (cuda_rng && numpy_rng)
+        return fail(POVS_ERR_INVALID_ARGUMENT, "POVS_FLAG_REFERENCE_RNG and POVS_FLAG_REFERENCE_NUMPY exclude each other");
+    *mode = cuda_rng ? povs::RNG_REFERENCE_CUDA : numpy_rng ? povs::RNG_REFERENCE_NUMPY : povs::RNG_UNIFORM;
+    return POVS_OK;
+}
+
+constexpr int64_t NP_TABLE_MAX_BYTES = int64_t{128} << 20;
+
+// For the NumPy path's distribution: numpy.random.RandomState(s).shuffle(arange(n)) for every seed
+// s in 1..999 and every valid-row count n a vblock can have (m whole pblocks, or m-1 whole ones and
+// the deck's truncated last pblock, m = 1..V), built on the host once per geometry and device and
+// kept until povs_release_v1.  Sets the launch parameters that point at it.
+int prepare_np_table(DeviceCtx& c, povs::IterParams& p)
+{
+    if (p.rng_mode != povs::RNG_REFERENCE_NUMPY) return POVS_OK;
+    const int P = p.pblock, V = p.vblock;
+    const int t = static_cast<int>(p.n_rows % P);
+    const uint64_t key = (static_cast<uint64_t>(P) << 40) | (static_cast<uint64_t>(V) << 32) | static_cast<uint32_t>(t);
+    std::lock_guard<std::mutex> lk(c.np_mu);
+    auto it = c.np_tables.find(key);
+    if (it == c.np_tables.end()) {
+        NpTable tab;
+        tab.off.assign(2 * povs::MAX_VBLOCK, -1);
+        std::vector<int> sizes(2 * V, 0);
+        int64_t total = 0;
+        for (int m = 1; m <= V; ++m) {
+            sizes[m - 1] = m * P;
+            if (t > 0) sizes[V + m - 1] = (m - 1) * P + t;
+        }
+        for (int n : sizes) total += static_cast<int64_t>(n) * 999;
+        if (total * 2 > NP_TABLE_MAX_BYTES)
+            return fail(POVS_ERR_UNSUPPORTED, "the NumPy-path permutation tables for P = %d, V = %d need %lld bytes "
+                        "(limit %lld)", P, V, static_cast<long long>(total * 2), static_cast<long long>(NP_TABLE_MAX_BYTES));
+        std::vector<uint16_t> host(static_cast<size_t>(total));
+        int64_t at = 0;
+        for (int cls = 0; cls < 2 * V; ++cls) {
+            const int n = sizes[cls];
+            if (n <= 0) continue;
+            tab.off[cls] = at;
+            for (uint32_t sd = 1; sd <= 999; ++sd) {
+                povs::numpy_legacy_shuffle(sd, n, host.data() + at);
+                at += n;
+            }
+        }
+        POVS_CUDA_TRY(cudaMalloc(&tab.dev, static_cast<size_t>(total) * sizeof(uint16_t)));
+        const cudaError_t e = cudaMemcpy(tab.dev, host.data(), static_cast<size_t>(total) * sizeof(uint16_t),
+                                         cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) {
+            cudaFree(tab.dev);
+            return cuda_fail(e, "cudaMemcpy(NumPy-path tables)");
+        }
+        it = c.np_tables.emplace(key, std::move(tab)).first;
+    }
+    p.np_table = it->second.dev;
+    p.np_trunc = t;
+    for (int i = 0; i < 2 * povs::MAX_VBLOCK; ++i) p.np_off[i] = it->second.off[i];
+    return POVS_OK;
+}
+
 int64_t sum_rows(const int64_t* shard_rows, int32_t n_shards)
 {
     int64_t n = 0;
@@ -561,11 +633,14 @@ int shuffle_on_device(void* data, int64_t n_rows, int64_t row_bytes, const int64
     base.deck_stride = deck_stride;
     base.deck_seeds = deck_seeds;
     base.seed = seed;
-    base.rng_mode = (flags & POVS_FLAG_REFERENCE_RNG) ? povs::RNG_REFERENCE_CUDA : povs::RNG_UNIFORM;
+    int r = rng_mode_of(flags, &base.rng_mode);
+    if (r != POVS_OK) return r;
+    r = prepare_np_table(c, base);
+    if (r != POVS_OK) return r;
     base.n_offsets = n_offsets;
     for (int i = 0; i < n_offsets; ++i) base.offsets[i] = offsets[i];
     Plan pl;
-    int r = plan_launch(base, c, false, pl, false, plain_loads);
+    r = plan_launch(base, c, false, pl, false, plain_loads);
     if (r != POVS_OK) return r;
     if (iterations == 0) return POVS_OK;
     std::vector<IterParams> ps(static_cast<size_t>(iterations), base);
@@ -830,6 +905,12 @@ extern "C" int povs_release_v1(void)
             if (kv.second.graph) cudaGraphDestroy(kv.second.graph);
         }
         c.graphs.clear();
+        {
+            std::lock_guard<std::mutex> lk3(c.np_mu);
+            for (auto& kv : c.np_tables)
+                if (kv.second.dev) cudaFree(kv.second.dev);
+            c.np_tables.clear();
+        }
         if (c.status) cudaFree(c.status);
         c.status = nullptr;
         c.ready = false;
@@ -1083,7 +1164,10 @@ extern "C" int povs_shuffle_shards_v1(void* const* shard_ptrs, void* const* scra
     r = set_shards(base, shard_ptrs, shard_rows, n_shards);
     if (r != POVS_OK) return r;
     base.seed = seed;
-    base.rng_mode = (flags & POVS_FLAG_REFERENCE_RNG) ? povs::RNG_REFERENCE_CUDA : povs::RNG_UNIFORM;
+    r = rng_mode_of(flags, &base.rng_mode);
+    if (r != POVS_OK) return r;
+    r = prepare_np_table(*c, base);
+    if (r != POVS_OK) return r;
     base.n_offsets = n_offsets;
     for (int i = 0; i < n_offsets; ++i) base.offsets[i] = offsets[i];
     base.push_rank = -1;
@@ -1145,7 +1229,10 @@ extern "C" int povs_shuffle_sharded_v1(void* const* shard_ptrs, void* const* scr
     r = set_shards(base, shard_ptrs, shard_rows, n_shards);
     if (r != POVS_OK) return r;
     base.seed = seed;
-    base.rng_mode = (flags & POVS_FLAG_REFERENCE_RNG) ? povs::RNG_REFERENCE_CUDA : povs::RNG_UNIFORM;
+    r = rng_mode_of(flags, &base.rng_mode);
+    if (r != POVS_OK) return r;
+    r = prepare_np_table(*c, base);
+    if (r != POVS_OK) return r;
     base.n_offsets = n_offsets;
     for (int i = 0; i < n_offsets; ++i) base.offsets[i] = offsets[i];
     if (push) {
@@ -1317,7 +1404,8 @@ extern "C" int povs_shuffle_batch_v1(void* data, int64_t n_decks, int64_t deck_s
     if (n_decks > 1 && deck_stride < n_rows * row_bytes)
         return fail(POVS_ERR_INVALID_ARGUMENT, "deck_stride (%lld) is smaller than a deck (%lld bytes)",
                     static_cast<long long>(deck_stride), static_cast<long long>(n_rows * row_bytes));
-    if ((flags & ~uint32_t{POVS_FLAG_NO_GRAPH | POVS_FLAG_SYNC | POVS_FLAG_REFERENCE_RNG | POVS_FLAG_NO_PDL}) != 0)
+    if ((flags & ~uint32_t{POVS_FLAG_NO_GRAPH | POVS_FLAG_SYNC | POVS_FLAG_REFERENCE_RNG | POVS_FLAG_NO_PDL |
+                           POVS_FLAG_REFERENCE_NUMPY}) != 0)
         return fail(POVS_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
     DeviceGuard dg;
     r = dg.enter(device);

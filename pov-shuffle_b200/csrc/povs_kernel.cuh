@@ -86,7 +86,7 @@ struct IterParams {
     uint64_t seed;
     int32_t n_offsets;
     int32_t sort_members; // injected mode: 1 = ascending, padding last (CUDA path); 0 = given order (NumPy path)
-    int32_t rng_mode;     // RNG_UNIFORM or RNG_REFERENCE_CUDA (device randomness only)
+    int32_t rng_mode;     // RNG_UNIFORM, RNG_REFERENCE_CUDA or RNG_REFERENCE_NUMPY (device randomness only)
     int64_t offset;       // injected mode: this iteration's offset
     const int64_t* assign; // injected mode: [n_vblocks][V] pblock ids, padding < 0 or >= n_pblocks
     const int32_t* perms;  // injected mode: [n_vblocks][V*P] source slot of each destination slot
@@ -113,6 +113,12 @@ struct IterParams {
     // vblock, or one column slab of it).  Unit slot f = s * vp + (slot of the s-th vblock), so the
     // unit has unit_vp = pack * vp slots; slots past a vblock's valid rows are holes.
     int32_t async_plain;     // plain-load path: asynchronous copies (whole rows, 4-byte multiples)
+    // RNG_REFERENCE_NUMPY: the permutation of a vblock of n valid rows drawing seed s (1..999) is
+    // np_table[np_off[class(n)] + (s - 1) * n + f], f < n, where class(n) = n / P - 1 for whole
+    // members and V + (n - np_trunc) / P when the deck's truncated last pblock is one of them.
+    const uint16_t* np_table;
+    int32_t np_trunc;        // n_rows % P
+    int64_t np_off[2 * MAX_VBLOCK];
     int32_t pack;
     int32_t unit_vp;
     int32_t vp_shift;        // log2(vp)
@@ -421,6 +427,24 @@ __device__ __forceinline__ void warp_make_perm_xorshift(const IterParams& p, uin
             perm[j] = t;
         }
     }
+    __syncwarp();
+}
+
+// The reference NumPy path's permutation of a vblock of n valid rows under per-vblock seed s:
+// numpy.random.RandomState(s).shuffle(arange(n)), precomputed on the host (povs_mt19937.h).
+__device__ __forceinline__ const uint16_t* np_perm(const IterParams& p, int n, uint32_t s)
+{
+    const int cls = (n & (p.pblock - 1)) == 0 ? (n >> p.pblock_shift) - 1
+                                              : p.vblock + ((n - p.np_trunc) >> p.pblock_shift);
+    return p.np_table + p.np_off[cls] + static_cast<int64_t>(s - 1u) * n;
+}
+
+__device__ __forceinline__ void warp_copy_np_perm(const IterParams& p, uint64_t seed, uint64_t vblock, int n_valid,
+                                                  uint16_t* perm, int lane)
+{
+    if (n_valid <= 0) return;
+    const uint16_t* src = np_perm(p, n_valid, vblock_seed(seed, p.iteration, vblock));
+    for (int f = lane; f < n_valid; f += 32) perm[f] = src[f];
     __syncwarp();
 }
 
@@ -915,7 +939,7 @@ __device__ __forceinline__ RingPos ring_at(uint64_t u, uint32_t n)
 template <int EPL, typename PI>
 __device__ __forceinline__ void make_packed_unit(const IterParams& p, StageMeta& m, uint16_t* perm, int64_t v0,
                                                  int n_seg, uint64_t seed, int64_t deck_offset, uintptr_t deck_shift,
-                                                 const PI& pi, bool ref_rng, int lane)
+                                                 const PI& pi, bool ref_rng, bool np_rng, int lane)
 {
     const int vshift = p.vblock_shift;
     const int seg = lane >> vshift;          // this lane's vblock within the unit
@@ -932,8 +956,11 @@ __device__ __forceinline__ void make_packed_unit(const IterParams& p, StageMeta&
         const int64_t left = p.n_rows - mem * p.pblock;
         rows = left < p.pblock ? static_cast<int>(left) : p.pblock;
     }
-    // Ascending member ids with padding last (the reference kernel's order, povs.cu:203-221).
-    const uint64_t key = valid ? static_cast<uint64_t>(mem) : ((uint64_t{1} << 63) | static_cast<uint64_t>(j));
+    // Ascending member ids with padding last (the reference kernel's order, povs.cu:203-221), or for
+    // the NumPy path's distribution the slot order with full members first, then a truncated one,
+    // then padding (numpy.py:125-136).
+    const uint64_t key = np_rng ? static_cast<uint64_t>(j) + (valid ? (rows == p.pblock ? 0u : 64u) : 128u)
+                         : valid ? static_cast<uint64_t>(mem) : ((uint64_t{1} << 63) | static_cast<uint64_t>(j));
     const int grp = seg << vshift;
     int rank = 0;
     for (int t = 0; t < p.vblock; ++t) {
@@ -957,6 +984,21 @@ __device__ __forceinline__ void make_packed_unit(const IterParams& p, StageMeta&
     const int pack_last = p.pack - 1;
     const int nv_lane = __shfl_sync(FULL_MASK, nv, min(lane, pack_last) << vshift);
     const int vpm = p.vp - 1;
+    if (np_rng) {
+        // Lane s (< n_seg) finds vblock s's precomputed permutation; every lane copies its share.
+        int64_t base = 0;
+        if (lane < n_seg && nv_lane > 0)
+            base = np_perm(p, nv_lane, vblock_seed(seed, p.iteration, static_cast<uint64_t>(v0 + lane))) - p.np_table;
+        for (int f = lane; f < p.unit_vp; f += 32) {
+            const int sf = f >> p.vp_shift;
+            const int nvf = __shfl_sync(FULL_MASK, nv_lane, sf);
+            const int64_t bf = __shfl_sync(FULL_MASK, base, sf);
+            const int fl = f & vpm;
+            perm[f] = fl < nvf ? static_cast<uint16_t>((sf << p.vp_shift) + p.np_table[bf + fl]) : HOLE;
+        }
+        __syncwarp();
+        return;
+    }
     if (ref_rng) {
         // The reference kernel's xorshift32 Fisher-Yates, one vblock per lane (povs.cu:282-321).
         for (int f = lane; f < p.unit_vp; f += 32) {
@@ -1073,6 +1115,7 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
         // Uniform mode maps all n_v*V slots (padding ids anywhere); the reference-CUDA mode maps
         // slots [0, n_p) and leaves the padding in the last slots, as the reference does.
         const bool ref_rng = p.rng_mode == RNG_REFERENCE_CUDA;
+        const bool np_rng = p.rng_mode == RNG_REFERENCE_NUMPY;
         const uint64_t domain = ref_rng ? static_cast<uint64_t>(p.n_pblocks) : static_cast<uint64_t>(p.n_vblocks) * p.vblock;
         if constexpr (!INJECTED) pi.init(p.seed, p.iteration, domain);
         // Batched decks: the randomness of the deck of the current unit.
@@ -1107,7 +1150,7 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
                     deck_shift = static_cast<uintptr_t>(d * p.deck_stride);
                 }
                 make_packed_unit<EPL>(p, sm.meta[k], sm.perm + static_cast<size_t>(k) * sm.perm_stride, v0, n_seg,
-                                      seed, deck_offset, deck_shift, pi, ref_rng, lane);
+                                      seed, deck_offset, deck_shift, pi, ref_rng, np_rng, lane);
                 __syncwarp();
                 mbar_arrive(&sm.pfull[k]); // each lane publishes its writes to the slot
             }
@@ -1191,7 +1234,7 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
             uint64_t key;
             if (lane >= p.vblock) {
                 key = ~uint64_t{0};
-            } else if (!INJECTED || p.sort_members) {
+            } else if (INJECTED ? p.sort_members != 0 : !np_rng) {
                 key = valid ? static_cast<uint64_t>(mem) : ((uint64_t{1} << 63) | static_cast<uint64_t>(lane));
             } else {
                 key = static_cast<uint64_t>(lane) + (valid ? (rows == p.pblock ? 0u : 64u) : 128u);
@@ -1231,8 +1274,11 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
                 const int own_rows = __shfl_sync(FULL_MASK, rows, own_lane);
                 const int first = own_rank << p.pblock_shift;
                 uint16_t* pos = sm.pos + static_cast<size_t>(k) * sm.pos_stride;
-                if (ref_rng) {
-                    warp_make_perm_xorshift(p, seed, static_cast<uint64_t>(v), n_valid, perm, lane);
+                if (ref_rng || np_rng) {
+                    if (ref_rng)
+                        warp_make_perm_xorshift(p, seed, static_cast<uint64_t>(v), n_valid, perm, lane);
+                    else
+                        warp_copy_np_perm(p, seed, static_cast<uint64_t>(v), n_valid, perm, lane);
                     for (int f = lane; f < n_valid; f += 32) {
                         const int e = static_cast<int>(perm[f]) - first;
                         if (e >= 0 && e < own_rows) pos[e] = static_cast<uint16_t>(f);
@@ -1243,6 +1289,8 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
             } else {
                 if (ref_rng)
                     warp_make_perm_xorshift(p, seed, static_cast<uint64_t>(v), n_valid, perm, lane);
+                else if (np_rng)
+                    warp_copy_np_perm(p, seed, static_cast<uint64_t>(v), n_valid, perm, lane);
                 else
                     warp_make_perm<EPL>(p, seed, static_cast<uint64_t>(v), n_valid, perm, lane);
             }

@@ -46,6 +46,8 @@ enum : int {
     RNG_UNIFORM = 0,        // uniform per-vblock permutations (sorted Philox keys), padding anywhere
     RNG_REFERENCE_CUDA = 1, // the reference CUDA path's distribution: per-vblock seeds 1..999,
                             // xorshift32 forward Fisher-Yates, padding in the last vblock
+    RNG_REFERENCE_NUMPY = 2, // the reference NumPy path's distribution: padding anywhere, members in
+                             // slot order, per-vblock seeds 1..999 and RandomState(seed).shuffle
 };
 
 constexpr int FEISTEL_ROUNDS = 12;

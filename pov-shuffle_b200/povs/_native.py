@@ -25,6 +25,7 @@ FLAG_NO_GRAPH = 1
 FLAG_SYNC = 2
 FLAG_REFERENCE_RNG = 4
 FLAG_NO_PDL = 8
+FLAG_REFERENCE_NUMPY = 16
 
 # (name, restype, argtypes) of every exported symbol declared in include/povs.h.
 _c_i32, _c_i64, _c_u32, _c_u64, _c_vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_void_p

@@ -40,10 +40,11 @@ def get_build_params() -> BuildParams:
 def get_int_seed(seed: int | np.random.Generator | torch.Generator | None, options: Options | None = None) -> int:
     """Normalise a seed: ints pass through, generators (or None -> fresh entropy) draw one integer,
     from [1, 2**63 - 1), or from the reference's [1, 1000) (common.py:29-42 there) when ``options``
-    ask for ``randomness="reference_cuda"``."""
+    ask for one of the reference's distributions (``randomness="reference_cuda"`` or
+    ``"reference_numpy"``)."""
     if isinstance(seed, (int, np.integer)) and not isinstance(seed, bool):
         return int(seed)
-    high = REFERENCE_MAX_SEED if options is not None and options.randomness == "reference_cuda" else MAX_SEED
+    high = REFERENCE_MAX_SEED if options is not None and options.randomness in REFERENCE_MODES else MAX_SEED
     if seed is None:
         seed = np.random.default_rng()
     if isinstance(seed, np.random.Generator):
@@ -58,14 +59,15 @@ def seed_to_u64(seed: int) -> int:
     return int(seed) & 0xFFFF_FFFF_FFFF_FFFF
 
 
-RANDOMNESS_MODES = ("uniform", "reference_cuda")
+RANDOMNESS_MODES = ("uniform", "reference_cuda", "reference_numpy")
+REFERENCE_MODES = ("reference_cuda", "reference_numpy")
 
 
 def randomness_flags(options: Options) -> int:
     """Native flags selecting the randomness mode of ``options`` (AssertionError if unknown)."""
     mode = options.randomness or "uniform"
     assert mode in RANDOMNESS_MODES, f"randomness ({mode!r}) must be one of {RANDOMNESS_MODES}"
-    return 4 if mode == "reference_cuda" else 0
+    return {"uniform": 0, "reference_cuda": 4, "reference_numpy": 16}[mode]
 
 
 def get_dtype_bytes(dataset: np.ndarray | torch.Tensor) -> int:

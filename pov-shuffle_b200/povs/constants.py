@@ -5,8 +5,8 @@ Values that differ from the reference, and why:
     [1, 2**63 - 1) instead of [1, 1000).  The reference narrowed it so that its 32-bit per-vblock
     seeds matched between CPU and CUDA (constants.py:1-4 there); the device RNG here is keyed
     by the full 64-bit seed, so a generator no longer collapses to 999 distinct shuffles.  With
-    ``randomness="reference_cuda"`` (the reference's distribution) a generator draws from the
-    reference's [1, 1000) again (``REFERENCE_MAX_SEED``).
+    ``randomness="reference_cuda"`` or ``"reference_numpy"`` (the reference's distributions) a
+    generator draws from the reference's [1, 1000) again (``REFERENCE_MAX_SEED``).
   * ``MIN_PBLOCK_SIZE`` is 8 (the reference has 16).  With 8-bit instances and P = 8 the offset
     chooser still finds the two offsets [0, 4], which is the invariant the reference's bound
     protects; P = 8 is needed by the bias suite (deck 1000, V = 2, P = 8).

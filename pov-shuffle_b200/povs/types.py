@@ -28,10 +28,12 @@ class Options(NamedTuple):
     :param physical_block_size: Physical block size, in number of instances.
     :param offsets: List of valid offsets to sample at random in each shuffling iteration, in number of instances.
     :param gpu_thread_block_size: Accepted for compatibility; the B200 kernels size their launch themselves.
-    :param randomness: ``"uniform"`` (default: uniformly random permutation of every virtual block) or
+    :param randomness: ``"uniform"`` (default: uniformly random permutation of every virtual block),
                        ``"reference_cuda"`` (the reference CUDA implementation's distribution: per-block seeds
-                       1..999 and an xorshift32 Fisher-Yates, padding in the last virtual block), for
-                       statistical comparisons with it.  Not part of the reference's options.
+                       1..999 and an xorshift32 Fisher-Yates, padding in the last virtual block) or
+                       ``"reference_numpy"`` (the reference NumPy implementation's distribution: padding
+                       anywhere, per-block seeds 1..999 and ``numpy.random.RandomState(seed).shuffle``), for
+                       statistical comparisons with them.  Not part of the reference's options.
     """
 
     virtual_block_size: int | None = None

@@ -13,7 +13,9 @@ shuffled deck is the episode.  Statistics (positional TVD, bigram TVD) for:
 * ``library``       - the library's device randomness through the oracle port; the GPU run must
                          reproduce these episodes exactly;
 * ``library_reference_cuda`` - the same with ``randomness="reference_cuda"`` (the reference CUDA
-                         path's distribution drawn on the device).
+                         path's distribution drawn on the device);
+* ``library_reference_numpy`` - the same with ``randomness="reference_numpy"`` (the reference NumPy
+                         path's distribution: its 999 seeded RandomState permutations).
 
 Pass ``--reuse`` to keep the ``reference_numpy`` statistics already in the file (they take minutes).
 
@@ -99,6 +101,7 @@ def main(reference_root: str, n_episodes: int = 3000, reuse: bool = False) -> No
     sets = {
         "library": oracle_episodes(n_episodes, "library"),
         "library_reference_cuda": oracle_episodes(n_episodes, "library", "reference_cuda"),
+        "library_reference_numpy": oracle_episodes(n_episodes, "library", "reference_numpy"),
         "reference_cuda": oracle_episodes(n_episodes, "reference_cuda"),
     }
     previous = json.loads(OUT.read_text()) if (reuse and OUT.exists()) else {}
@@ -118,7 +121,7 @@ def main(reference_root: str, n_episodes: int = 3000, reuse: bool = False) -> No
         base[s] = a
     result["numpy_shuffle"] = {"positional_tvd": metrics.positional_tvd(base), "bigram_tvd": metrics.bigram_tvd(base)}
     # Checksums of the library's episodes, so the GPU run can be compared exactly.
-    for key in ("library", "library_reference_cuda"):
+    for key in ("library", "library_reference_cuda", "library_reference_numpy"):
         tb = sets[key].astype(np.int64)
         result[f"{key}_checksums"] = [
             int((tb[i] * np.arange(1, N_ROWS + 1)).sum() % (2**61 - 1)) for i in range(len(ITERATIONS))

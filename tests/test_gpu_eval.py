@@ -39,7 +39,7 @@ def _bytes_deck(n_decks: int, n_rows: int, row_bytes: int, seed: int) -> torch.T
         (300, 50, 4, 8, 2, [0, 1, 2], 5),
     ],
 )
-@pytest.mark.parametrize("randomness", ["uniform", "reference_cuda"])
+@pytest.mark.parametrize("randomness", ["uniform", "reference_cuda", "reference_numpy"])
 def test_batch_equals_one_deck_at_a_time(n_decks, n_rows, row_bytes, P, V, offsets, iterations, randomness):
     decks = _bytes_deck(n_decks, n_rows, row_bytes, seed=n_decks)
     single = decks.clone()

@@ -58,7 +58,7 @@ def _worker(rank: int, world: int, port: int, out_dir: str, randomness: str, dou
 
 
 CASES = [("uniform", False), ("uniform", True), ("reference_cuda", False), ("reference_cuda", True),
-         ("uniform", None)]
+         ("uniform", None), ("reference_numpy", True)]
 
 
 @pytest.mark.parametrize("randomness,double_buffer", CASES)

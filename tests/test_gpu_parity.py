@@ -91,11 +91,12 @@ PACKED_CASES = [
 
 
 @pytest.mark.parametrize("n_decks,n_rows,row_bytes,P,V,offsets,iterations", PACKED_CASES)
-@pytest.mark.parametrize("randomness", ["uniform", "reference_cuda"])
+@pytest.mark.parametrize("randomness", ["uniform", "reference_cuda", "reference_numpy"])
 def test_packed_units_match_single_vblock_units_and_oracle(oracle_api, n_decks, n_rows, row_bytes, P, V, offsets,
                                                           iterations, randomness):
     """Small vblocks travel several per unit; the shuffle is the one-vblock-per-unit plan's and the oracle's."""
-    flags = _native.FLAG_REFERENCE_RNG if randomness == "reference_cuda" else 0
+    flags = {"uniform": 0, "reference_cuda": _native.FLAG_REFERENCE_RNG,
+             "reference_numpy": _native.FLAG_REFERENCE_NUMPY}[randomness]
     host = np.random.default_rng(n_rows + row_bytes).integers(0, 256, size=(n_decks, n_rows, row_bytes), dtype=np.uint8)
     seeds = torch.arange(7, 7 + n_decks, dtype=torch.int64, device=DEV)
     results = []
@@ -119,6 +120,28 @@ def test_packed_units_match_single_vblock_units_and_oracle(oracle_api, n_decks, 
         want = host[d].copy()
         oracle_api.shuffle(want, iterations, P, V, offsets, 7 + d, randomness)
         assert np.array_equal(results[0][d], want), f"deck {d}"
+
+
+@pytest.mark.parametrize(
+    "n_rows,row_bytes,P,V,offsets,iterations",
+    [(1000, 64, 8, 2, list(range(8)), 4), (4099, 256, 32, 4, [0, 1, 2, 5], 3), (20_003, 12, 16, 8, [0, 1, 3], 2),
+     (3001, 8, 64, 4, [0, 1, 5], 2), (1200, 12288, 16, 2, [0, 1, 2], 2), (777, 2, 16, 8, [0, 1, 2], 3)],
+)
+def test_reference_numpy_randomness_mode_matches_oracle(oracle_api, n_rows, row_bytes, P, V, offsets, iterations):
+    """randomness="reference_numpy": the library's tables (host MT19937 restatement) against the oracle
+    fed tables made by numpy.random.RandomState itself; packed and unpacked units, column slabs,
+    truncated last pblocks."""
+    host = random_rows(n_rows, row_bytes, seed=13)
+    got = gpu_shuffle_bytes(host, P, V, offsets, iterations, 91, flags=_native.FLAG_REFERENCE_NUMPY)
+    want = host.copy()
+    oracle_api.shuffle(want, iterations, P, V, offsets, 91, "reference_numpy")
+    assert np.array_equal(got, want)
+
+
+def test_reference_modes_exclude_each_other():
+    deck = torch.zeros((1000, 16), dtype=torch.uint8, device=DEV)
+    with pytest.raises(RuntimeError, match="exclude each other"):
+        _native.shuffle_device(deck, 16, [0, 1], 1, 8, 2, 1, _native.FLAG_REFERENCE_RNG | _native.FLAG_REFERENCE_NUMPY)
 
 
 @pytest.mark.parametrize("row_bytes", [4, 64, 256])
@@ -502,7 +525,7 @@ def test_full_size_decks_match_oracle_byte_for_byte(oracle_api, name, n_rows, el
         ([1 << 15] * 8, 128, 64, 4, list(range(16)), 2),
     ],
 )
-@pytest.mark.parametrize("randomness", ["uniform", "reference_cuda"])
+@pytest.mark.parametrize("randomness", ["uniform", "reference_cuda", "reference_numpy"])
 @pytest.mark.parametrize("double_buffer", [False, True])
 def test_shards_match_the_concatenated_deck(oracle_api, rows, row_bytes, P, V, offsets, iterations, randomness,
                                             double_buffer):
