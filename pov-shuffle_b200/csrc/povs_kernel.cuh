@@ -41,6 +41,16 @@
 
 #include "povs_rng.cuh"
 
+// Cache-hint variants of the data path, off: on B200 both were slower (32 GiB bf16 and 256 MiB fp16
+// decks, same box: streaming stores -7 to -10 %, evict-first bulk loads about -1 %; neutral on 12 KiB
+// and 64-byte rows).
+#ifndef POVS_LOAD_EVICT_FIRST
+#define POVS_LOAD_EVICT_FIRST 0
+#endif
+#ifndef POVS_STREAM_STORES
+#define POVS_STREAM_STORES 0
+#endif
+
 namespace povs {
 
 constexpr int MAX_INLINE_OFFSETS = 256;
@@ -186,10 +196,33 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 
 __device__ __forceinline__ void bulk_load(void* dst_smem, const void* src_gmem, uint32_t bytes, uint64_t* bar)
 {
+#if POVS_LOAD_EVICT_FIRST
+    uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_addr(dst_smem)),
+        "l"(src_gmem), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+#else
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                      smem_addr(dst_smem)),
                  "l"(src_gmem), "r"(bytes), "r"(smem_addr(bar))
                  : "memory");
+#endif
+}
+
+// Row stores of the write-back pass (POVS_STREAM_STORES: streaming cache hint).
+template <typename T>
+__device__ __forceinline__ void store_row_chunk(T* dst, const T& v)
+{
+#if POVS_STREAM_STORES
+    if constexpr (sizeof(T) == 16) {
+        __stcs(reinterpret_cast<uint4*>(dst), *reinterpret_cast<const uint4*>(&v));
+        return;
+    }
+#endif
+    *dst = v;
 }
 
 // Per-thread asynchronous copies global -> shared of 4 or 8 bytes (both addresses aligned to the
@@ -731,7 +764,7 @@ __device__ __forceinline__ void store_share_div(const IterParams& p, const Stage
             const T* src = reinterpret_cast<const T*>(stage + static_cast<size_t>(src_row(f)) * p.slab_bytes);
             T* dst = reinterpret_cast<T*>(slot_ptr(m, dst_slot(f), p.pblock_shift, pmask, p.row_bytes) + col);
 #pragma unroll 4
-            for (int q = lane; q < cpr; q += 32) dst[q] = src[q];
+            for (int q = lane; q < cpr; q += 32) store_row_chunk(dst + q, src[q]);
         }
     } else {
         const int g = 32 / cpr;
@@ -754,7 +787,7 @@ __device__ __forceinline__ void store_share_div(const IterParams& p, const Stage
             }
 #pragma unroll
             for (int u = 0; u < U; ++u)
-                if (ok[u]) *dst[u] = v[u];
+                if (ok[u]) store_row_chunk(dst[u], v[u]);
         }
         for (; t < n_pass; t += n_warps) {
             const int f = t * g + lrow;
@@ -794,7 +827,7 @@ __device__ __forceinline__ void store_share(const IterParams& p, const StageMeta
             const T* src = reinterpret_cast<const T*>(stage + static_cast<size_t>(src_row(f)) * p.slab_bytes);
             T* dst = reinterpret_cast<T*>(slot_ptr(m, dst_slot(f), p.pblock_shift, pmask, p.row_bytes) + col);
 #pragma unroll 4
-            for (int q = lane; q < cpr; q += 32) dst[q] = src[q];
+            for (int q = lane; q < cpr; q += 32) store_row_chunk(dst + q, src[q]);
         }
     } else {
         const int g = lg.g, lrow = lg.lrow, lq = lg.lq;
@@ -822,7 +855,7 @@ __device__ __forceinline__ void store_share(const IterParams& p, const StageMeta
             }
 #pragma unroll
             for (int u = 0; u < U; ++u)
-                if (ok[u]) *dst[u] = v[u];
+                if (ok[u]) store_row_chunk(dst[u], v[u]);
         }
         for (; t < n_pass; t += n_warps) {
             const int f = t * g + lrow;
