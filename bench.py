@@ -68,6 +68,11 @@ WORKLOADS = {
         desc="int32 deck 33,554,432 x 16 (64-byte rows and V=2, P=8 of the bias suite, 2 GiB), uniform bytes "
         "from seed 4, iterations=4",
     ),
+    "f32x4_2GiB": dict(
+        rows=134_217_728, shape=(4,), dtype="float32", iterations=4, V=2, P=64, seed=5, init="bytes",
+        desc="fp32 deck 134,217,728 x 4 (16-byte rows with the reference chooser's V=2, P=64, 2 GiB), uniform "
+        "bytes from seed 5, iterations=4",
+    ),
     "u8_12KiB": dict(
         rows=1_000_000, shape=(3, 64, 64), dtype="uint8", iterations=3, V=2, P=16, seed=2, init="bytes",
         desc="uint8 deck 1,000,000 x 3x64x64 (12,288 B rows, 12.3 GB), uniform 0..255 from seed 2, iterations=3, V=2, P=16",
@@ -381,26 +386,28 @@ def run_e2e(args, w, deck, opts, offsets, iters, world, rank, local, stream, sha
     total_bytes = w["rows"] * row_bytes_of(w)
     # One GPU: three host decks in rotation through three device buffers keep both PCIe directions
     # busy (a deck's copy in never waits for its own previous copy out); two when host memory is short.
+    # Several ranks: two sharded decks per rank (the resident one and a second of the same split),
+    # so that one deck's copies in overlap the other's shuffle and copy out.
     avail = psutil.virtual_memory().available
-    n_host = (3 if avail >= 3.5 * total_bytes else 2) if world == 1 else 1
-    if world == 1:
-        # The extra device buffers must fit next to the resident deck.
-        free_dev, _ = torch.cuda.mem_get_info(deck.device)
-        while n_host > 1 and (n_host - 1) * shard_bytes + (2 << 30) > free_dev:
-            n_host -= 1
-    # Decide once (rank 0, before anything is pinned) so that every rank takes the same steps.
-    ok = torch.tensor([1 if avail >= (n_host + 0.5) * total_bytes else 0], device=deck.device)
+    n_host = 3 if world == 1 and avail >= 3.5 * total_bytes else 2
+    free_dev, _ = torch.cuda.mem_get_info(deck.device)
+    # The extra device buffers must fit next to the resident deck (and its scratch buffer).
+    per_buffer = shard_bytes * (2 if world > 1 and sharded.double_buffer else 1)
+    while n_host > 1 and (n_host - 1) * per_buffer + (2 << 30) > free_dev:
+        n_host -= 1
+    # Decide together, before anything is pinned, so that every rank takes the same steps.
+    ok = torch.tensor([1 if avail >= (n_host + 0.5) * total_bytes else 0, n_host], device=deck.device)
     if world > 1:
-        dist.broadcast(ok, src=0)
-    if not int(ok.item()):
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if not int(ok[0].item()):
         return {"value": None, "unit": "GB/s", "skipped": "not enough host memory for pinned copies of the deck"}
+    n_host = int(ok[1].item())
     flat = deck.view(torch.uint8).reshape(-1)
     hosts = []
     for _ in range(n_host):
         h = torch.empty(shard_bytes, dtype=torch.uint8, pin_memory=True)
         h.copy_(flat)
         hosts.append(h)
-    host = hosts[0]
     R = row_bytes_of(w)
     P, V = w["P"], w["V"]
     e2e_steps = max(2, args.e2e_steps)
@@ -415,13 +422,15 @@ def run_e2e(args, w, deck, opts, offsets, iters, world, rank, local, stream, sha
         path = (f"povs_shuffle_host_batch_v1 (povs.shuffle_many): {n_host} pinned host decks in rotation, "
                 f"{n_host} device buffers")
     else:
+        decks = [sharded] + [povs.ShardedDeck(torch.empty_like(deck), double_buffer=sharded.double_buffer)
+                             for _ in range(n_host - 1)]
+        host_shards = [h.view(deck.dtype).view(deck.shape) for h in hosts]
+
         def run_steps(n: int, seed: int) -> None:
-            for k in range(n):
-                flat.copy_(host, non_blocking=True)
-                sharded.shuffle(iterations=iters, options=opts, seed=seed + k)
-                host.copy_(flat, non_blocking=True)
-                torch.cuda.current_stream().synchronize()
-        path = "per rank: pinned host shard -> ShardedDeck.shuffle -> host"
+            povs.shuffle_host_shards(decks, [host_shards[k % n_host] for k in range(n)], iterations=iters,
+                                     options=opts, seed=seed)
+        path = (f"povs.shuffle_host_shards per rank: {n_host} pinned host shards in rotation through {n_host} "
+                f"sharded decks, copies on their own streams")
 
     run_steps(2, 7)
     if world > 1:
@@ -437,6 +446,9 @@ def run_e2e(args, w, deck, opts, offsets, iters, world, rank, local, stream, sha
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e_ms = float(t.item())
     povs.check_device_status(deck.device)
+    if world > 1:
+        for d in decks[1:]:
+            d.close()
     return {
         "value": round(2 * total_bytes * iters / (e_ms / e2e_steps / 1e3) / 1e9, 3),
         "unit": "GB/s",

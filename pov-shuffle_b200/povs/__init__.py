@@ -4,8 +4,9 @@ Public API kept from the reference: ``shuffle``, ``Options``, ``BuildParams``, `
 ``optim_options_for_dataset``.  Additions: ``apply_randomness`` (inject offsets, block assignments
 and per-vblock permutations, for bit-exact comparison with other implementations),
 ``check_device_status``, decks split into shards: ``shuffle_shards`` (one process) and
-``ShardedDeck`` (one process per GPU), many host decks streamed through the GPU (``shuffle_many``)
-and many independent CUDA decks shuffled together (``shuffle_batch``).  ``povs.eval`` holds the
+``ShardedDeck`` (one process per GPU, host shards streamed through it by ``shuffle_host_shards``),
+many host decks streamed through the GPU (``shuffle_many``) and many independent CUDA decks
+shuffled together (``shuffle_batch``).  ``povs.eval`` holds the
 shuffle-bias metrics and exercises on the GPU.
 """
 
@@ -19,7 +20,7 @@ import torch as t
 from . import numpy as povs_numpy
 from . import torch as povs_torch
 from .common import get_build_params, get_int_seed
-from .distributed import ShardedDeck, shuffle_shards
+from .distributed import ShardedDeck, shuffle_host_shards, shuffle_shards
 from .injection import apply_randomness
 from .types import BuildParams, Options
 
@@ -32,6 +33,7 @@ __all__ = [
     "apply_randomness",
     "check_device_status",
     "shuffle_shards",
+    "shuffle_host_shards",
     "ShardedDeck",
     "shuffle_many",
     "shuffle_batch",

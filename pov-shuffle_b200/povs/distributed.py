@@ -221,6 +221,11 @@ class ShardedDeck:
         opts = self.options(options)
         validate(self.n_rows, self.instance_size, self.dtype_bytes, iterations, opts, self.shard_rows)
         seed_u64 = self.broadcast_seed(seed, opts)
+        self.run(seed_u64, iterations, opts, flags)
+
+    def run(self, seed_u64: int, iterations: int, opts: Options, flags: int = 0) -> None:
+        """The iterations with a seed every rank already holds (no collective; every rank must call with
+        the same arguments), on the current stream."""
         if self.row_bytes == 0:
             return
         self.native.shuffle_sharded(
@@ -239,3 +244,75 @@ class ShardedDeck:
         for base in self._mapped:
             self.native.ipc_close(base, self.device.index if self.device.type == "cuda" else -1)
         self._mapped = []
+
+
+def shuffle_host_shards(decks: list[ShardedDeck], host_shards: list[torch.Tensor], iterations: int = 1,
+                        options: Options | None = None, seed: int | Any | None = None) -> None:
+    """Collective: stream this rank's host shards of several decks through sharded GPU buffers.
+
+    Host shard ``k`` (a CPU tensor shaped like the decks' shards; pin it for overlap) is copied into
+    ``decks[k % len(decks)]``, shuffled as that deck with seed ``s + k`` (``s`` is rank 0's seed), and
+    copied back in place, on three streams ordered by events: deck k+1's copy in overlaps deck k's
+    iterations and copy out, so each GPU's PCIe link carries both directions at once.  A host shard
+    listed twice is shuffled twice in order.  Every rank calls with the same number of host shards,
+    iterations and options; the seed is broadcast once (the only collective), and each deck's first
+    device barrier orders a shuffle after every rank's copy in, which itself waits for that buffer's
+    previous copy out.  Returns when every host shard is back.  Addition to the reference API (the
+    sharded counterpart of ``povs.shuffle_many``).
+    """
+    assert decks and host_shards is not None, "at least one deck is required"
+    d0 = decks[0]
+    for d in decks:
+        assert d.shard.shape == d0.shard.shape and d.shard.dtype == d0.shard.dtype and d.device == d0.device, \
+            "the decks must have the same shard shape, dtype and device"
+        assert d.shard_rows == d0.shard_rows, "the decks must be split the same way"
+    for h in host_shards:
+        assert isinstance(h, torch.Tensor) and not h.is_cuda and h.is_contiguous(), "host shards must be contiguous CPU tensors"
+        assert h.shape == d0.shard.shape and h.dtype == d0.shard.dtype, "host shards must be shaped like the decks' shards"
+    opts = d0.options(options)
+    validate(d0.n_rows, d0.instance_size, d0.dtype_bytes, iterations, opts, d0.shard_rows)
+    base = d0.broadcast_seed(seed, opts)
+    if not host_shards:
+        return
+    nd = len(decks)
+    dev = d0.device
+    if dev.type != "cuda":
+        # Decks in host memory (the native layer's own checks then decide): one step after another.
+        for k, h in enumerate(host_shards):
+            deck = decks[k % nd]
+            deck.shard.copy_(h)
+            deck.run((base + k) & 0xFFFF_FFFF_FFFF_FFFF, iterations, opts)
+            h.copy_(deck.shard)
+        return
+    caller = torch.cuda.current_stream(dev)
+    s_in, s_cmp, s_out = (torch.cuda.Stream(dev) for _ in range(3))
+    for st in (s_in, s_cmp, s_out):
+        st.wait_stream(caller)
+    out_done: list[torch.cuda.Event] = []
+    last_use: dict[int, int] = {}
+    for k, h in enumerate(host_shards):
+        deck = decks[k % nd]
+        with torch.cuda.stream(s_in):
+            if k >= nd:
+                s_in.wait_event(out_done[k - nd])
+            prev = last_use.get(h.data_ptr())
+            if prev is not None:
+                s_in.wait_event(out_done[prev])
+            last_use[h.data_ptr()] = k
+            deck.shard.copy_(h, non_blocking=True)
+            in_done = torch.cuda.Event()
+            in_done.record(s_in)
+        with torch.cuda.stream(s_cmp):
+            s_cmp.wait_event(in_done)
+            deck.run((base + k) & 0xFFFF_FFFF_FFFF_FFFF, iterations, opts)
+            cmp_done = torch.cuda.Event()
+            cmp_done.record(s_cmp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(cmp_done)
+            h.copy_(deck.shard, non_blocking=True)
+            done = torch.cuda.Event()
+            done.record(s_out)
+            out_done.append(done)
+    for st in (s_in, s_cmp, s_out):
+        caller.wait_stream(st)
+    caller.synchronize()

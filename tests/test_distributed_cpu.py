@@ -63,6 +63,11 @@ def _worker(rank: int, world: int, port: int, out_dir: str):
         errors.append(str(e))
     in_place = ShardedDeck(shard, native=RecordingNative(), double_buffer=False)
     errors.append(f"in_place scratch={in_place.scratch_ptrs}")
+    # Host shards through two decks: one seed broadcast, step k uses rank 0's seed + k on deck k % 2.
+    streamed = [ShardedDeck(torch.zeros_like(shard), native=RecordingNative(), double_buffer=False) for _ in range(2)]
+    hosts = [torch.full_like(shard, float(d)) for d in range(3)]
+    povs.shuffle_host_shards(streamed, hosts, iterations=2, options=opts, seed=40 if rank == 0 else 1)
+    host_calls = [[(c[1][8], c[1][10]) for c in d.native.calls if c[0] == "shuffle"] for d in streamed]
     calls = [c for c in native.calls if c[0] == "shuffle"]
     result = {
         "shard_rows": deck.shard_rows,
@@ -74,6 +79,7 @@ def _worker(rank: int, world: int, port: int, out_dir: str):
         "scratch": [c[2] for c in calls],
         "errors": errors,
         "closed": len([c for c in native.calls if c[0] == "close"]),
+        "host_calls": host_calls,
     }
     torch.save(result, os.path.join(out_dir, f"rank{rank}.pt"))
     dist.destroy_process_group()
@@ -93,4 +99,6 @@ def test_two_rank_control_plane(tmp_path):
         assert "same double_buffer" in res["errors"][1] and res["errors"][2] == "in_place scratch=None"
         assert res["closed"] == 3, "shard, barrier flags and scratch of the one peer are unmapped"
         assert len(res["scratch"]) == 2 and all(len(p) == 2 for p in res["scratch"])
+        assert res["host_calls"] == [[(40, 0), (42, 3)], [(41, 0)]], \
+            "host shard k: rank 0's seed + k on deck k % 2, each deck's epochs advancing on their own"
     assert r0["shard_ptrs"][1] == 1000 + 1 and r1["shard_ptrs"][0] == 1000 + 0

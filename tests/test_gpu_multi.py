@@ -78,6 +78,54 @@ def test_sharded_deck_matches_oracle(oracle_api, tmp_path, randomness, double_bu
     assert np.array_equal(got, want)
 
 
+def _host_worker(rank: int, world: int, port: int, out_dir: str, randomness: str, double_buffer: bool):
+    sys.path[:0] = [str(REPO), str(REPO / "pov-shuffle_b200")]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    import povs
+
+    rows = _split(world)
+    start = sum(rows[:rank])
+    decks = [povs.ShardedDeck(torch.empty((rows[rank], ROW_BYTES), dtype=torch.uint8, device=f"cuda:{rank}"),
+                              double_buffer=double_buffer) for _ in range(2)]
+    hosts = [torch.from_numpy(_host_deck(d)[start:start + rows[rank]].copy()).pin_memory() for d in range(3)]
+    opts = povs.Options(V, P, OFFSETS, 64, randomness)
+    # Host shard 0 goes through twice (steps 0 and 3), the others once; three steps share two decks.
+    povs.shuffle_host_shards(decks, [hosts[0], hosts[1], hosts[2], hosts[0]], iterations=ITERATIONS,
+                             options=opts, seed=SEED if rank == 0 else 999)
+    povs.check_device_status(rank)
+    for d in range(3):
+        np.save(os.path.join(out_dir, f"host{d}_rank{rank}.npy"), hosts[d].numpy())
+    for deck in decks:
+        deck.close()
+    dist.destroy_process_group()
+
+
+def _host_deck(d: int) -> np.ndarray:
+    return np.random.default_rng(100 + d).integers(0, 256, size=(N_ROWS, ROW_BYTES), dtype=np.uint8)
+
+
+@pytest.mark.parametrize("randomness,double_buffer", [("uniform", True), ("reference_cuda", False)])
+def test_host_shards_streamed_through_two_sharded_decks(oracle_api, tmp_path, randomness, double_buffer):
+    """povs.shuffle_host_shards: step k shuffles its host shard with seed SEED + k; a host shard listed
+    twice is shuffled twice in order; every host deck ends as the oracle's shuffle of it."""
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
+        pytest.skip("needs at least two GPUs")
+    port = 33500 + (os.getpid() % 2000) + (11 if double_buffer else 0)
+    mp.start_processes(_host_worker, args=(world, port, str(tmp_path), randomness, double_buffer), nprocs=world,
+                       start_method="spawn", join=True)
+    steps = {0: [0, 3], 1: [1], 2: [2]}
+    for d, ks in steps.items():
+        got = np.concatenate([np.load(tmp_path / f"host{d}_rank{r}.npy") for r in range(world)])
+        want = _host_deck(d)
+        for k in ks:
+            oracle_api.shuffle(want, ITERATIONS, P, V, OFFSETS, SEED + k, randomness)
+        assert np.array_equal(got, want), f"host deck {d}"
+
+
 @pytest.mark.parametrize("double_buffer", [False, True])
 def test_one_process_shards_on_two_gpus(oracle_api, double_buffer):
     """One process, shards on GPUs 0 and 1 (and their scratch buffers): the kernels on GPU 0 reach GPU 1's
