@@ -281,105 +281,112 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* s
 }
 
 // ---------------------------------------------------------------------------------------------
-// Register bitonic sort over one warp: n = 32 * EPL values (T = uint32_t), lane l owns elements
-// l*EPL .. l*EPL+EPL-1.  Ascending.  For distances j >= EPL the partner is in lane l ^ (j/EPL)
-// at the same register; the direction bits of the element index then depend on the lane only.
+// Register sorting networks over one warp: n = 32 * EPL values (T = uint32_t), lane l owns
+// elements l*EPL .. l*EPL+EPL-1.  Ascending.
 // ---------------------------------------------------------------------------------------------
 
-// Compare-exchange of registers r and r|j inside one lane (ascending when `up`).
+// Ascending compare-exchange of registers r < s: the smaller key goes to r.
 template <int EPL, typename T>
-__device__ __forceinline__ void cx_regs(T (&x)[EPL], int r, int j, bool up)
+__device__ __forceinline__ void cx_asc(T (&x)[EPL], int r, int s)
 {
-    const T a = x[r], b = x[r | j];
-    const T lo = min(a, b), hi = max(a, b);
-    x[r] = up ? lo : hi;
-    x[r | j] = up ? hi : lo;
+    const T a = x[r], b = x[s];
+    x[r] = min(a, b);
+    x[s] = max(a, b);
 }
 
+// Sorts every aligned block of `seg` elements ascending (seg a power of two, 2 <= seg <= 32 * EPL);
+// element e = lane * EPL + r is register r of lane `lane`, and elements of different blocks are
+// never compared.  Bitonic merging in the form whose comparators all point one way (Batcher's
+// network with the first stage of every merge mirrored): phase k = 2, 4, .., seg compares element
+// e with e ^ (k - 1), its mirror image inside its block of k (which merges two ascending halves
+// without reversing one of them), then with e ^ j for j = k/4, .., 1, always keeping the smaller
+// key at the lower index.  Inside a lane every comparator is a fixed register pair (a min and a
+// max); across lanes a stage is one shuffle per register.  The keys are distinct, so the order
+// equals that of any other correct sort.
 template <int EPL, typename T>
-__device__ __forceinline__ void warp_bitonic_sort(T (&x)[EPL], int lane)
+__device__ __forceinline__ void warp_sort_blocks(T (&x)[EPL], int lane, int seg)
 {
-    const int base = lane * EPL; // element index of register 0 (its low log2(EPL) bits are zero)
-    // Phases k = 2 .. EPL sort within each lane's registers (compile-time network).
-#pragma unroll
-    for (int k = 2; k <= EPL; k <<= 1) {
-#pragma unroll
-        for (int j = k >> 1; j > 0; j >>= 1) {
-#pragma unroll
-            for (int r = 0; r < EPL; ++r) {
-                if ((r & j) == 0) {
-                    const bool up = (k == EPL) ? ((base & k) == 0) : ((r & k) == 0);
-                    cx_regs<EPL, T>(x, r, j, up);
-                }
-            }
-        }
-    }
-    // Phases k = 2*EPL .. 32*EPL: a runtime loop, so the code stays small for large EPL.  Distances
-    // j >= EPL pair register r with the same register of lane ^ (j / EPL); the sort direction and
-    // the side of the pair then depend on the lane only.  Distances j < EPL stay inside the lane.
-#pragma unroll 1
-    for (int k = 2 * EPL; k <= 32 * EPL; k <<= 1) {
-        const bool up = (base & k) == 0;
-#pragma unroll 1
-        for (int j = k >> 1; j >= EPL; j >>= 1) {
-            const bool keep_min = ((base & j) == 0) == up;
-            const int lm = j / EPL;
-#pragma unroll
-            for (int r = 0; r < EPL; ++r) {
-                const T y = __shfl_xor_sync(FULL_MASK, x[r], lm);
-                x[r] = keep_min ? min(x[r], y) : max(x[r], y);
-            }
-        }
-#pragma unroll
-        for (int j = EPL >> 1; j > 0; j >>= 1) {
-#pragma unroll
-            for (int r = 0; r < EPL; ++r)
-                if ((r & j) == 0) cx_regs<EPL, T>(x, r, j, up);
-        }
-    }
-}
-
-// Same network restricted to its phases k = 2 .. seg (seg a power of two, 2 <= seg <= 32 * EPL),
-// the last of them ascending everywhere: every aligned block of seg elements ends sorted ascending
-// on its own (elements of different blocks are never compared).  With seg = 32 * EPL it is
-// warp_bitonic_sort.  Packed units sort the keys of several vblocks at once this way.
-template <int EPL, typename T>
-__device__ __forceinline__ void warp_bitonic_sort_blocks(T (&x)[EPL], int lane, int seg)
-{
-    const int base = lane * EPL;
+    // Phases k <= EPL: inside each lane's registers.
 #pragma unroll
     for (int k = 2; k <= EPL; k <<= 1) {
         if (k <= seg) {
 #pragma unroll
-            for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int r = 0; r < EPL; ++r)
+                if ((r & (k >> 1)) == 0) cx_asc<EPL, T>(x, r, r ^ (k - 1));
 #pragma unroll
-                for (int r = 0; r < EPL; ++r) {
-                    if ((r & j) == 0) {
-                        const bool up = (k == seg) || (((base + r) & k) == 0);
-                        cx_regs<EPL, T>(x, r, j, up);
-                    }
-                }
+            for (int j = k >> 2; j > 0; j >>= 1) {
+#pragma unroll
+                for (int r = 0; r < EPL; ++r)
+                    if ((r & j) == 0) cx_asc<EPL, T>(x, r, r | j);
             }
         }
     }
+    // Phases k = 2 * EPL .. seg: blocks of lk = k / EPL lanes (a runtime loop keeps the code small).
 #pragma unroll 1
     for (int k = 2 * EPL; k <= seg; k <<= 1) {
-        const bool up = (k == seg) || ((base & k) == 0);
+        const int lk = k / EPL;
+        const bool low = (lane & (lk >> 1)) == 0; // this lane holds the lower half of its block
+        // Mirror stage: register r pairs with register EPL - 1 - r of lane ^ (lk - 1).
+        if constexpr (EPL == 1) {
+            const T y = __shfl_xor_sync(FULL_MASK, x[0], lk - 1);
+            x[0] = low ? min(x[0], y) : max(x[0], y);
+        } else {
+#pragma unroll
+            for (int r = 0; r < EPL / 2; ++r) {
+                const int s = EPL - 1 - r;
+                const T ya = __shfl_xor_sync(FULL_MASK, x[s], lk - 1);
+                const T yb = __shfl_xor_sync(FULL_MASK, x[r], lk - 1);
+                x[r] = low ? min(x[r], ya) : max(x[r], ya);
+                x[s] = low ? min(x[s], yb) : max(x[s], yb);
+            }
+        }
+        // Distances j = k/4 .. EPL: register r with the same register of lane ^ (j / EPL).
 #pragma unroll 1
-        for (int j = k >> 1; j >= EPL; j >>= 1) {
-            const bool keep_min = ((base & j) == 0) == up;
-            const int lm = j / EPL;
+        for (int lm = lk >> 2; lm >= 1; lm >>= 1) {
+            const bool keep_min = (lane & lm) == 0;
 #pragma unroll
             for (int r = 0; r < EPL; ++r) {
                 const T y = __shfl_xor_sync(FULL_MASK, x[r], lm);
                 x[r] = keep_min ? min(x[r], y) : max(x[r], y);
             }
         }
+        // Distances j = EPL/2 .. 1: inside the lane.
 #pragma unroll
         for (int j = EPL >> 1; j > 0; j >>= 1) {
 #pragma unroll
             for (int r = 0; r < EPL; ++r)
-                if ((r & j) == 0) cx_regs<EPL, T>(x, r, j, up);
+                if ((r & j) == 0) cx_asc<EPL, T>(x, r, r | j);
+        }
+    }
+}
+
+// All 32 * EPL elements of the warp in one ascending order.
+template <int EPL, typename T>
+__device__ __forceinline__ void warp_bitonic_sort(T (&x)[EPL], int lane)
+{
+    warp_sort_blocks<EPL, T>(x, lane, 32 * EPL);
+}
+
+// A lane's EPL consecutive uint16 entries (register r -> dst[r]) in as few stores as their
+// alignment allows: dst is 2 * EPL-byte aligned (a permutation slot is 16-byte aligned and the
+// lane's run starts at lane * EPL).  Lanes 64 bytes apart (EPL = 32) touch 2 bank groups per
+// 16-byte store instead of 2 banks per 2-byte store.
+template <int EPL>
+__device__ __forceinline__ void store_u16_run(uint16_t* dst, const uint32_t (&v)[EPL])
+{
+    if constexpr (EPL == 1) {
+        dst[0] = static_cast<uint16_t>(v[0]);
+    } else if constexpr (EPL == 2) {
+        *reinterpret_cast<uint32_t*>(dst) = (v[0] & 0xFFFFu) | (v[1] << 16);
+    } else if constexpr (EPL == 4) {
+        *reinterpret_cast<uint2*>(dst) = make_uint2((v[0] & 0xFFFFu) | (v[1] << 16), (v[2] & 0xFFFFu) | (v[3] << 16));
+    } else {
+#pragma unroll
+        for (int c = 0; c < EPL / 8; ++c) {
+            const uint32_t* w = v + 8 * c;
+            *reinterpret_cast<uint4*>(dst + 8 * c) =
+                make_uint4((w[0] & 0xFFFFu) | (w[1] << 16), (w[2] & 0xFFFFu) | (w[3] << 16),
+                           (w[4] & 0xFFFFu) | (w[5] << 16), (w[6] & 0xFFFFu) | (w[7] << 16));
         }
     }
 }
@@ -433,10 +440,10 @@ __device__ __forceinline__ void warp_make_perm(const IterParams& p, uint64_t see
     perm_sort_keys<EPL>(p, seed, vblock, n_valid, x, lane);
     warp_bitonic_sort<EPL, uint32_t>(x, lane);
 #pragma unroll
-    for (int r = 0; r < EPL; ++r) {
-        const int f = lane * EPL + r;
-        if (f < n_valid) perm[f] = static_cast<uint16_t>(x[r] & PermKey<EPL>::IDX_MASK);
-    }
+    for (int r = 0; r < EPL; ++r) x[r] &= PermKey<EPL>::IDX_MASK;
+    // Entries n_valid .. vp-1 get the invalid elements' indices, which no mover reads; lanes past
+    // the slot's vp entries (vp < 32, one entry per lane) store nothing.
+    if (lane * EPL < p.unit_vp) store_u16_run<EPL>(perm + lane * EPL, x);
 }
 
 // The reference kernel's permutation (src/povs/__cuda/lib/povs.cu:282-321): identity over the
@@ -1074,14 +1081,22 @@ __device__ __forceinline__ void make_packed_unit(const IterParams& p, StageMeta&
             x[4 * q + t] = ((static_cast<int>(e) < nvq) ? (pick_word(k, static_cast<int>(e & 3u)) & ~M) : ~M) | e;
         }
     }
-    warp_bitonic_sort_blocks<EPL, uint32_t>(x, lane, p.vp);
+    warp_sort_blocks<EPL, uint32_t>(x, lane, p.vp);
+    // Destination slot fg = lane * EPL + r of the unit takes unit row (fg & ~vpm) + (x[r] & M), or
+    // HOLE past its vblock's valid rows (only in units with a short or missing vblock).
+    if (total == p.unit_vp) {
 #pragma unroll
-    for (int r = 0; r < EPL; ++r) {
-        const int fg = lane * EPL + r;
-        const int sr = fg >> p.vp_shift;
-        const int nvr = __shfl_sync(FULL_MASK, nv_lane, sr);
-        perm[fg] = (fg & vpm) < nvr ? static_cast<uint16_t>((sr << p.vp_shift) + static_cast<int>(x[r] & M)) : HOLE;
+        for (int r = 0; r < EPL; ++r) x[r] = ((lane * EPL + r) & ~vpm) | (x[r] & M);
+    } else {
+#pragma unroll
+        for (int r = 0; r < EPL; ++r) {
+            const int fg = lane * EPL + r;
+            const int sr = fg >> p.vp_shift;
+            const int nvr = __shfl_sync(FULL_MASK, nv_lane, sr);
+            x[r] = (fg & vpm) < nvr ? static_cast<uint32_t>((sr << p.vp_shift) + static_cast<int>(x[r] & M)) : HOLE;
+        }
     }
+    store_u16_run<EPL>(perm + lane * EPL, x);
 }
 
 // RING: the permuter and mover warps carry their units' stage / slot ring positions from unit to
