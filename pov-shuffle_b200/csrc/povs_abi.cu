@@ -61,24 +61,27 @@ int ilog2(int64_t x)
 
 using KernelFn = void (*)(IterParams);
 
-template <bool INJ, bool BULK, bool PUSH, bool RING>
+template <bool INJ, bool BULK, bool PUSH, bool RING, bool WIDE = false>
 KernelFn kernel_for_epl(int epl)
 {
     switch (epl) {
-    case 1: return povs::povs_iteration_kernel<1, INJ, BULK, PUSH, RING>;
-    case 2: return povs::povs_iteration_kernel<2, INJ, BULK, PUSH, RING>;
-    case 4: return povs::povs_iteration_kernel<4, INJ, BULK, PUSH, RING>;
-    case 8: return povs::povs_iteration_kernel<8, INJ, BULK, PUSH, RING>;
-    case 16: return povs::povs_iteration_kernel<16, INJ, BULK, PUSH, RING>;
-    case 32: return povs::povs_iteration_kernel<32, INJ, BULK, PUSH, RING>;
+    case 1: return povs::povs_iteration_kernel<1, INJ, BULK, PUSH, RING, false, WIDE>;
+    case 2: return povs::povs_iteration_kernel<2, INJ, BULK, PUSH, RING, false, WIDE>;
+    case 4: return povs::povs_iteration_kernel<4, INJ, BULK, PUSH, RING, false, WIDE>;
+    case 8: return povs::povs_iteration_kernel<8, INJ, BULK, PUSH, RING, false, WIDE>;
+    case 16: return povs::povs_iteration_kernel<16, INJ, BULK, PUSH, RING, false, WIDE>;
+    case 32: return povs::povs_iteration_kernel<32, INJ, BULK, PUSH, RING, false, WIDE>;
     default: return nullptr;
     }
 }
 
+// wide: slabs of 512 to 1024 bytes (TMA loads only), whose stores keep several loads in flight.
 template <bool INJ, bool PUSH>
-KernelFn kernel_for(int epl, bool bulk, bool ring)
+KernelFn kernel_for(int epl, bool bulk, bool ring, bool wide)
 {
     if (!bulk) return kernel_for_epl<INJ, false, PUSH, true>(epl);
+    if (wide)
+        return ring ? kernel_for_epl<INJ, true, PUSH, true, true>(epl) : kernel_for_epl<INJ, true, PUSH, false, true>(epl);
     return ring ? kernel_for_epl<INJ, true, PUSH, true>(epl) : kernel_for_epl<INJ, true, PUSH, false>(epl);
 }
 
@@ -97,12 +100,13 @@ KernelFn packed_kernel_for_epl(int epl)
 }
 
 // Push mode exists for device randomness only.  Plain-load kernels always carry ring positions.
-KernelFn select_kernel(int epl, bool injected, bool bulk, bool push = false, bool ring = false, bool packed = false)
+KernelFn select_kernel(int epl, bool injected, bool bulk, bool push = false, bool ring = false, bool packed = false,
+                       bool wide = false)
 {
     if (packed) return bulk ? packed_kernel_for_epl<true>(epl) : packed_kernel_for_epl<false>(epl);
-    if (push) return kernel_for<false, true>(epl, bulk, ring);
-    if (injected) return kernel_for<true, false>(epl, bulk, ring);
-    return kernel_for<false, false>(epl, bulk, ring);
+    if (push) return kernel_for<false, true>(epl, bulk, ring, wide);
+    if (injected) return kernel_for<true, false>(epl, bulk, ring, wide);
+    return kernel_for<false, false>(epl, bulk, ring, wide);
 }
 
 // Decks (all decks of a batch together) of at least this many bytes are launched one iteration
@@ -210,12 +214,13 @@ int set_smem_attr_all(int smem)
     for (int mode = 0; mode < 3; ++mode)
         for (int bulk = 0; bulk < 2; ++bulk)
             for (int ring = 0; ring < 2; ++ring)
-                for (int epl = 1; epl <= 32; epl <<= 1) {
-                    KernelFn fn = select_kernel(epl, mode == 1, bulk != 0, mode == 2, ring != 0);
-                    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
-                                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-                    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
-                }
+                for (int wide = 0; wide <= bulk; ++wide)
+                    for (int epl = 1; epl <= 32; epl <<= 1) {
+                        KernelFn fn = select_kernel(epl, mode == 1, bulk != 0, mode == 2, ring != 0, false, wide != 0);
+                        cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+                        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+                    }
     for (int bulk = 0; bulk < 2; ++bulk)
         for (int epl = 2; epl <= 32; epl <<= 1) {
             KernelFn fn = select_kernel(epl, false, bulk != 0, false, true, true);
@@ -319,6 +324,17 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out, boo
         std::max(1, std::min(pack > 1 && !bulk ? std::min(t.permuters, 2) : t.permuters, 16 - movers));
     // Permutation slots: the stages' worth plus room for every permuter to work ahead.
     auto slots_for = [&](int stages) { return std::min(povs::MAX_SLOTS, stages + 2 * permuters); };
+    // The most stages (<= max_stages) of slabs of sl bytes per row that fit next to their
+    // permutation slots (slots_for(n) of them for n stages).
+    auto stages_for = [&](int64_t sl, int64_t& stage_bytes) {
+        stage_bytes = ((stage_rows * sl + 127) / 128) * 128;
+        const int64_t per_stage = stage_bytes + 16;
+        int n = max_stages;
+        while (n > 0 && povs::cta_smem_bytes(0, 0, slots_for(n), static_cast<int>(unit_vp), p.pblock) + n * per_stage >
+                            c.smem_optin)
+            --n;
+        return n;
+    };
     int64_t slab = p.row_bytes;
     if (stage_rows * p.row_bytes > t.stage_cap) {
         const int64_t fit = t.stage_cap / stage_rows;
@@ -327,19 +343,22 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out, boo
         // Wide rows: pieces of at least SLAB_FLOOR bytes per row and stage when three such stages
         // fit (per-row copies of 1 KiB and less leave the DRAM well short of its copy bandwidth).
         const int64_t wide = std::min<int64_t>(p.row_bytes, ((SLAB_FLOOR_BYTES / vec) * vec));
-        if (slab < wide) {
-            const int64_t wide_stage = ((stage_rows * wide + 127) / 128) * 128;
-            const int64_t fixed = povs::cta_smem_bytes(0, 0, slots_for(3), static_cast<int>(unit_vp), p.pblock);
-            if (fixed + 3 * (wide_stage + 16) <= c.smem_optin) slab = wide;
+        int64_t sb = 0;
+        if (slab < wide && stages_for(wide, sb) >= 3) slab = wide;
+        // Narrow rows in a vblock of many rows: per-row copies under 128 bytes are slow (measured on
+        // B200: 64-byte rows in 1024-row vblocks moved 0.59 TB/s as 32-byte slabs), so take the
+        // fewest slabs per row, whole rows first, with which two stages fit.
+        if (slab < std::min<int64_t>(p.row_bytes, 128)) {
+            for (int64_t n = 1; n * vec <= p.row_bytes; ++n) {
+                const int64_t cand = (((p.row_bytes + n - 1) / n + vec - 1) / vec) * vec;
+                if (cand <= slab) break;
+                if (stages_for(cand, sb) >= 2) {
+                    slab = cand;
+                    break;
+                }
+            }
         }
     }
-    auto stages_for = [&](int64_t sl, int64_t& stage_bytes) {
-        stage_bytes = ((stage_rows * sl + 127) / 128) * 128;
-        const int kp = slots_for(max_stages);
-        const int64_t fixed = povs::cta_smem_bytes(0, 0, kp, static_cast<int>(unit_vp), p.pblock);
-        const int64_t per_stage = stage_bytes + 16;
-        return static_cast<int>(std::min<int64_t>(max_stages, (c.smem_optin - fixed) / per_stage));
-    };
     int64_t stage_bytes = 0;
     int nst = stages_for(slab, stage_bytes);
     // Shrink the slab until at least two stages fit.
@@ -381,7 +400,8 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out, boo
     p.n_movers = movers;
     p.n_permuters = permuters;
 
-    out.fn = select_kernel(epl, injected, bulk, push, stage_bytes <= RING_STAGE_BYTES || pack > 1, pack > 1);
+    out.fn = select_kernel(epl, injected, bulk, push, stage_bytes <= RING_STAGE_BYTES || pack > 1, pack > 1,
+                           bulk && pack == 1 && slab >= 512 && slab <= 1024);
     out.grid = std::max(1, grid);
     out.block = warps * 32;
     out.smem = cta_smem;

@@ -296,28 +296,37 @@ __device__ __forceinline__ void cx_asc(T (&x)[EPL], int r, int s)
 
 // Sorts every aligned block of `seg` elements ascending (seg a power of two, 2 <= seg <= 32 * EPL);
 // element e = lane * EPL + r is register r of lane `lane`, and elements of different blocks are
-// never compared.  Bitonic merging in the form whose comparators all point one way (Batcher's
-// network with the first stage of every merge mirrored): phase k = 2, 4, .., seg compares element
-// e with e ^ (k - 1), its mirror image inside its block of k (which merges two ascending halves
-// without reversing one of them), then with e ^ j for j = k/4, .., 1, always keeping the smaller
-// key at the lower index.  Inside a lane every comparator is a fixed register pair (a min and a
-// max); across lanes a stage is one shuffle per register.  The keys are distinct, so the order
-// equals that of any other correct sort.
+// never compared.  Every comparator keeps the smaller key at the lower index.  Blocks inside a
+// lane are sorted by a fixed network of register pairs (a min and a max each); larger blocks by
+// bitonic merging in the form whose comparators all point one way (Batcher's network with the
+// first stage of every merge mirrored): phase k = 2 EPL, .., seg compares element e with
+// e ^ (k - 1), its mirror image inside its block of k (which merges two ascending halves without
+// reversing one of them), then with e ^ j for j = k/4, .., 1; across lanes a stage is one shuffle
+// per register.  The keys are distinct, so the order equals that of any other correct sort.
 template <int EPL, typename T>
 __device__ __forceinline__ void warp_sort_blocks(T (&x)[EPL], int lane, int seg)
 {
-    // Phases k <= EPL: inside each lane's registers.
+    // Blocks of up to EPL elements, inside each lane's registers: Batcher's odd-even merge sort,
+    // cut after its merges into blocks of min(seg, EPL) (191 comparators for 32 elements where the
+    // bitonic network takes 240).  Merge of blocks of pp into 2 pp: distances kk = pp, pp/2, .., 1;
+    // element a meets a + kk when a - (kk mod pp) lies in the lower half of a run of 2 kk and both
+    // are in the same block of 2 pp.
+    // Loops of fixed trip counts, so that every register index is a compile-time constant.
+    constexpr int LOG_EPL = EPL >= 32 ? 5 : EPL >= 16 ? 4 : EPL >= 8 ? 3 : EPL >= 4 ? 2 : EPL >= 2 ? 1 : 0;
 #pragma unroll
-    for (int k = 2; k <= EPL; k <<= 1) {
-        if (k <= seg) {
+    for (int lp = 0; lp < LOG_EPL; ++lp) {
+        const int pp = 1 << lp;
+        if (2 * pp <= seg) {
 #pragma unroll
-            for (int r = 0; r < EPL; ++r)
-                if ((r & (k >> 1)) == 0) cx_asc<EPL, T>(x, r, r ^ (k - 1));
+            for (int lk = lp; lk >= 0; --lk) {
+                const int kk = 1 << lk;
+                const int j0 = kk % pp;
 #pragma unroll
-            for (int j = k >> 2; j > 0; j >>= 1) {
-#pragma unroll
-                for (int r = 0; r < EPL; ++r)
-                    if ((r & j) == 0) cx_asc<EPL, T>(x, r, r | j);
+                for (int a = 0; a < EPL; ++a) {
+                    const int b = a + kk;
+                    if (a >= j0 && (a - j0) % (2 * kk) < kk && b < EPL && a / (2 * pp) == b / (2 * pp))
+                        cx_asc<EPL, T>(x, a, b);
+                }
             }
         }
     }
@@ -744,12 +753,56 @@ __device__ __forceinline__ void async_load_unit(const IterParams& p, const Stage
     cp_async_arrive_noinc(bar);
 }
 
+// Rows (or slabs) of at most 32 * C chunks of T, this warp's share (rows f = warp, warp + n_warps,
+// ..): lane l moves chunks l, l + 32, .. of a row, and the chunks of U rows are loaded before any
+// is stored, so that each lane has up to U * C loads in flight (a row-by-row loop waited for every
+// row's loads: 512-byte rows moved 3.4-3.9 TB/s that way).  Packed units skip holes.
+template <int C, int U, typename T, bool PACK, typename SrcRow, typename DstSlot>
+__device__ __forceinline__ void store_wide_rows(const IterParams& p, const StageMeta& m, const uint8_t* stage,
+                                                int64_t col, int n, int cpr, int lane, int warp, int n_warps,
+                                                SrcRow src_row, DstSlot dst_slot)
+{
+    const int pmask = p.pblock - 1;
+    for (int f = warp; f < n; f += U * n_warps) {
+        T v[U][C];
+        T* dst[U];
+        bool ok[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int fu = f + u * n_warps;
+            ok[u] = fu < n;
+            int s = 0, d = 0;
+            if (ok[u]) {
+                s = src_row(fu);
+                d = dst_slot(fu);
+                if constexpr (PACK) ok[u] = s != HOLE;
+            }
+            if (!ok[u]) s = d = 0;
+            const T* src = reinterpret_cast<const T*>(stage + static_cast<size_t>(s) * p.slab_bytes);
+            dst[u] = reinterpret_cast<T*>(slot_ptr(m, d, p.pblock_shift, pmask, p.row_bytes) + col);
+#pragma unroll
+            for (int c = 0; c < C; ++c) {
+                const int q = lane + 32 * c;
+                if (ok[u] && q < cpr) v[u][c] = src[q];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+#pragma unroll
+            for (int c = 0; c < C; ++c) {
+                const int q = lane + 32 * c;
+                if (ok[u] && q < cpr) store_row_chunk(dst[u] + q, v[u][c]);
+            }
+        }
+    }
+}
+
 // store_share with the lane geometry computed by divisions: the form the bulk (TMA) path uses,
 // where it measured faster than the shift form below (the per-unit share of this arithmetic is
 // small there).  This warp's share of the copy stage -> global.  In place: destination slot f receives stage row
 // idx[f] (idx = the permutation).  Push: stage row f (the unit's own member) goes to destination
 // slot idx[f] (idx = the member's destination slots).  Work items are interleaved over the warps.
-template <int W, bool PUSH>
+template <int W, bool PUSH, bool WIDE = false>
 __device__ __forceinline__ void store_share_div(const IterParams& p, const StageMeta& m, const uint8_t* stage,
                                             const uint16_t* idx, int64_t col, int slen, int lane, int warp,
                                             int n_warps)
@@ -767,11 +820,20 @@ __device__ __forceinline__ void store_share_div(const IterParams& p, const Stage
         else return f;
     };
     if (cpr >= 32) {
-        for (int f = warp; f < n; f += n_warps) {
-            const T* src = reinterpret_cast<const T*>(stage + static_cast<size_t>(src_row(f)) * p.slab_bytes);
-            T* dst = reinterpret_cast<T*>(slot_ptr(m, dst_slot(f), p.pblock_shift, pmask, p.row_bytes) + col);
+        bool done = false;
+        if constexpr (WIDE) {
+            if (cpr <= 64) {
+                store_wide_rows<2, 2, T, false>(p, m, stage, col, n, cpr, lane, warp, n_warps, src_row, dst_slot);
+                done = true;
+            }
+        }
+        if (!done) {
+            for (int f = warp; f < n; f += n_warps) {
+                const T* src = reinterpret_cast<const T*>(stage + static_cast<size_t>(src_row(f)) * p.slab_bytes);
+                T* dst = reinterpret_cast<T*>(slot_ptr(m, dst_slot(f), p.pblock_shift, pmask, p.row_bytes) + col);
 #pragma unroll 4
-            for (int q = lane; q < cpr; q += 32) store_row_chunk(dst + q, src[q]);
+                for (int q = lane; q < cpr; q += 32) store_row_chunk(dst + q, src[q]);
+            }
         }
     } else {
         const int g = 32 / cpr;
@@ -809,7 +871,11 @@ __device__ __forceinline__ void store_share_div(const IterParams& p, const Stage
 // This warp's share of the copy stage -> global.  In place: destination slot f receives stage row
 // idx[f] (idx = the permutation).  Push: stage row f (the unit's own member) goes to destination
 // slot idx[f] (idx = the member's destination slots).  Work items are interleaved over the warps.
-template <int W, bool PUSH, bool PACK = false>
+// WIDE (kernels launched for slabs of 512 to 1024 bytes): rows of 32 to 64 chunks keep four chunk
+// loads per lane in flight (store_wide_rows; 512- to 1024-byte rows moved 1.1-1.7x faster).  The
+// other kernels keep the row-by-row loop: compiled into them, the wide form cost the 256-byte-row
+// kernels 1-2 % (more registers), and 2 KiB slabs ran 1 % slower with it.
+template <int W, bool PUSH, bool PACK = false, bool WIDE = false>
 __device__ __forceinline__ void store_share(const IterParams& p, const StageMeta& m, const uint8_t* stage,
                                             const uint16_t* idx, int64_t col, int slen, int lane, int warp,
                                             int n_warps)
@@ -829,12 +895,21 @@ __device__ __forceinline__ void store_share(const IterParams& p, const StageMeta
         else return f;
     };
     if (cpr >= 32) {
-        for (int f = warp; f < n; f += n_warps) {
-            if (PACK && idx[f] == HOLE) continue;
-            const T* src = reinterpret_cast<const T*>(stage + static_cast<size_t>(src_row(f)) * p.slab_bytes);
-            T* dst = reinterpret_cast<T*>(slot_ptr(m, dst_slot(f), p.pblock_shift, pmask, p.row_bytes) + col);
+        bool done = false;
+        if constexpr (WIDE) {
+            if (cpr <= 64) {
+                store_wide_rows<2, 2, T, PACK>(p, m, stage, col, n, cpr, lane, warp, n_warps, src_row, dst_slot);
+                done = true;
+            }
+        }
+        if (!done) {
+            for (int f = warp; f < n; f += n_warps) {
+                if (PACK && idx[f] == HOLE) continue;
+                const T* src = reinterpret_cast<const T*>(stage + static_cast<size_t>(src_row(f)) * p.slab_bytes);
+                T* dst = reinterpret_cast<T*>(slot_ptr(m, dst_slot(f), p.pblock_shift, pmask, p.row_bytes) + col);
 #pragma unroll 4
-            for (int q = lane; q < cpr; q += 32) store_row_chunk(dst + q, src[q]);
+                for (int q = lane; q < cpr; q += 32) store_row_chunk(dst + q, src[q]);
+            }
         }
     } else {
         const int g = lg.g, lrow = lg.lrow, lq = lg.lq;
@@ -1104,9 +1179,10 @@ __device__ __forceinline__ void make_packed_unit(const IterParams& p, StageMeta&
 // plain-load kernel); otherwise they recompute them per unit, which measured faster on large
 // bulk-loaded units.
 // PACK: units are groups of `pack` small vblocks (device randomness, in place, whole rows).
-template <int EPL, bool INJECTED, bool BULK, bool PUSH, bool RING, bool PACK = false>
+template <int EPL, bool INJECTED, bool BULK, bool PUSH, bool RING, bool PACK = false, bool WIDE = false>
 __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_constant__ IterParams p)
 {
+    static_assert(!WIDE || (BULK && !PACK), "the wide-row store form is built into TMA-loaded, unpacked kernels");
     static_assert(BULK || RING, "plain-load kernels carry ring positions");
     static_assert(!(PUSH && INJECTED), "push mode draws its randomness on the device");
     static_assert(!PACK || (RING && !PUSH && !INJECTED), "packed units: device randomness, in place, ring positions");
@@ -1421,7 +1497,7 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
             const int slab = static_cast<int>(j % p.n_slabs);
             const int64_t col = static_cast<int64_t>(slab) * p.slab_bytes;
             const int slen = static_cast<int>(min(static_cast<int64_t>(p.slab_bytes), p.row_bytes - col));
-            store_share_div<16, PUSH>(p, m, stage, idx, col, slen, lane, mw, n_movers);
+            store_share_div<16, PUSH, WIDE>(p, m, stage, idx, col, slen, lane, mw, n_movers);
             mbar_arrive(&sm.empty[st]);  // this thread's reads of the data stage are done
             mbar_arrive(&sm.pempty[k]);  // ... and of the permutation slot
             return true;
@@ -1536,7 +1612,7 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
             const int64_t col = static_cast<int64_t>(slab) * p.slab_bytes;
             const int slen = static_cast<int>(min(static_cast<int64_t>(p.slab_bytes), p.row_bytes - col));
             if constexpr (BULK) {
-                store_share<16, PUSH, PACK>(p, m, stage, idx, col, slen, lane, mw, n_movers);
+                store_share<16, PUSH, PACK, WIDE>(p, m, stage, idx, col, slen, lane, mw, n_movers);
             } else {
                 switch (p.vec_bytes) {
                 case 16: store_share<16, PUSH, PACK>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;

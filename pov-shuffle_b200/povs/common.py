@@ -204,31 +204,32 @@ def _choose_base_offset(
 
 # B200 option tuning (``tuning="b200"``): the iteration kernel stages one vblock (V * P rows) per
 # unit in shared memory, or several small vblocks per unit (packed units).  Measured on B200 (GB/s
-# of 2 x deck bytes per iteration, V = 2, 2-4 GiB decks): rows of 96 B and more stream best in
-# vblocks of 32-64 KiB (5.5-6.4 TB/s); more than 512 rows per vblock makes the permutation slots
-# crowd out the data stages; rows of 2 KiB and more are staged as 2 KiB column slabs of 32 rows
-# (6.3-6.4 TB/s).  Smaller rows travel in packed units, whose cost per row grows with the vblock's
-# sort width, so they do best with short vblocks: 32 rows below 8 B, 64 below 32 B, 128 below 64 B
-# and 256 below 96 B (4 B rows 595 GB/s, 16 B 3394, 32 B 5401, 64 B 5886).
+# of 2 x deck bytes per iteration, V = 2, 2 GiB decks, a sweep of P for every row size): rows of
+# 96 B and more stream best in vblocks of 32-64 KiB (5.7-6.2 TB/s) and at most 512 rows; rows of
+# 2 KiB and more are staged as 2 KiB column slabs of 32 rows (6.1-6.2 TB/s).  Rows under 96 B
+# travel in packed units; their best vblock lengths, which balance the sort network per key
+# against the fixed costs per unit and member, were 1024 rows below 8 B (4 B: 968 GB/s), 256
+# below 16 B (8 B: 1999), 128 below 24 B (16 B: 4956), 256 below 48 B (32 B: 5649), 1024 below
+# 64 B (48 B: 4741) and 256 below 96 B (64 B: 5788).
 B200_VBLOCK_BYTES = 64 * 1024
 B200_MAX_VBLOCK_ROWS = 512
 B200_WIDE_ROW_BYTES = 2048
 B200_WIDE_VBLOCK_ROWS = 32
-B200_SMALL_ROW_VBLOCK_ROWS = ((8, 32), (32, 64), (64, 128), (96, 256))  # (row bytes below, vblock rows)
+B200_SMALL_ROW_VBLOCK_ROWS = ((8, 1024), (16, 256), (24, 128), (48, 256), (64, 1024), (96, 256))  # (row bytes below, vblock rows)
 
 
 def choose_pblock_size_b200(row_bytes: int, vblock_size: int, deck_size: int) -> int:
     """Physical block size for the B200 kernel: the largest power of two that keeps a vblock within
-    64 KiB and 512 rows (32 rows for rows of 2 KiB and more; 32 to 256 rows for rows under 96 bytes,
-    which travel in packed units), at least ``MIN_PBLOCK_SIZE``, and at most what leaves the deck two
-    vblocks."""
+    64 KiB and 512 rows (32 rows for rows of 2 KiB and more; the measured best length, 128 to 1024
+    rows, for rows under 96 bytes, which travel in packed units), at least ``MIN_PBLOCK_SIZE``, and
+    at most what leaves the deck two vblocks."""
     if row_bytes >= B200_WIDE_ROW_BYTES:
         rows = B200_WIDE_VBLOCK_ROWS
     else:
         rows = min(B200_MAX_VBLOCK_ROWS, B200_VBLOCK_BYTES // max(1, row_bytes))
         for below, small_rows in B200_SMALL_ROW_VBLOCK_ROWS:
             if row_bytes < below:
-                rows = min(rows, small_rows)
+                rows = small_rows
                 break
     pblock = max(MIN_PBLOCK_SIZE, round_down_to_power_of_2(max(1, rows // vblock_size)))
     room = deck_size // (2 * vblock_size)

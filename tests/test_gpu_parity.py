@@ -52,6 +52,14 @@ DEFAULT_CASES = [
     (50_000, 32, 64, 8, [0, 3, 6, 11], 3),
     (9999, 24, 16, 2, [0, 5], 2),
     (1 << 16, 256, 8, 2, [0, 1], 1),
+    # Rows of 32 to 128 16-byte chunks (several chunk loads in flight per lane), small and large units.
+    (3001, 512, 16, 2, [0, 1, 3], 3),
+    (2500, 768, 32, 2, [0, 2], 2),
+    (1500, 1040, 8, 2, [0, 1], 2),
+    # Vblocks of 1024 and 512 rows: whole narrow rows in two or three large stages, or two slabs.
+    (4000, 64, 512, 2, [0, 1], 2),
+    (5000, 96, 512, 2, [0, 2], 2),
+    (3000, 128, 256, 2, [0, 1], 2),
 ]
 
 
