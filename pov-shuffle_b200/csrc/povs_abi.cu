@@ -287,10 +287,37 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out, boo
     // travel `pack` at a time, so the per-unit costs (barrier round trips, member ranks, the sort
     // network, copy issue) are paid once per pack * V * P rows.  One member per lane (pack * V <= 32),
     // one sort of pack * V * P <= 1024 keys, at least 2 keys per lane, unit bytes <= pack_bytes.
+    uintptr_t addr = 0;
+    for (int i = 0; i < p.n_shards; ++i) addr |= reinterpret_cast<uintptr_t>(p.shard_base[i]);
+    if (push)
+        for (int i = 0; i < p.n_shards; ++i) addr |= reinterpret_cast<uintptr_t>(p.dst_base[i]);
+    if (p.n_decks > 1) addr |= static_cast<uintptr_t>(p.deck_stride);
+    int vec = 16;
+    while (vec > 1 && ((p.row_bytes % vec) != 0 || (addr % vec) != 0)) vec >>= 1;
+    const bool bulk = (vec == 16) && !t.force_plain && !plain_loads;
+
+    // TMA-loaded rows whose 16-byte chunk count is not a power of two (48, 80, 96, .. bytes) spread
+    // over the lanes unevenly, and ran best in larger units (measured on B200, 2 GiB decks: 48-byte
+    // rows, P = 64, 3,756 GB/s in 12 KiB units, 5,387 in 48 KiB; 96-byte rows, P = 32, 4,418 in 12
+    // KiB, 5,359 in 24 KiB), so their packs may grow to three times pack_bytes.
+    const int64_t pack_limit =
+        (bulk && (p.row_bytes & (p.row_bytes - 1)) != 0) ? 3 * static_cast<int64_t>(t.pack_bytes) : t.pack_bytes;
+    // A packed unit is always staged as whole rows: beyond the stage cap it must still fit three
+    // whole-row stages next to their permutation slots (the slab rule below then keeps whole rows).
+    auto packed_fits = [&](int64_t pk) {
+        const int64_t urows = pk * vp;
+        const int64_t ubytes = urows * p.row_bytes;
+        if (ubytes <= t.stage_cap) return true;
+        const int mv = std::max(1, std::min(!bulk ? std::min(t.movers, 2) : t.movers, 15));
+        const int pm = std::max(1, std::min(!bulk ? std::min(t.permuters, 2) : t.permuters, 16 - mv));
+        const int slots = std::min(povs::MAX_SLOTS, 3 + 2 * pm);
+        const int64_t fixed = povs::cta_smem_bytes(0, 0, slots, static_cast<int>(urows), p.pblock);
+        return fixed + 3 * (((ubytes + 127) / 128) * 128 + 16) <= c.smem_optin;
+    };
     int pack = 1;
     if (!injected && !push && p.vb_begin == 0 && p.vb_step == 1 && t.pack_bytes > 0 && vp >= 8) {
         while (2 * pack * p.vblock <= 32 && 2 * pack * vp <= POVS_MAX_VP &&
-               2 * pack * vp * p.row_bytes <= t.pack_bytes && pack < p.n_vblocks)
+               2 * pack * vp * p.row_bytes <= pack_limit && pack < p.n_vblocks && packed_fits(2 * pack))
             pack *= 2;
         if (pack * vp < 64) pack = 1;
     }
@@ -300,15 +327,6 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out, boo
     p.pack = pack;
     p.unit_vp = static_cast<int32_t>(unit_vp);
     p.groups_per_deck = (p.n_vblocks + pack - 1) / pack;
-
-    uintptr_t addr = 0;
-    for (int i = 0; i < p.n_shards; ++i) addr |= reinterpret_cast<uintptr_t>(p.shard_base[i]);
-    if (push)
-        for (int i = 0; i < p.n_shards; ++i) addr |= reinterpret_cast<uintptr_t>(p.dst_base[i]);
-    if (p.n_decks > 1) addr |= static_cast<uintptr_t>(p.deck_stride);
-    int vec = 16;
-    while (vec > 1 && ((p.row_bytes % vec) != 0 || (addr % vec) != 0)) vec >>= 1;
-    const bool bulk = (vec == 16) && !t.force_plain && !plain_loads;
 
     // Slab width: whole rows when a vblock fits a stage, else the widest 128-byte (or vec) multiple that does.
     // A stage holds a unit's rows: the vblock's V*P rows in place (pack of them when packed), one
@@ -359,6 +377,9 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out, boo
             }
         }
     }
+    if (pack > 1 && slab != p.row_bytes)
+        return fail(POVS_ERR_UNSUPPORTED, "packed units of %lld bytes do not fit as whole rows",
+                    static_cast<long long>(stage_rows * p.row_bytes));
     int64_t stage_bytes = 0;
     int nst = stages_for(slab, stage_bytes);
     // Shrink the slab until at least two stages fit.

@@ -209,13 +209,13 @@ def _choose_base_offset(
 # 2 KiB and more are staged as 2 KiB column slabs of 32 rows (6.1-6.2 TB/s).  Rows under 96 B
 # travel in packed units; their best vblock lengths, which balance the sort network per key
 # against the fixed costs per unit and member, were 1024 rows below 8 B (4 B: 968 GB/s), 256
-# below 16 B (8 B: 1999), 128 below 24 B (16 B: 4956), 256 below 48 B (32 B: 5649), 1024 below
-# 64 B (48 B: 4741) and 256 below 96 B (64 B: 5788).
+# below 16 B (8 B: 1999), 128 below 24 B (16 B: 4956), 256 below 48 B (32 B: 5649), 512 below
+# 64 B (48 B: 5376) and 256 below 96 B (64 B: 5788).
 B200_VBLOCK_BYTES = 64 * 1024
 B200_MAX_VBLOCK_ROWS = 512
 B200_WIDE_ROW_BYTES = 2048
 B200_WIDE_VBLOCK_ROWS = 32
-B200_SMALL_ROW_VBLOCK_ROWS = ((8, 1024), (16, 256), (24, 128), (48, 256), (64, 1024), (96, 256))  # (row bytes below, vblock rows)
+B200_SMALL_ROW_VBLOCK_ROWS = ((8, 1024), (16, 256), (24, 128), (48, 256), (64, 512), (96, 256))  # (row bytes below, vblock rows)
 
 
 def choose_pblock_size_b200(row_bytes: int, vblock_size: int, deck_size: int) -> int:

@@ -95,6 +95,8 @@ PACKED_CASES = [
     (1, 65_536, 256, 8, 2, [0, 1], 2),  # 4 KiB vblocks, 4 per unit
     (1, 999, 32, 4, 8, [0, 1, 2, 3], 3),  # V = 8, 4 vblocks per unit
     (37, 1000, 64, 8, 2, list(range(8)), 3),  # batched decks: units never straddle two decks
+    (1, 30_011, 48, 64, 2, [0, 1, 3, 5], 3),  # 48-byte rows: 8 vblocks, 48 KiB units beyond the stage cap
+    (1, 20_003, 96, 32, 2, [0, 2], 2),  # 96-byte rows: 4 vblocks, 24 KiB units
 ]
 
 

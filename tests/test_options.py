@@ -193,7 +193,7 @@ def test_thread_block_hint_for_small_vblocks():
         (128, 2, 1 << 30, 256),   # 512 rows
         (96, 2, 1 << 30, 256),
         (64, 2, 1 << 30, 128),    # measured best vblock lengths for small rows (packed units)
-        (48, 2, 1 << 30, 512),
+        (48, 2, 1 << 30, 256),
         (32, 4, 1 << 30, 64),
         (24, 2, 1 << 30, 128),
         (16, 2, 1 << 30, 64),
