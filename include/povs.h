@@ -251,10 +251,22 @@ int povs_set_pack_bytes_v1(int32_t pack_bytes);
  * Advanced: report the launch plan povs_shuffle_v1 would use, as int64 values
  * {grid, block, dynamic smem, sort elements per lane, bulk (0/1), slab bytes, slabs,
  *  stages per CTA, stage bytes, vector bytes, vblocks, SM count, rows per bulk copy,
- *  permutation slots, mover warps, permuter warps, vblocks per unit}; returns how many were written.
+ *  permutation slots, mover warps, permuter warps, vblocks per unit, rows per unit,
+ *  wide-row store kernel (0/1), chunked store kernel (0/1)}; returns how many were written.
  */
 int povs_describe_plan_v1(void* data, int64_t n_rows, int64_t row_bytes, int32_t pblock, int32_t vblock,
                           int32_t device, int64_t* out, int32_t n_out);
+
+/*
+ * Advanced: the same plan computed on the host for given device resources, without a GPU: SM
+ * count, the opt-in maximum of dynamic shared memory per block, shared memory per SM and threads
+ * per SM (B200: 148, 232448, 233472, 2048).  data_address only sets the alignment the plan sees
+ * (nonzero).  Same output as povs_describe_plan_v1, under the process-wide tuning.  For checking
+ * plans in tests and tools; replaces nothing in the reference.
+ */
+int povs_plan_for_resources_v1(uint64_t data_address, int64_t n_rows, int64_t row_bytes, int32_t pblock,
+                               int32_t vblock, int32_t sm_count, int32_t smem_optin, int32_t smem_per_sm,
+                               int32_t max_threads_per_sm, int64_t* out, int32_t n_out);
 
 /*
  * Allocation-free variant of povs_apply_v1 (no counterpart in the reference).

@@ -86,24 +86,27 @@ KernelFn kernel_for(int epl, bool bulk, bool ring, bool wide)
 }
 
 // Packed units (device randomness, in place, ring positions): 2 to 32 sort elements per lane.
-template <bool BULK>
+// CHUNK: plain-load rows stored as 16-byte chunks of each member's run.
+template <bool BULK, bool CHUNK = false>
 KernelFn packed_kernel_for_epl(int epl)
 {
     switch (epl) {
-    case 2: return povs::povs_iteration_kernel<2, false, BULK, false, true, true>;
-    case 4: return povs::povs_iteration_kernel<4, false, BULK, false, true, true>;
-    case 8: return povs::povs_iteration_kernel<8, false, BULK, false, true, true>;
-    case 16: return povs::povs_iteration_kernel<16, false, BULK, false, true, true>;
-    case 32: return povs::povs_iteration_kernel<32, false, BULK, false, true, true>;
+    case 2: return povs::povs_iteration_kernel<2, false, BULK, false, true, true, false, CHUNK>;
+    case 4: return povs::povs_iteration_kernel<4, false, BULK, false, true, true, false, CHUNK>;
+    case 8: return povs::povs_iteration_kernel<8, false, BULK, false, true, true, false, CHUNK>;
+    case 16: return povs::povs_iteration_kernel<16, false, BULK, false, true, true, false, CHUNK>;
+    case 32: return povs::povs_iteration_kernel<32, false, BULK, false, true, true, false, CHUNK>;
     default: return nullptr;
     }
 }
 
 // Push mode exists for device randomness only.  Plain-load kernels always carry ring positions.
 KernelFn select_kernel(int epl, bool injected, bool bulk, bool push = false, bool ring = false, bool packed = false,
-                       bool wide = false)
+                       bool wide = false, bool chunk = false)
 {
-    if (packed) return bulk ? packed_kernel_for_epl<true>(epl) : packed_kernel_for_epl<false>(epl);
+    if (packed)
+        return bulk ? packed_kernel_for_epl<true>(epl)
+                    : (chunk ? packed_kernel_for_epl<false, true>(epl) : packed_kernel_for_epl<false>(epl));
     if (push) return kernel_for<false, true>(epl, bulk, ring, wide);
     if (injected) return kernel_for<true, false>(epl, bulk, ring, wide);
     return kernel_for<false, false>(epl, bulk, ring, wide);
@@ -115,6 +118,12 @@ constexpr int64_t GRAPH_MAX_BYTES = int64_t{32} << 20;
 
 // Bulk-loaded units (stages) of at most this many bytes use the ring-position kernels.
 constexpr int RING_STAGE_BYTES = 16 * 1024;
+
+// Packed plain-load units write 16-byte chunks of each member's destination run (0: one lane per
+// vector piece of a row, as unpacked units do).
+#ifndef POVS_CHUNKED_STORES
+#define POVS_CHUNKED_STORES 1
+#endif
 
 // ------------------------------------------------------------------------------------------
 // Tuning knobs (process-wide; defaults chosen by measurement on B200).
@@ -221,9 +230,9 @@ int set_smem_attr_all(int smem)
                                                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
                         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
                     }
-    for (int bulk = 0; bulk < 2; ++bulk)
+    for (int kind = 0; kind < 3; ++kind) // packed: TMA loads, plain loads, plain loads with chunked stores
         for (int epl = 2; epl <= 32; epl <<= 1) {
-            KernelFn fn = select_kernel(epl, false, bulk != 0, false, true, true);
+            KernelFn fn = select_kernel(epl, false, kind == 0, false, true, true, false, kind == 2);
             cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
             if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
@@ -269,6 +278,8 @@ struct Plan {
     int grid = 0, block = 0, smem = 0, epl = 0;
     bool bulk = false;
     int pack = 1;
+    bool wide = false;  // the WIDE kernel variant (slabs of 512 to 1024 bytes)
+    bool chunk = false; // the CHUNK kernel variant (packed plain-load rows, chunked stores)
 };
 
 int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out, bool push = false,
@@ -417,12 +428,32 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out, boo
         (!bulk && vec >= 4 && p.n_slabs == 1 && static_cast<int64_t>(p.pblock) * p.row_bytes >= 192 && t.force_plain != 2)
             ? 1 : 0;
     p.copy_rows = static_cast<int32_t>(std::max<int64_t>(1, std::min<int64_t>(p.pblock, t.copy_bytes / p.row_bytes)));
+    // Packed plain-load units of 4-byte-multiple rows under 128 bytes store 16-byte chunks of each
+    // member's destination run.  A run is at most one packed unit, which three whole-row stages
+    // must fit in shared memory (under 76 KiB): inside the 2^17 bytes for which the kernel's
+    // division by multiplication with row_magic is exact.
+    // Each lane takes 16-byte chunks of one member run at a time, so members of fewer than 32
+    // chunks, or of 33 to 63, leave lanes idle: measured on B200 (2 GiB decks, GB/s, one lane per
+    // piece -> chunks) 12-byte rows P = 64 (768-byte members) 1769 -> 1724 and V = 4, P = 16 (192 bytes)
+    // 947 -> 720, against 4 B P = 128 (512 bytes) 879 -> 997, 20 B P = 64 1716 -> 2126, 24 B P = 128
+    // 3200 -> 3872, 28 B P = 64 2667 -> 3563, 56 B P = 64 3998 -> 5168.
+    const int64_t member_bytes = static_cast<int64_t>(p.pblock) * p.row_bytes;
+    p.chunked_store = (pack > 1 && !bulk && vec >= 4 && p.row_bytes < 128 && POVS_CHUNKED_STORES &&
+                       (member_bytes == 512 || member_bytes >= 1024))
+                          ? 1
+                          : 0;
+    p.row_magic = p.chunked_store
+                      ? static_cast<uint32_t>(((uint64_t{1} << 32) + static_cast<uint64_t>(p.row_bytes) - 1) /
+                                              static_cast<uint64_t>(p.row_bytes))
+                      : 0u;
     p.n_slots = kp;
     p.n_movers = movers;
     p.n_permuters = permuters;
 
+    out.wide = bulk && pack == 1 && slab >= 512 && slab <= 1024;
+    out.chunk = p.chunked_store != 0;
     out.fn = select_kernel(epl, injected, bulk, push, stage_bytes <= RING_STAGE_BYTES || pack > 1, pack > 1,
-                           bulk && pack == 1 && slab >= 512 && slab <= 1024);
+                           out.wide, out.chunk);
     out.grid = std::max(1, grid);
     out.block = warps * 32;
     out.smem = cta_smem;
@@ -991,6 +1022,20 @@ extern "C" int povs_set_pack_bytes_v1(int32_t pack_bytes)
     return POVS_OK;
 }
 
+namespace {
+// The values povs_describe_plan_v1 and povs_plan_for_resources_v1 report, in the header's order.
+int plan_values(const IterParams& p, const Plan& pl, int sm_count, int64_t* out, int32_t n_out)
+{
+    const int64_t vals[] = {pl.grid,       pl.block,     pl.smem,       pl.epl,        pl.bulk ? 1 : 0,
+                            p.slab_bytes,  p.n_slabs,    p.n_stages,    p.stage_bytes, p.vec_bytes,
+                            p.n_vblocks,   sm_count,     p.copy_rows,   p.n_slots,     p.n_movers,
+                            p.n_permuters, pl.pack,      p.unit_vp,     pl.wide ? 1 : 0, pl.chunk ? 1 : 0};
+    const int n = std::min<int>(n_out, static_cast<int>(sizeof(vals) / sizeof(vals[0])));
+    for (int i = 0; i < n; ++i) out[i] = vals[i];
+    return n;
+}
+} // namespace
+
 extern "C" int povs_describe_plan_v1(void* data, int64_t n_rows, int64_t row_bytes, int32_t pblock, int32_t vblock,
                                      int32_t device, int64_t* out, int32_t n_out)
 {
@@ -1008,13 +1053,31 @@ extern "C" int povs_describe_plan_v1(void* data, int64_t n_rows, int64_t row_byt
     Plan pl;
     r = plan_launch(p, *c, false, pl);
     if (r != POVS_OK) return r;
-    const int64_t vals[] = {pl.grid,      pl.block,       pl.smem,        pl.epl,      pl.bulk ? 1 : 0,
-                            p.slab_bytes, p.n_slabs,      p.n_stages,     p.stage_bytes, p.vec_bytes,
-                            p.n_vblocks,  c->sm_count,    p.copy_rows,    p.n_slots,     p.n_movers,
-                            p.n_permuters, pl.pack};
-    const int n = std::min<int>(n_out, static_cast<int>(sizeof(vals) / sizeof(vals[0])));
-    for (int i = 0; i < n; ++i) out[i] = vals[i];
-    return n;
+    return plan_values(p, pl, c->sm_count, out, n_out);
+}
+
+extern "C" int povs_plan_for_resources_v1(uint64_t data_address, int64_t n_rows, int64_t row_bytes, int32_t pblock,
+                                          int32_t vblock, int32_t sm_count, int32_t smem_optin, int32_t smem_per_sm,
+                                          int32_t max_threads_per_sm, int64_t* out, int32_t n_out)
+{
+    g_err[0] = '\0';
+    void* data = reinterpret_cast<void*>(static_cast<uintptr_t>(data_address));
+    int r = check_common(data, n_rows, row_bytes, pblock, vblock, 1);
+    if (r != POVS_OK) return r;
+    if (out == nullptr || n_out < 0) return fail(POVS_ERR_INVALID_ARGUMENT, "out is NULL");
+    if (sm_count < 1 || smem_optin < 1024 || smem_per_sm < smem_optin || max_threads_per_sm < 512)
+        return fail(POVS_ERR_INVALID_ARGUMENT, "device resources out of range");
+    DeviceCtx c;
+    c.sm_count = sm_count;
+    c.smem_optin = smem_optin;
+    c.smem_per_sm = smem_per_sm;
+    c.max_threads_per_sm = max_threads_per_sm;
+    IterParams p;
+    fill_geometry(p, data, n_rows, row_bytes, pblock, vblock, nullptr);
+    Plan pl;
+    r = plan_launch(p, c, false, pl);
+    if (r != POVS_OK) return r;
+    return plan_values(p, pl, c.sm_count, out, n_out);
 }
 
 // ------------------------------------------------------------------------------------------

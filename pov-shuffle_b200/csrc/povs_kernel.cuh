@@ -135,6 +135,11 @@ struct IterParams {
     int32_t vblock_shift;    // log2(V)
     int32_t idx_bits;        // index bits of a vblock's permutation sort keys: max(5, log2(vp))
     int64_t groups_per_deck; // ceil(n_vblocks / pack)
+    // Packed units of plain-loaded rows (R a multiple of 4, R < 128) launched with the CHUNK kernels:
+    // stores go out as 16-byte chunks of each member's destination run (store_unit_chunked);
+    // row_magic = ceil(2^32 / R).
+    int32_t chunked_store;
+    uint32_t row_magic;
     int64_t offsets[MAX_INLINE_OFFSETS];
 };
 
@@ -951,6 +956,58 @@ __device__ __forceinline__ void store_share(const IterParams& p, const StageMeta
     }
 }
 
+// Packed units of rows that are a multiple of 4 bytes (plain loads, R < 128), this warp's share:
+// members r = warp, warp + n_warps, .. of the unit.  A member's valid rows are at most two
+// contiguous destination runs (rows before n_a at run a, the rest at run b); the lanes write each
+// run's 16-byte aligned chunks, lane l chunks l, l + 32, .., each assembled from four 4-byte words
+// of the stage rows that land there (word at byte o of the run: destination row o / R, byte o % R
+// of stage row perm[row]; the division is a multiply by row_magic, exact for o < 2^17).  The
+// unaligned head and tail of a run (< 16 bytes each) go out as word stores.  Against one lane per
+// 4-byte piece of a row, this stores 16 bytes per lane and computes no per-row global addresses.
+__device__ __forceinline__ void store_unit_chunked(const IterParams& p, const StageMeta& m, const uint8_t* stage,
+                                                   const uint16_t* perm, int lane, int warp, int n_warps)
+{
+    const uint32_t R = static_cast<uint32_t>(p.row_bytes);
+    const uint32_t magic = p.row_magic;
+    const int n_mem = p.pack << p.vblock_shift;
+    for (int r = warp; r < n_mem; r += n_warps) {
+        const int rows = m.mrows[r];
+        if (rows <= 0) continue;
+        const int na = m.n_a[r];
+        for (int piece = 0; piece < 2; ++piece) {
+            const int i_lo = piece == 0 ? 0 : na;
+            const int i_hi = piece == 0 ? min(rows, na) : rows;
+            if (i_lo >= i_hi) continue;
+            const uintptr_t g0 = (piece == 0 ? m.run_a[r] : m.run_b[r]) + static_cast<uintptr_t>(i_lo) * R;
+            const uint16_t* pr = perm + (r << p.pblock_shift) + i_lo;
+            const uint32_t len = static_cast<uint32_t>(i_hi - i_lo) * R;
+            const uint32_t head = min(len, (16u - static_cast<uint32_t>(g0 & 15u)) & 15u);
+            const uint32_t n_chunks = (len - head) >> 4;
+            const uint32_t tail_at = head + (n_chunks << 4);
+            auto word = [&](uint32_t o) -> uint32_t {
+                const uint32_t q = __umulhi(o, magic);
+                return *reinterpret_cast<const uint32_t*>(stage + static_cast<size_t>(pr[q]) * R + (o - q * R));
+            };
+            for (uint32_t c = static_cast<uint32_t>(lane); c < n_chunks; c += 32u) {
+                const uint32_t o = head + (c << 4);
+                uint4 v;
+                v.x = word(o);
+                v.y = word(o + 4u);
+                v.z = word(o + 8u);
+                v.w = word(o + 12u);
+                store_row_chunk(reinterpret_cast<uint4*>(g0 + o), v);
+            }
+            if (static_cast<uint32_t>(lane) * 4u < head) {
+                const uint32_t o = static_cast<uint32_t>(lane) * 4u;
+                *reinterpret_cast<uint32_t*>(g0 + o) = word(o);
+            } else if (lane >= 4 && tail_at + static_cast<uint32_t>(lane - 4) * 4u < len) {
+                const uint32_t o = tail_at + static_cast<uint32_t>(lane - 4) * 4u;
+                *reinterpret_cast<uint32_t*>(g0 + o) = word(o);
+            }
+        }
+    }
+}
+
 // Push mode: the destination slot of every element of the unit's own member (elements
 // first .. first+count-1 of the vblock) under the uniform permutation; same sort as warp_make_perm.
 template <int EPL>
@@ -1179,10 +1236,12 @@ __device__ __forceinline__ void make_packed_unit(const IterParams& p, StageMeta&
 // plain-load kernel); otherwise they recompute them per unit, which measured faster on large
 // bulk-loaded units.
 // PACK: units are groups of `pack` small vblocks (device randomness, in place, whole rows).
-template <int EPL, bool INJECTED, bool BULK, bool PUSH, bool RING, bool PACK = false, bool WIDE = false>
+template <int EPL, bool INJECTED, bool BULK, bool PUSH, bool RING, bool PACK = false, bool WIDE = false,
+          bool CHUNK = false>
 __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_constant__ IterParams p)
 {
     static_assert(!WIDE || (BULK && !PACK), "the wide-row store form is built into TMA-loaded, unpacked kernels");
+    static_assert(!CHUNK || (PACK && !BULK), "chunked stores are built into packed plain-load kernels");
     static_assert(BULK || RING, "plain-load kernels carry ring positions");
     static_assert(!(PUSH && INJECTED), "push mode draws its randomness on the device");
     static_assert(!PACK || (RING && !PUSH && !INJECTED), "packed units: device randomness, in place, ring positions");
@@ -1613,6 +1672,8 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
             const int slen = static_cast<int>(min(static_cast<int64_t>(p.slab_bytes), p.row_bytes - col));
             if constexpr (BULK) {
                 store_share<16, PUSH, PACK, WIDE>(p, m, stage, idx, col, slen, lane, mw, n_movers);
+            } else if constexpr (CHUNK) {
+                store_unit_chunked(p, m, stage, idx, lane, mw, n_movers);
             } else {
                 switch (p.vec_bytes) {
                 case 16: store_share<16, PUSH, PACK>(p, m, stage, idx, col, slen, lane, mw, n_movers); break;

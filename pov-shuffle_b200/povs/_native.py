@@ -51,6 +51,10 @@ SIGNATURES: dict[str, tuple] = {
     "povs_set_pack_bytes_v1": (ctypes.c_int, [_c_i32]),
     "povs_enable_peer_access_v1": (ctypes.c_int, [_c_i32, _c_i32]),
     "povs_describe_plan_v1": (ctypes.c_int, [_c_vp, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _P_I64, _c_i32]),
+    "povs_plan_for_resources_v1": (
+        ctypes.c_int,
+        [_c_u64, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _P_I64, _c_i32],
+    ),
     "povs_shuffle_shards_v1": (
         ctypes.c_int,
         [_c_vp, _c_vp, _P_I64, _c_i32, _c_i64, _P_I64, _c_i32, _c_i32, _c_i32, _c_i32, _c_u64, _c_i32, _c_vp, _c_u32],
@@ -563,7 +567,14 @@ PLAN_FIELDS = (
     "movers",
     "permuters",
     "vblocks_per_unit",
+    "rows_per_unit",
+    "wide_kernel",
+    "chunked_kernel",
 )
+
+# B200 (sm_100a) resources for plan_for_resources: SMs, opt-in dynamic shared memory per block,
+# shared memory per SM, threads per SM.
+B200_RESOURCES = (148, 232448, 233472, 2048)
 
 
 def describe_plan(data: torch.Tensor, row_bytes: int, pblock: int, vblock: int) -> dict[str, int]:
@@ -573,6 +584,17 @@ def describe_plan(data: torch.Tensor, row_bytes: int, pblock: int, vblock: int) 
         ctypes.c_void_p(data.data_ptr()), data.shape[0], row_bytes, pblock, vblock, data.device.index, out, len(PLAN_FIELDS)
     )
     check(n, "povs_describe_plan_v1")
+    return {k: int(out[i]) for i, k in enumerate(PLAN_FIELDS[:n])}
+
+
+def plan_for_resources(n_rows: int, row_bytes: int, pblock: int, vblock: int,
+                       resources: tuple[int, int, int, int] = B200_RESOURCES, address: int = 1 << 20) -> dict[str, int]:
+    """The launch plan for a deck of n_rows x row_bytes at ``address`` on a device with ``resources``,
+    computed on the host (no GPU needed)."""
+    lib = load()
+    out = (ctypes.c_int64 * len(PLAN_FIELDS))()
+    n = lib.povs_plan_for_resources_v1(address, n_rows, row_bytes, pblock, vblock, *resources, out, len(PLAN_FIELDS))
+    check(n, "povs_plan_for_resources_v1")
     return {k: int(out[i]) for i, k in enumerate(PLAN_FIELDS[:n])}
 
 

@@ -97,6 +97,11 @@ PACKED_CASES = [
     (37, 1000, 64, 8, 2, list(range(8)), 3),  # batched decks: units never straddle two decks
     (1, 30_011, 48, 64, 2, [0, 1, 3, 5], 3),  # 48-byte rows: 8 vblocks, 48 KiB units beyond the stage cap
     (1, 20_003, 96, 32, 2, [0, 2], 2),  # 96-byte rows: 4 vblocks, 24 KiB units
+    # Plain-load rows stored as 16-byte chunks of each member's run (runs start at any 4-byte offset).
+    (1, 20_011, 12, 128, 2, [0, 1, 3, 5], 3),
+    (1, 10_007, 20, 64, 2, [0, 1, 2], 2),
+    (1, 40_003, 4, 128, 2, [0, 1, 3], 3),
+    (5, 3001, 24, 64, 2, [0, 1, 2, 3], 2),
 ]
 
 
