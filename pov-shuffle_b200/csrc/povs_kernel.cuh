@@ -1672,7 +1672,10 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
             const int slen = static_cast<int>(min(static_cast<int64_t>(p.slab_bytes), p.row_bytes - col));
             if constexpr (BULK) {
                 store_share<16, PUSH, PACK, WIDE>(p, m, stage, idx, col, slen, lane, mw, n_movers);
-            } else if constexpr (CHUNK) {
+            } else if (CHUNK && p.chunked_store) {
+                // The CHUNK kernels keep the piecewise stores below compiled in as well: with both
+                // forms in one kernel the chunked stores measured 5-22 % faster than in a kernel
+                // with the chunked form alone (same plans, same box).
                 store_unit_chunked(p, m, stage, idx, lane, mw, n_movers);
             } else {
                 switch (p.vec_bytes) {
