@@ -208,14 +208,16 @@ def _choose_base_offset(
 # 96 B and more stream best in vblocks of 32-64 KiB (5.7-6.2 TB/s) and at most 512 rows; rows of
 # 2 KiB and more are staged as 2 KiB column slabs of 32 rows (6.1-6.2 TB/s).  Rows under 96 B
 # travel in packed units; their best vblock lengths, which balance the sort network per key
-# against the fixed costs per unit and member, were 1024 rows below 8 B (4 B: 968 GB/s), 256
-# below 16 B (8 B: 1999), 128 below 24 B (16 B: 4956), 256 below 48 B (32 B: 5649), 512 below
-# 64 B (48 B: 5376) and 256 below 96 B (64 B: 5788).
+# against the fixed costs per unit and member, were 256 rows below 16 B (4 B: 997 GB/s, 8 B:
+# 2014, 12 B: 2288), 128 below 20 B (16 B: 4956), 256 below 40 B (20 B: 2839,
+# 24 B: 3874, 28 B: 4298, 32 B: 5649), 1024 below 48 B (40 B: 4183), 128 below 64 B (48 B: 5353,
+# 56 B: 5169), 256 below 80 B (64 B: 5936) and 512 below 96 B (80 B: 5864).
 B200_VBLOCK_BYTES = 64 * 1024
 B200_MAX_VBLOCK_ROWS = 512
 B200_WIDE_ROW_BYTES = 2048
 B200_WIDE_VBLOCK_ROWS = 32
-B200_SMALL_ROW_VBLOCK_ROWS = ((8, 1024), (16, 256), (24, 128), (48, 256), (64, 512), (96, 256))  # (row bytes below, vblock rows)
+B200_SMALL_ROW_VBLOCK_ROWS = ((16, 256), (20, 128), (40, 256), (48, 1024), (64, 128), (80, 256),
+                              (96, 512))  # (row bytes below, vblock rows)
 
 
 def choose_pblock_size_b200(row_bytes: int, vblock_size: int, deck_size: int) -> int:

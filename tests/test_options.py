@@ -193,14 +193,18 @@ def test_thread_block_hint_for_small_vblocks():
         (128, 2, 1 << 30, 256),   # 512 rows
         (96, 2, 1 << 30, 256),
         (64, 2, 1 << 30, 128),    # measured best vblock lengths for small rows (packed units)
-        (48, 2, 1 << 30, 256),
+        (80, 2, 1 << 30, 256),
+        (56, 2, 1 << 30, 64),
+        (48, 2, 1 << 30, 64),
+        (40, 2, 1 << 30, 512),
+        (20, 2, 1 << 30, 128),
         (32, 4, 1 << 30, 64),
         (24, 2, 1 << 30, 128),
         (16, 2, 1 << 30, 64),
         (12, 2, 1 << 30, 128),
         (8, 2, 1 << 30, 128),
-        (4, 2, 1 << 30, 512),
-        (4, 4, 1 << 30, 256),
+        (4, 2, 1 << 30, 128),
+        (4, 4, 1 << 30, 64),
         (1024, 4, 1 << 30, 16),
         (12288, 2, 1 << 30, 16),  # wide rows: 32-row vblocks of 2 KiB slabs
         (12288, 4, 1 << 30, 8),
