@@ -73,6 +73,11 @@ WORKLOADS = {
         desc="fp32 deck 134,217,728 x 4 (16-byte rows with the reference chooser's V=2, P=64, 2 GiB), uniform "
         "bytes from seed 5, iterations=4",
     ),
+    "f32x6_2GiB": dict(
+        rows=89_478_485, shape=(6,), dtype="float32", iterations=4, V=2, P=64, seed=6, init="bytes",
+        desc="fp32 deck 89,478,485 x 6 (24-byte rows, not a multiple of 16 bytes: plain loads and chunked "
+        "stores, with the reference chooser's V=2, P=64, 2 GiB), uniform bytes from seed 6, iterations=4",
+    ),
     "u8_12KiB": dict(
         rows=1_000_000, shape=(3, 64, 64), dtype="uint8", iterations=3, V=2, P=16, seed=2, init="bytes",
         desc="uint8 deck 1,000,000 x 3x64x64 (12,288 B rows, 12.3 GB), uniform 0..255 from seed 2, iterations=3, V=2, P=16",
