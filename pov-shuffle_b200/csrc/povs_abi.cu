@@ -87,25 +87,25 @@ KernelFn kernel_for(int epl, bool bulk, bool ring, bool wide)
 
 // Packed units (device randomness, in place, ring positions): 2 to 32 sort elements per lane.
 // CHUNK: plain-load rows stored as 16-byte chunks of each member's run.
-template <bool BULK, bool CHUNK = false>
+template <bool BULK, bool CHUNK = false, bool FAST = false>
 KernelFn packed_kernel_for_epl(int epl)
 {
     switch (epl) {
-    case 2: return povs::povs_iteration_kernel<2, false, BULK, false, true, true, false, CHUNK>;
-    case 4: return povs::povs_iteration_kernel<4, false, BULK, false, true, true, false, CHUNK>;
-    case 8: return povs::povs_iteration_kernel<8, false, BULK, false, true, true, false, CHUNK>;
-    case 16: return povs::povs_iteration_kernel<16, false, BULK, false, true, true, false, CHUNK>;
-    case 32: return povs::povs_iteration_kernel<32, false, BULK, false, true, true, false, CHUNK>;
+    case 2: return povs::povs_iteration_kernel<2, false, BULK, false, true, true, false, CHUNK, FAST>;
+    case 4: return povs::povs_iteration_kernel<4, false, BULK, false, true, true, false, CHUNK, FAST>;
+    case 8: return povs::povs_iteration_kernel<8, false, BULK, false, true, true, false, CHUNK, FAST>;
+    case 16: return povs::povs_iteration_kernel<16, false, BULK, false, true, true, false, CHUNK, FAST>;
+    case 32: return povs::povs_iteration_kernel<32, false, BULK, false, true, true, false, CHUNK, FAST>;
     default: return nullptr;
     }
 }
 
 // Push mode exists for device randomness only.  Plain-load kernels always carry ring positions.
 KernelFn select_kernel(int epl, bool injected, bool bulk, bool push = false, bool ring = false, bool packed = false,
-                       bool wide = false, bool chunk = false)
+                       bool wide = false, bool chunk = false, bool fast = false)
 {
     if (packed)
-        return bulk ? packed_kernel_for_epl<true>(epl)
+        return bulk ? (fast ? packed_kernel_for_epl<true, false, true>(epl) : packed_kernel_for_epl<true>(epl))
                     : (chunk ? packed_kernel_for_epl<false, true>(epl) : packed_kernel_for_epl<false>(epl));
     if (push) return kernel_for<false, true>(epl, bulk, ring, wide);
     if (injected) return kernel_for<true, false>(epl, bulk, ring, wide);
@@ -123,6 +123,11 @@ constexpr int RING_STAGE_BYTES = 16 * 1024;
 // vector piece of a row, as unpacked units do).
 #ifndef POVS_CHUNKED_STORES
 #define POVS_CHUNKED_STORES 1
+#endif
+
+// Packed TMA-loaded units of power-of-two rows take their FAST kernel variants (0: never).
+#ifndef POVS_UNIFORM_MEMBER_STORES
+#define POVS_UNIFORM_MEMBER_STORES 1
 #endif
 
 // ------------------------------------------------------------------------------------------
@@ -230,9 +235,9 @@ int set_smem_attr_all(int smem)
                                                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
                         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
                     }
-    for (int kind = 0; kind < 3; ++kind) // packed: TMA loads, plain loads, plain loads with chunked stores
+    for (int kind = 0; kind < 4; ++kind) // packed: TMA loads (kind 3: uniform-member stores), plain loads, chunked
         for (int epl = 2; epl <= 32; epl <<= 1) {
-            KernelFn fn = select_kernel(epl, false, kind == 0, false, true, true, false, kind == 2);
+            KernelFn fn = select_kernel(epl, false, kind == 0 || kind == 3, false, true, true, false, kind == 2, kind == 3);
             cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
             if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
@@ -280,6 +285,7 @@ struct Plan {
     int pack = 1;
     bool wide = false;  // the WIDE kernel variant (slabs of 512 to 1024 bytes)
     bool chunk = false; // the CHUNK kernel variant (packed plain-load rows, chunked stores)
+    bool fast = false;  // the FAST kernel variant (packed TMA-loaded rows, uniform-member stores)
 };
 
 int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out, bool push = false,
@@ -452,8 +458,14 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out, boo
 
     out.wide = bulk && pack == 1 && slab >= 512 && slab <= 1024;
     out.chunk = p.chunked_store != 0;
+    // Packed TMA-loaded rows of a power-of-two count of 16-byte chunks, at most a pblock per warp
+    // store pass: the FAST kernels, whose full units take the member of each pass once per warp.
+    const int64_t chunks_per_row = p.row_bytes / 16;
+    const int64_t rows_per_pass = chunks_per_row > 0 && chunks_per_row < 32 ? 32 / chunks_per_row : 1;
+    out.fast = bulk && pack > 1 && chunks_per_row > 0 && (chunks_per_row & (chunks_per_row - 1)) == 0 &&
+               rows_per_pass <= p.pblock && POVS_UNIFORM_MEMBER_STORES;
     out.fn = select_kernel(epl, injected, bulk, push, stage_bytes <= RING_STAGE_BYTES || pack > 1, pack > 1,
-                           out.wide, out.chunk);
+                           out.wide, out.chunk, out.fast);
     out.grid = std::max(1, grid);
     out.block = warps * 32;
     out.smem = cta_smem;

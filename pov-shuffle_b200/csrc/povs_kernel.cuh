@@ -880,7 +880,7 @@ __device__ __forceinline__ void store_share_div(const IterParams& p, const Stage
 // loads per lane in flight (store_wide_rows; 512- to 1024-byte rows moved 1.1-1.7x faster).  The
 // other kernels keep the row-by-row loop: compiled into them, the wide form cost the 256-byte-row
 // kernels 1-2 % (more registers), and 2 KiB slabs ran 1 % slower with it.
-template <int W, bool PUSH, bool PACK = false, bool WIDE = false>
+template <int W, bool PUSH, bool PACK = false, bool WIDE = false, bool FAST = false>
 __device__ __forceinline__ void store_share(const IterParams& p, const StageMeta& m, const uint8_t* stage,
                                             const uint16_t* idx, int64_t col, int slen, int lane, int warp,
                                             int n_warps)
@@ -919,6 +919,37 @@ __device__ __forceinline__ void store_share(const IterParams& p, const StageMeta
     } else {
         const int g = lg.g, lrow = lg.lrow, lq = lg.lq;
         if (lrow >= g) return;
+        if constexpr (FAST) {
+            if (m.n_valid == p.unit_vp && lg.g_shift >= 0 && g <= p.pblock) {
+                // A packed unit without holes whose passes (g rows each) lie inside one member: the
+                // member of a pass and its run bases are the same for the whole warp, and no slot
+                // needs the hole test.
+                const int n_pass = n >> lg.g_shift;
+                constexpr int U = 4;
+                for (int t = warp; t < n_pass; t += U * n_warps) {
+                    T v[U];
+                    T* dst[U];
+                    bool ok[U];
+#pragma unroll
+                    for (int u = 0; u < U; ++u) {
+                        const int pass = t + u * n_warps;
+                        ok[u] = pass < n_pass;
+                        const int fb = (ok[u] ? pass : 0) << lg.g_shift;
+                        const int r = fb >> p.pblock_shift;
+                        const int i = (fb & pmask) + lrow;
+                        const int src = idx[fb + lrow];
+                        const uintptr_t base = i < m.n_a[r] ? m.run_a[r] : m.run_b[r];
+                        dst[u] = reinterpret_cast<T*>(base + static_cast<uintptr_t>(i) * static_cast<uintptr_t>(p.row_bytes) +
+                                                      static_cast<uintptr_t>(col)) + lq;
+                        v[u] = reinterpret_cast<const T*>(stage + static_cast<size_t>(src) * p.slab_bytes)[lq];
+                    }
+#pragma unroll
+                    for (int u = 0; u < U; ++u)
+                        if (ok[u]) store_row_chunk(dst[u], v[u]);
+                }
+                return;
+            }
+        }
         const int n_pass = lg.passes(n);
         constexpr int U = 4;
         int t = warp;
@@ -1237,9 +1268,10 @@ __device__ __forceinline__ void make_packed_unit(const IterParams& p, StageMeta&
 // bulk-loaded units.
 // PACK: units are groups of `pack` small vblocks (device randomness, in place, whole rows).
 template <int EPL, bool INJECTED, bool BULK, bool PUSH, bool RING, bool PACK = false, bool WIDE = false,
-          bool CHUNK = false>
+          bool CHUNK = false, bool FAST = false>
 __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_constant__ IterParams p)
 {
+    static_assert(!FAST || (PACK && BULK), "the uniform-member store form is built into packed TMA-loaded kernels");
     static_assert(!WIDE || (BULK && !PACK), "the wide-row store form is built into TMA-loaded, unpacked kernels");
     static_assert(!CHUNK || (PACK && !BULK), "chunked stores are built into packed plain-load kernels");
     static_assert(BULK || RING, "plain-load kernels carry ring positions");
@@ -1671,7 +1703,7 @@ __global__ void __launch_bounds__(512, 1) povs_iteration_kernel(const __grid_con
             const int64_t col = static_cast<int64_t>(slab) * p.slab_bytes;
             const int slen = static_cast<int>(min(static_cast<int64_t>(p.slab_bytes), p.row_bytes - col));
             if constexpr (BULK) {
-                store_share<16, PUSH, PACK, WIDE>(p, m, stage, idx, col, slen, lane, mw, n_movers);
+                store_share<16, PUSH, PACK, WIDE, FAST>(p, m, stage, idx, col, slen, lane, mw, n_movers);
             } else if (CHUNK && p.chunked_store) {
                 // The CHUNK kernels keep the piecewise stores below compiled in as well: with both
                 // forms in one kernel the chunked stores measured 5-22 % faster than in a kernel
