@@ -107,14 +107,17 @@ def _host_deck(d: int) -> np.ndarray:
     return np.random.default_rng(100 + d).integers(0, 256, size=(N_ROWS, ROW_BYTES), dtype=np.uint8)
 
 
+@pytest.mark.parametrize("one_rank", [False, True])
 @pytest.mark.parametrize("randomness,double_buffer", [("uniform", True), ("reference_cuda", False)])
-def test_host_shards_streamed_through_two_sharded_decks(oracle_api, tmp_path, randomness, double_buffer):
+def test_host_shards_streamed_through_two_sharded_decks(oracle_api, tmp_path, randomness, double_buffer, one_rank):
     """povs.shuffle_host_shards: step k shuffles its host shard with seed SEED + k; a host shard listed
-    twice is shuffled twice in order; every host deck ends as the oracle's shuffle of it."""
-    world = min(torch.cuda.device_count(), 8)
-    if world < 2:
+    twice is shuffled twice in order; every host deck ends as the oracle's shuffle of it.  With one
+    rank (any machine with a GPU) the whole deck is one shard and the streams and events still
+    order every copy against the shuffles."""
+    world = 1 if one_rank else min(torch.cuda.device_count(), 8)
+    if world < 1 or (not one_rank and world < 2):
         pytest.skip("needs at least two GPUs")
-    port = 33500 + (os.getpid() % 2000) + (11 if double_buffer else 0)
+    port = 33500 + (os.getpid() % 2000) + (11 if double_buffer else 0) + (5 if one_rank else 0)
     mp.start_processes(_host_worker, args=(world, port, str(tmp_path), randomness, double_buffer), nprocs=world,
                        start_method="spawn", join=True)
     steps = {0: [0, 3], 1: [1], 2: [2]}
