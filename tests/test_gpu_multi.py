@@ -1,7 +1,8 @@
 """Sharded mode across GPUs (one process per GPU, NCCL for the seed broadcast only).
 
-Runs when at least two GPUs are visible: each rank holds a shard of one deck, and the
-concatenation of the shuffled shards must equal the oracle's shuffle of the whole deck.
+Each rank holds a shard of one deck, and the concatenation of the shuffled shards must equal the
+oracle's shuffle of the whole deck.  Most cases need at least two GPUs; the one-rank cases (the
+whole deck as one shard) run on any machine with a GPU.
 NVLS is switched off for these child processes.
 """
 
@@ -76,6 +77,19 @@ def test_sharded_deck_matches_oracle(oracle_api, tmp_path, randomness, double_bu
     oracle_api.shuffle(want, ITERATIONS, P, V, OFFSETS, SEED, randomness)
     oracle_api.shuffle(want, 2, P, V, OFFSETS, SEED + 1, randomness)
     assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("randomness,double_buffer", [("uniform", True), ("reference_numpy", False)])
+def test_one_rank_sharded_deck_matches_oracle(oracle_api, tmp_path, randomness, double_buffer):
+    """A ShardedDeck of one rank (the whole deck is its shard): the sharded entry's barrier kernels
+    and, double-buffered, the push order against its own scratch buffer, on any machine with a GPU."""
+    port = 32800 + (os.getpid() % 2000) + (7 if double_buffer else 0)
+    mp.start_processes(_worker, args=(1, port, str(tmp_path), randomness, double_buffer), nprocs=1,
+                       start_method="spawn", join=True)
+    want = _deck()
+    oracle_api.shuffle(want, ITERATIONS, P, V, OFFSETS, SEED, randomness)
+    oracle_api.shuffle(want, 2, P, V, OFFSETS, SEED + 1, randomness)
+    assert np.array_equal(np.load(tmp_path / "rank0.npy"), want)
 
 
 def _host_worker(rank: int, world: int, port: int, out_dir: str, randomness: str, double_buffer: bool):
