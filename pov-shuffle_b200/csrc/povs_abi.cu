@@ -350,8 +350,9 @@ int plan_launch(IterParams& p, const DeviceCtx& c, bool injected, Plan& out, boo
     // member's P rows in push mode.
     const int64_t stage_rows = push ? p.pblock : unit_vp;
     // Packed units run best as several small CTAs per SM, each its own pipeline (measured on B200,
-    // 2 GiB decks of 16- to 256-byte rows): at most 4 stages with TMA loads; with plain loads, whose
-    // issuing warp waits for its loads, 2 mover and 2 permuter warps and at most 3 stages.
+    // 2 GiB decks of 16- to 256-byte rows): at most 4 stages with TMA loads (5 or 6 stages were
+    // 0-14 % slower on every shape tried, 3 or 2 slower still); with plain loads, whose issuing warp
+    // waits for its loads, 2 mover and 2 permuter warps and at most 3 stages.
     const int stage_limit = pack == 1 ? t.n_stages : std::min(t.n_stages, bulk ? 4 : 3);
     const int max_stages = std::max(2, std::min(stage_limit, povs::MAX_STAGES));
     const int movers = std::max(1, std::min(pack > 1 && !bulk ? std::min(t.movers, 2) : t.movers, 15));
